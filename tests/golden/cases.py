@@ -1,0 +1,323 @@
+"""Golden-case catalogue: KTIR sources + seeded inputs for the parity fixtures.
+
+Each case is executed once by the ktir-cpu reference interpreter
+(``make_golden.py``, run in a container that has the reference checked out)
+and its outputs, or the exception it raised, are stored in
+``tests/golden/<name>.npz``.  The tests replay the same source and inputs
+through the oracle (CPU) and through the B200 backend (GPU) and compare.
+
+Edge cases mirror what the reference's own tests pin for this path:
+strided and permuted tile loads, non-box access sets, reads past the end of
+an allocation (zero fill) and writes past it (truncation), odd-length tree
+reductions, the float16 coercion of scalar operands, indirect gathers,
+bijective and colliding scatters (last writer wins), negative indices,
+permuted variable-space order, cross-core read-modify-write ordering and
+LX overflow.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Dict, List
+
+import numpy as np
+
+from ktir_cpu_b200 import workloads as W
+
+HBM = "memory_space = #ktdp.spyre_memory_space<HBM>"
+
+
+def _box(shape):
+    return W._box(tuple(shape))
+
+
+def _view(name, ptr, shape, dtype, strides=None):
+    if strides is None:
+        strides, acc = [], 1
+        for s in reversed(shape):
+            strides.append(acc)
+            acc *= s
+        strides = list(reversed(strides))
+    ty = "x".join(str(s) for s in shape) + "x" + dtype
+    return (f"{name} = ktdp.construct_memory_view {ptr}, sizes: {list(shape)}, strides: {strides} "
+            f"{{coordinate_set = {_box(shape)}, {HBM}}} : memref<{ty}>")
+
+
+def _mref(shape, dtype):
+    return "memref<" + "x".join(str(s) for s in shape) + "x" + dtype + ">"
+
+
+def _at(shape):
+    return "!ktdp.access_tile<" + "x".join(str(s) for s in shape) + "xindex>"
+
+
+def _tt(shape, dtype):
+    return "tensor<" + "x".join(str(s) for s in shape) + "x" + dtype + ">"
+
+
+def _tile(name, view, idx, vshape, dtype, tshape, cset=None, order=None):
+    cset = cset or _box(tshape)
+    order = order or W._ident(len(tshape))
+    return (f"{name} = ktdp.construct_access_tile {view}[{', '.join(idx)}] "
+            f"{{access_tile_set = {cset}, access_tile_order = {order}}} : "
+            f"{_mref(vshape, dtype)} -> {_at(tshape)}")
+
+
+def _fn(name, args, body, grid=(1,)):
+    g = ", ".join(str(v) for v in grid)
+    a = ", ".join(f"%{n}: index" for n in args)
+    lines = "\n    ".join(body)
+    return f"module {{\n  func.func @{name}({a}) attributes {{grid = [{g}]}} {{\n    {lines}\n    return\n  }}\n}}\n"
+
+
+CASES: List[Dict[str, Any]] = []
+
+
+def case(name, src, func, inputs, tol=None, expect_error=None):
+    CASES.append(dict(name=name, src=src, func=func, inputs=inputs, tol=tol,
+                      expect_error=expect_error))
+
+
+rng = np.random.default_rng(1234)
+
+# --- benchmark workloads at reduced sizes -----------------------------------
+for nm, p in [
+    ("vector_add", dict(n=1024, grid=1)),
+    ("vector_add", dict(n=1024, grid=8)),
+    ("softmax", dict(rows=128, cols=1024, grid=4, chunk=32)),
+    ("gemm", dict(m=256, n=256, k=256, grid=(2, 2), sub=(128, 128))),
+    ("gather_add", dict(rows=2048, cols=128, n_idx=4096, grid=8, chunk=256)),
+    ("attention", dict(batch=1, heads=2, seq=256, dim=128, grid=2, bq=64, bk=64)),
+]:
+    tag = nm + "_" + "_".join(f"{k}{v}" if not isinstance(v, tuple) else f"{k}{'x'.join(map(str, v))}"
+                              for k, v in p.items())
+    tol = None if nm in ("vector_add", "gather_add") else 1e-2
+    case(tag, W.source(nm, **p), W.FUNC[nm], W.inputs(nm, seed=7, **p), tol=tol)
+
+# gather_add with heavy duplication inside and across cores
+p = dict(rows=64, cols=128, n_idx=1024, grid=4, chunk=64)
+inp = W.inputs("gather_add", seed=3, **p)
+case("gather_add_dups", W.source("gather_add", **p), "gather_add", inp)
+
+# --- strided column tiles: strided load and read-modify-write store -----------
+case("strided_columns", _fn("cols", ["x", "o"], [
+    "%c = ktdp.get_compute_tile_id : index",
+    "%c0 = arith.constant 0 : index",
+    _view("%xv", "%x", (64, 64), "f16"),
+    _view("%ov", "%o", (64, 4), "f16"),
+    _tile("%xt", "%xv", ["%c0", "%c"], (64, 64), "f16", (64, 1)),
+    _tile("%ot", "%ov", ["%c0", "%c"], (64, 4), "f16", (64, 1)),
+    f"%t = ktdp.load %xt : {_at((64, 1))} -> {_tt((64, 1), 'f16')}",
+    f"%u = arith.mulf %t, %t : {_tt((64, 1), 'f16')}",
+    f"ktdp.store %u, %ot : {_tt((64, 1), 'f16')}, {_at((64, 1))}",
+], grid=(4,)), "cols", {"x": rng.standard_normal((64, 64)).astype(np.float16),
+                        "o": np.full((64, 4), -1, np.float16)})
+
+# --- permuted access order (transposed load) -----------------------------------
+case("transposed_load", _fn("tr", ["x", "o"], [
+    "%c0 = arith.constant 0 : index",
+    _view("%xv", "%x", (8, 16), "f16"),
+    _view("%ov", "%o", (16, 8), "f16"),
+    _tile("%xt", "%xv", ["%c0", "%c0"], (8, 16), "f16", (16, 8),
+          cset=_box((16, 8)), order="affine_map<(d0, d1) -> (d1, d0)>"),
+    _tile("%ot", "%ov", ["%c0", "%c0"], (16, 8), "f16", (16, 8)),
+    f"%t = ktdp.load %xt : {_at((16, 8))} -> {_tt((16, 8), 'f16')}",
+    f"ktdp.store %t, %ot : {_tt((16, 8), 'f16')}, {_at((16, 8))}",
+]), "tr", {"x": rng.standard_normal((8, 16)).astype(np.float16), "o": np.zeros((16, 8), np.float16)})
+
+# --- non-box access set: upper triangle gather and scatter -------------------------
+tri = "affine_set<(d0, d1) : (d0 >= 0, -d0 + 7 >= 0, d1 - d0 >= 0, -d1 + 7 >= 0)>"
+case("triangle_gather_scatter", _fn("tri", ["x", "o", "flat"], [
+    "%c0 = arith.constant 0 : index",
+    _view("%xv", "%x", (8, 8), "f16"),
+    _view("%ov", "%o", (8, 8), "f16"),
+    _view("%fv", "%flat", (36,), "f16"),
+    _tile("%xt", "%xv", ["%c0", "%c0"], (8, 8), "f16", (8, 8), cset=tri),
+    _tile("%ot", "%ov", ["%c0", "%c0"], (8, 8), "f16", (8, 8), cset=tri),
+    _tile("%ft", "%fv", ["%c0"], (36,), "f16", (36,)),
+    f"%t = ktdp.load %xt : {_at((8, 8))} -> {_tt((36,), 'f16')}",
+    f"ktdp.store %t, %ft : {_tt((36,), 'f16')}, {_at((36,))}",
+    f"%u = arith.negf %t : {_tt((36,), 'f16')}",
+    f"ktdp.store %u, %ot : {_tt((36,), 'f16')}, {_at((8, 8))}",
+]), "tri", {"x": rng.standard_normal((8, 8)).astype(np.float16),
+            "o": np.full((8, 8), 7, np.float16), "flat": np.zeros(36, np.float16)})
+
+# --- view larger than the allocation: zero-filled reads, truncated writes --------
+case("read_past_end", _fn("pad", ["x", "o"], [
+    "%c96 = arith.constant 96 : index",
+    "%c0 = arith.constant 0 : index",
+    _view("%xv", "%x", (128,), "f16"),
+    _view("%ov", "%o", (128,), "f16"),
+    _tile("%xt", "%xv", ["%c96"], (128,), "f16", (32,)),
+    _tile("%ot", "%ov", ["%c96"], (128,), "f16", (32,)),
+    f"%t = ktdp.load %xt : {_at((32,))} -> {_tt((32,), 'f16')}",
+    "%one = arith.constant 1.0 : f16",
+    f"%u = arith.addf %t, %one : {_tt((32,), 'f16')}",
+    f"ktdp.store %u, %ot : {_tt((32,), 'f16')}, {_at((32,))}",
+]), "pad", {"x": rng.standard_normal(100).astype(np.float16), "o": np.zeros(100, np.float16)})
+
+# --- tree reductions over odd lengths, both axes and to a scalar -------------------
+case("odd_reductions", _fn("red", ["x", "s", "m", "c"], [
+    "%c0 = arith.constant 0 : index",
+    _view("%xv", "%x", (37, 1000), "f32"),
+    _view("%sv", "%s", (37,), "f32"),
+    _view("%mv", "%m", (37,), "f32"),
+    _view("%cv", "%c", (1000,), "f32"),
+    _tile("%xt", "%xv", ["%c0", "%c0"], (37, 1000), "f32", (37, 1000)),
+    f"%x = ktdp.load %xt : {_at((37, 1000))} -> {_tt((37, 1000), 'f32')}",
+    "%z = arith.constant 0.0 : f32",
+    f"%i0 = tensor.splat %z : {_tt((37,), 'f32')}",
+    f"%i1 = tensor.splat %z : {_tt((1000,), 'f32')}",
+    f"%rs = linalg.reduce {{ arith.addf }} ins(%x : {_tt((37, 1000), 'f32')}) outs(%i0 : {_tt((37,), 'f32')}) dimensions = [1]",
+    f"%rm = linalg.reduce {{ arith.maxnumf }} ins(%x : {_tt((37, 1000), 'f32')}) outs(%i0 : {_tt((37,), 'f32')}) dimensions = [1]",
+    f"%cs = linalg.reduce {{ arith.addf }} ins(%x : {_tt((37, 1000), 'f32')}) outs(%i1 : {_tt((1000,), 'f32')}) dimensions = [0]",
+    _tile("%st", "%sv", ["%c0"], (37,), "f32", (37,)),
+    _tile("%mt", "%mv", ["%c0"], (37,), "f32", (37,)),
+    _tile("%ct", "%cv", ["%c0"], (1000,), "f32", (1000,)),
+    f"ktdp.store %rs, %st : {_tt((37,), 'f32')}, {_at((37,))}",
+    f"ktdp.store %rm, %mt : {_tt((37,), 'f32')}, {_at((37,))}",
+    f"ktdp.store %cs, %ct : {_tt((1000,), 'f32')}, {_at((1000,))}",
+]), "red", {"x": rng.standard_normal((37, 1000)).astype(np.float32),
+            "s": np.zeros(37, np.float32), "m": np.zeros(37, np.float32),
+            "c": np.zeros(1000, np.float32)})
+
+# --- scalar operands are rounded to float16 even against f32 tiles -------------------
+case("scalar_f16_coercion", _fn("coerce", ["x", "o"], [
+    "%c0 = arith.constant 0 : index",
+    _view("%xv", "%x", (256,), "f32"),
+    _view("%ov", "%o", (256,), "f32"),
+    _tile("%xt", "%xv", ["%c0"], (256,), "f32", (256,)),
+    _tile("%ot", "%ov", ["%c0"], (256,), "f32", (256,)),
+    f"%x = ktdp.load %xt : {_at((256,))} -> {_tt((256,), 'f32')}",
+    "%sc = arith.constant 0.08838834764831845 : f32",
+    "%b = arith.constant 3.14159265 : f32",
+    "%sb = arith.mulf %sc, %b : f32",
+    f"%y = arith.mulf %x, %sc : {_tt((256,), 'f32')}",
+    f"%y2 = arith.addf %y, %sb : {_tt((256,), 'f32')}",
+    f"ktdp.store %y2, %ot : {_tt((256,), 'f32')}, {_at((256,))}",
+]), "coerce", {"x": rng.standard_normal(256).astype(np.float32), "o": np.zeros(256, np.float32)})
+
+# --- elementwise math / integer semantics -------------------------------------------
+case("elementwise_math", _fn("ew", ["x", "o1", "o2", "o3"], [
+    "%c0 = arith.constant 0 : index",
+    _view("%xv", "%x", (512,), "f16"),
+    _view("%o1v", "%o1", (512,), "f16"),
+    _view("%o2v", "%o2", (512,), "f16"),
+    _view("%o3v", "%o3", (512,), "f16"),
+    _tile("%xt", "%xv", ["%c0"], (512,), "f16", (512,)),
+    f"%x = ktdp.load %xt : {_at((512,))} -> {_tt((512,), 'f16')}",
+    f"%a = math.absf %x : {_tt((512,), 'f16')}",
+    f"%s = math.sqrt %a : {_tt((512,), 'f16')}",
+    f"%t = math.tanh %x : {_tt((512,), 'f16')}",
+    f"%e = math.exp %t : {_tt((512,), 'f16')}",
+    "%half = arith.constant 0.5 : f16",
+    f"%sh = arith.subf %x, %half : {_tt((512,), 'f16')}",
+    f"%pos = arith.cmpf ogt, %sh, %t : {_tt((512,), 'f16')}",
+    f"%sel = arith.select %pos, %s, %e : {_tt((512,), 'i1')}, {_tt((512,), 'f16')}",
+    f"%mx = arith.maximumf %sel, %t : {_tt((512,), 'f16')}",
+    f"%dv = arith.divf %mx, %e : {_tt((512,), 'f16')}",
+    _tile("%t1", "%o1v", ["%c0"], (512,), "f16", (512,)),
+    _tile("%t2", "%o2v", ["%c0"], (512,), "f16", (512,)),
+    _tile("%t3", "%o3v", ["%c0"], (512,), "f16", (512,)),
+    f"ktdp.store %sel, %t1 : {_tt((512,), 'f16')}, {_at((512,))}",
+    f"ktdp.store %mx, %t2 : {_tt((512,), 'f16')}, {_at((512,))}",
+    f"ktdp.store %dv, %t3 : {_tt((512,), 'f16')}, {_at((512,))}",
+]), "ew", {"x": (2 * rng.standard_normal(512)).astype(np.float16),
+           "o1": np.zeros(512, np.float16), "o2": np.zeros(512, np.float16),
+           "o3": np.zeros(512, np.float16)}, tol=2e-3)
+
+case("integer_ops", _fn("iops", ["a", "b", "q", "r"], [
+    "%c0 = arith.constant 0 : index",
+    _view("%av", "%a", (256,), "i32"),
+    _view("%bv", "%b", (256,), "i32"),
+    _view("%qv", "%q", (256,), "i32"),
+    _view("%rv", "%r", (256,), "i32"),
+    _tile("%at", "%av", ["%c0"], (256,), "i32", (256,)),
+    _tile("%bt", "%bv", ["%c0"], (256,), "i32", (256,)),
+    f"%x = ktdp.load %at : {_at((256,))} -> {_tt((256,), 'i32')}",
+    f"%y = ktdp.load %bt : {_at((256,))} -> {_tt((256,), 'i32')}",
+    f"%d = arith.divsi %x, %y : {_tt((256,), 'i32')}",
+    f"%m = arith.remsi %x, %y : {_tt((256,), 'i32')}",
+    "%k = arith.constant 3 : i32",
+    f"%mk = arith.muli %m, %k : {_tt((256,), 'i32')}",
+    _tile("%qt", "%qv", ["%c0"], (256,), "i32", (256,)),
+    _tile("%rt", "%rv", ["%c0"], (256,), "i32", (256,)),
+    f"ktdp.store %d, %qt : {_tt((256,), 'i32')}, {_at((256,))}",
+    f"ktdp.store %mk, %rt : {_tt((256,), 'i32')}, {_at((256,))}",
+]), "iops", {"a": rng.integers(-1000, 1000, 256).astype(np.int32),
+             "b": np.where(rng.integers(0, 2, 256) == 0, -1, 1).astype(np.int32) *
+             rng.integers(1, 50, 256).astype(np.int32),
+             "q": np.zeros(256, np.int32), "r": np.zeros(256, np.int32)})
+
+# --- indirect access (gather / scatter) ----------------------------------------------
+def _indirect_copy(name, scatter: bool, order=None, n=4):
+    vs = _box((n, n))
+    vo = order or W._ident(2)
+    body = [
+        "%c0 = arith.constant 0 : index",
+        _view("%X", "%x", (n, n), "f16"),
+        _view("%I1", "%i1", (n, n), "i32"),
+        _view("%I2", "%i2", (n, n), "i32"),
+        _view("%Y", "%y", (n, n), "f16"),
+        f"%iat = ktdp.construct_indirect_access_tile intermediate_variables(%m, %k) "
+        f"{'%Y' if scatter else '%X'}[ind(%I1[%m, %k]), ind(%I2[%m, %k])] "
+        f"{{variables_space_set = {vs}, variables_space_order = {vo}}} : "
+        f"{_mref((n, n), 'f16')}, {_mref((n, n), 'i32')}, {_mref((n, n), 'i32')} -> {_at((n, n))}",
+        _tile("%dt", "%X" if scatter else "%Y", ["%c0", "%c0"], (n, n), "f16", (n, n)),
+    ]
+    if scatter:
+        body += [f"%v = ktdp.load %dt : {_at((n, n))} -> {_tt((n, n), 'f16')}",
+                 f"ktdp.store %v, %iat : {_tt((n, n), 'f16')}, {_at((n, n))}"]
+    else:
+        body += [f"%v = ktdp.load %iat : {_at((n, n))} -> {_tt((n, n), 'f16')}",
+                 f"ktdp.store %v, %dt : {_tt((n, n), 'f16')}, {_at((n, n))}"]
+    return _fn(name, ["x", "i1", "i2", "y"], body)
+
+
+X16 = np.arange(16, dtype=np.float16).reshape(4, 4)
+case("indirect_gather_4x4", _indirect_copy("g4", False), "g4",
+     {"x": X16.copy(), "i1": np.tile(np.array([3, 2, 1, 0], np.int32), (4, 1)),
+      "i2": np.tile(np.arange(4, dtype=np.int32), (4, 1)), "y": np.zeros((4, 4), np.float16)})
+case("indirect_scatter_bijection", _indirect_copy("s4", True), "s4",
+     {"x": X16.copy(), "i1": np.repeat(np.array([3, 2, 1, 0], np.int32), 4).reshape(4, 4),
+      "i2": np.tile(np.array([3, 2, 1, 0], np.int32), (4, 1)), "y": np.zeros((4, 4), np.float16)})
+case("indirect_scatter_collision", _indirect_copy("s4", True), "s4",
+     {"x": X16.copy(), "i1": np.zeros((4, 4), np.int32), "i2": np.zeros((4, 4), np.int32),
+      "y": np.full((4, 4), -1, np.float16)})
+case("indirect_scatter_collision_vso", _indirect_copy("s4", True,
+                                                      order="affine_map<(d0, d1) -> (d1, d0)>"), "s4",
+     {"x": X16.copy(), "i1": np.zeros((4, 4), np.int32), "i2": np.zeros((4, 4), np.int32),
+      "y": np.full((4, 4), -1, np.float16)})
+case("indirect_gather_vso", _indirect_copy("g4", False, order="affine_map<(d0, d1) -> (d1, d0)>"),
+     "g4", {"x": X16.copy(), "i1": rng.integers(0, 4, (4, 4)).astype(np.int32),
+            "i2": rng.integers(0, 4, (4, 4)).astype(np.int32), "y": np.zeros((4, 4), np.float16)})
+neg = np.tile(np.array([3, 2, 1, 0], np.int32), (4, 1))
+neg[2, 1] = -1
+case("indirect_negative_index", _indirect_copy("g4", False), "g4",
+     {"x": X16.copy(), "i1": neg, "i2": np.zeros((4, 4), np.int32),
+      "y": np.zeros((4, 4), np.float16)}, expect_error="IndexError")
+
+# --- LX overflow -----------------------------------------------------------------
+case("lx_overflow", _fn("big", ["x"], [
+    "%c0 = arith.constant 0 : index",
+    _view("%xv", "%x", (1024, 1024), "f32"),
+    _tile("%xt", "%xv", ["%c0", "%c0"], (1024, 1024), "f32", (1024, 1024)),
+    f"%t = ktdp.load %xt : {_at((1024, 1024))} -> {_tt((1024, 1024), 'f32')}",
+]), "big", {"x": np.zeros((1024, 1024), np.float32)}, expect_error="MemoryError")
+
+# --- f16 matmul (np.matmul f16 semantics) + outs accumulation ------------------------------
+case("matmul_f16_tiles", _fn("mm", ["a", "b", "c"], [
+    "%c0 = arith.constant 0 : index",
+    _view("%av", "%a", (64, 128), "f16"),
+    _view("%bv", "%b", (128, 64), "f16"),
+    _view("%cv", "%c", (64, 64), "f16"),
+    _tile("%at", "%av", ["%c0", "%c0"], (64, 128), "f16", (64, 128)),
+    _tile("%bt", "%bv", ["%c0", "%c0"], (128, 64), "f16", (128, 64)),
+    _tile("%ct", "%cv", ["%c0", "%c0"], (64, 64), "f16", (64, 64)),
+    f"%x = ktdp.load %at : {_at((64, 128))} -> {_tt((64, 128), 'f16')}",
+    f"%y = ktdp.load %bt : {_at((128, 64))} -> {_tt((128, 64), 'f16')}",
+    f"%z = tensor.empty() : {_tt((64, 64), 'f16')}",
+    f"%p = linalg.matmul ins(%x, %y : {_tt((64, 128), 'f16')}, {_tt((128, 64), 'f16')}) outs(%z : {_tt((64, 64), 'f16')}) -> {_tt((64, 64), 'f16')}",
+    f"ktdp.store %p, %ct : {_tt((64, 64), 'f16')}, {_at((64, 64))}",
+]), "mm", {"a": rng.uniform(-1, 1, (64, 128)).astype(np.float16),
+           "b": rng.uniform(-1, 1, (128, 64)).astype(np.float16),
+           "c": np.zeros((64, 64), np.float16)}, tol=1e-2)

@@ -1,0 +1,46 @@
+"""Loading and comparing the committed golden fixtures."""
+
+import glob
+import os
+
+import numpy as np
+
+GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def golden_names():
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+
+
+def load_golden(name):
+    z = np.load(os.path.join(GOLDEN_DIR, name + ".npz"), allow_pickle=False)
+    inputs = {k[4:]: z[k] for k in z.files if k.startswith("in__")}
+    outputs = {k[5:]: z[k] for k in z.files if k.startswith("out__")}
+    for k, v in inputs.items():
+        outputs.setdefault(k, v)
+    tol = float(z["tol"])
+    return {
+        "src": str(z["src"]), "func": str(z["func"]), "inputs": inputs, "outputs": outputs,
+        "tol": None if tol < 0 else tol, "error": str(z["error"]),
+        "error_msg": str(z["error_msg"]) if "error_msg" in z.files else "",
+    }
+
+
+def max_rel_err(got, want, floor=1e-3):
+    got = got.astype(np.float64)
+    want = want.astype(np.float64)
+    denom = np.maximum(np.abs(want), floor)
+    return float(np.max(np.abs(got - want) / denom)) if want.size else 0.0
+
+
+def assert_matches(name, got, want, tol):
+    assert got.shape == want.shape and got.dtype == want.dtype, (name, got.shape, want.shape)
+    if tol is None:
+        if not np.array_equal(got, want, equal_nan=True):
+            bad = np.argwhere(~((got == want) | (np.isnan(got.astype(np.float64)) &
+                                                  np.isnan(want.astype(np.float64)))))
+            raise AssertionError(f"{name}: not bit-exact at {len(bad)} positions, first {bad[:3].tolist()}")
+    else:
+        # max relative error with near-zero outputs judged against an absolute floor
+        err = max_rel_err(got, want, floor=max(tol, 1e-3))
+        assert err <= tol, f"{name}: max rel err {err:.3e} > {tol}"
