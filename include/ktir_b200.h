@@ -1,0 +1,235 @@
+/*
+ * ktir_b200.h — C ABI of the B200 execution backend for KTIR kernels.
+ *
+ * The reference interpreter (ktir-cpu) executes a KTIR function by running
+ * every core's op list through NumPy handlers.  This library is what those
+ * handlers are replaced by on a B200: the host lowers a traced KTIR function
+ * into a short list of device programs, and each entry point below launches
+ * one program over all the work units (cores x loop iterations) it covers.
+ *
+ * Conventions
+ *  - Every entry point returns 0 on success or a negative code; the message
+ *    of the last failure on the calling thread is ktir_last_error().
+ *  - No C++ exception crosses this boundary.
+ *  - Descriptors are plain structs passed by host pointer; they are copied
+ *    into kernel parameters, so the caller may free them after the call.
+ *  - Device pointers are passed as void*; `stream` is a cudaStream_t (NULL =
+ *    the legacy default stream).  Calls are asynchronous on that stream.
+ *  - A device-side status word (int32, device memory owned by the caller)
+ *    collects data-dependent failures such as negative indirect indices;
+ *    the caller reads it after synchronising and raises accordingly.
+ *
+ * Element bounds: every access names a slot of KtirBuffers; elements at or
+ * past numel[slot] read as zero and are not written.  This is the
+ * reference's memory rule — reads that run past the allocation holding
+ * their start address are zero-filled and writes are truncated
+ * (ktir_cpu/memory.py:131-198).
+ */
+#ifndef KTIR_B200_H
+#define KTIR_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KTIR_MAX_BUFFERS 16   /* call tensors + arena + scratch slots            */
+#define KTIR_MAX_RANK 6
+#define KTIR_MAX_VIEWS 12
+#define KTIR_MAX_INSTR 64
+#define KTIR_NREG 12
+
+/* error codes */
+#define KTIR_OK 0
+#define KTIR_ERR_ARG (-1)
+#define KTIR_ERR_CUDA (-2)
+#define KTIR_ERR_UNSUPPORTED (-3)
+
+/* status word bits set by kernels */
+#define KTIR_STATUS_NEGATIVE_INDEX 1
+#define KTIR_STATUS_TIMEOUT 2
+
+enum KtirDtype { KTIR_F16 = 0, KTIR_F32 = 1, KTIR_I32 = 2, KTIR_I64 = 3, KTIR_BOOL = 4 };
+
+typedef struct {
+  void* base[KTIR_MAX_BUFFERS];
+  int64_t numel[KTIR_MAX_BUFFERS];
+} KtirBuffers;
+
+/* A strided view over one buffer slot, aligned with an iteration space. */
+typedef struct {
+  int32_t slot;
+  int32_t dtype;       /* KtirDtype of the stored elements */
+  int32_t unit_col;    /* column of the per-unit offset table added to off, or -1 */
+  int32_t pad;
+  int64_t off;
+  int64_t stride[KTIR_MAX_RANK];
+} KtirView;
+
+/* Elementwise bytecode (see csrc/ew_ops.cuh for the opcode list). */
+typedef struct {
+  uint8_t op, dst, a, b, c, dt, aux, flags;
+  int64_t imm;         /* IMM: int64 value, or the bits of a double */
+} KtirInstr;
+
+typedef struct {
+  int32_t rank;
+  int32_t n_views;
+  int32_t n_instr;
+  int32_t n_units;
+  int32_t unit_cols;   /* columns of the per-unit offset table */
+  int32_t contiguous;  /* all views dense row-major over the iteration space */
+  int64_t numel;       /* elements of the iteration space per unit */
+  int64_t shape[KTIR_MAX_RANK];
+  KtirView view[KTIR_MAX_VIEWS];
+  KtirInstr code[KTIR_MAX_INSTR];
+} KtirEwProgram;
+
+/* Row softmax: out = exp(x - max) / sum(exp(x - max)) over the last dim,
+ * max/sum folded in the reference's pairwise-halving order. */
+typedef struct {
+  int32_t rows;        /* rows per unit */
+  int32_t cols;
+  int32_t n_units;
+  int32_t unit_cols;
+  int32_t compute_f16; /* 1: every intermediate rounded to f16 (f16 program) */
+  int32_t pad;
+  KtirView in;         /* stride[0] = row stride, stride[1] = 1 */
+  KtirView out;
+} KtirSoftmaxDesc;
+
+/* Indirect row gather -> f -> scatter to the same rows, repeated over units
+ * whose index ranges may overlap (each row gets f applied once per unit that
+ * names it, in any order, as the reference's sequential units do). */
+typedef struct {
+  int32_t table_slot;
+  int32_t idx_slot;
+  int32_t idx_dtype;
+  int32_t n_units;
+  int32_t unit_len;    /* indices per unit */
+  int32_t row_len;     /* elements per gathered row */
+  int64_t table_off;   /* element offset of row 0 */
+  int64_t row_stride;
+  int64_t idx_off;     /* element offset of the first index of unit 0 */
+  int64_t idx_unit_stride; /* index offset step between consecutive units */
+  KtirEwProgram f;     /* view 0 = the gathered element (load), view 1 = result (store) */
+} KtirGatherRmwDesc;
+
+/* Tree reduction along one axis of a dense [outer, n, inner] arena tile. */
+typedef struct {
+  int32_t combiner;    /* opcode of the binary combiner */
+  int32_t dt;          /* compute/round dtype */
+  int32_t n_units;
+  int32_t pad;
+  int64_t outer, n, inner;
+  int64_t in_off, out_off, tmp_off;  /* arena element offsets (unit 0) */
+  int64_t unit_stride;               /* arena elements between units */
+  int32_t in_slot, out_slot;
+} KtirReduceDesc;
+
+/* Plain CUDA-core matmul for generic tiles: out[b,m,n] = sum_k a[b,m,k]*b[b,k,n],
+ * accumulated in f32 in increasing k, rounded once to the output dtype. */
+typedef struct {
+  int64_t batch, m, n, k;
+  KtirView a, b, out;  /* strides: [batch, row, col] */
+  int32_t n_units, unit_cols;
+} KtirMatmulDesc;
+
+/* Gather / scatter through a per-unit element offset list. */
+typedef struct {
+  KtirView buf;        /* base view (slot, off, unit_col) */
+  KtirView dense;      /* arena side, contiguous */
+  int64_t count;       /* offsets per unit */
+  int32_t n_units;
+  int32_t scatter;     /* 0 gather buf->dense, 1 scatter dense->buf */
+} KtirOffsetsDesc;
+
+/* Indirect access: per point, element offset = direct[i] + sum_k idx_k * stride_k
+ * where idx_k is read from buffer idx_slot[k] at idx_off_k[i]. */
+typedef struct {
+  KtirView buf;        /* parent tensor */
+  KtirView dense;      /* arena side */
+  int64_t count;       /* points per unit */
+  int32_t n_units;
+  int32_t n_ind;
+  int32_t scatter;
+  int32_t pad;
+  int32_t idx_slot[4];
+  int32_t idx_dtype[4];
+  int64_t stride[4];
+} KtirIndirectDesc;
+
+/* Tiled f16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM, TMA fed).
+ * C[m0:m0+TM, n0:n0+TN] = epilogue(A[m0:, k0:k0+K] @ B[k0:k0+K, n0:]) for every
+ * listed output tile; f32 accumulation, f16 store. */
+typedef struct {
+  void* a; void* b; void* c;
+  int64_t lda, ldb, ldc;       /* row strides in elements (row-major A[M,K], B[K,N], C[M,N]) */
+  int64_t m, n, k;             /* full problem */
+  int32_t add_zero;            /* epilogue adds +0.0 (normalises -0) as outs-init does */
+  int32_t pad;
+} KtirGemmDesc;
+
+/* Causal flash attention over [bh, seq, d] f16 tensors laid out as
+ * [bh*seq, d] rows; scale applied to S in f32; online softmax in f32. */
+typedef struct {
+  void* q; void* k; void* v; void* o;
+  int64_t bh, seq, d;
+  float scale;
+  int32_t causal;
+  int64_t row_stride;          /* elements between consecutive rows (= d for dense) */
+} KtirFmhaDesc;
+
+/* ----------------------------------------------------------------------- */
+
+/* Library version (major*100 + minor). */
+int ktir_version(void);
+/* Message of the last failure on this thread ("" if none). */
+const char* ktir_last_error(void);
+/* Number of visible CUDA devices. */
+int ktir_device_count(int* count);
+
+/* Elementwise program over n_units units (replaces the arith/math handlers,
+ * ktir_cpu/dialects/arith_ops.py:40-448, math_ops.py:24-110, and the
+ * rectangular ktdp.load/store copies, ops/memory_ops.py:438-587). */
+int ktir_ew(const KtirEwProgram* prog, const KtirBuffers* bufs, const int64_t* unit_table,
+            void* stream);
+
+/* Fused row softmax (replaces the linalg.reduce max/sum tree folds,
+ * ktir_cpu/dialects/linalg_ops.py:86-219, and the elementwise chain between them). */
+int ktir_softmax_rows(const KtirSoftmaxDesc* desc, const KtirBuffers* bufs,
+                      const int64_t* unit_table, void* stream);
+
+/* Indirect gather -> elementwise -> indirect scatter with the reference's
+ * sequential-unit read-modify-write semantics (replaces MemoryOps.indirect_load /
+ * indirect_store, ktir_cpu/ops/memory_ops.py:589-630, 914-966).  `counts` is
+ * an int32 scratch array of one entry per table row, zero on entry and left
+ * zero on exit; `status` receives KTIR_STATUS_NEGATIVE_INDEX. */
+int ktir_gather_rmw(const KtirGatherRmwDesc* desc, const KtirBuffers* bufs, int32_t* counts,
+                    int64_t n_rows, int32_t* status, void* stream);
+
+/* Generic-path kernels (linalg.reduce tree fold, linalg.matmul on CUDA cores,
+ * coordinate-set gathers/scatters, indirect access tiles). */
+int ktir_reduce(const KtirReduceDesc* desc, const KtirBuffers* bufs, void* stream);
+int ktir_matmul(const KtirMatmulDesc* desc, const KtirBuffers* bufs, const int64_t* unit_table,
+                void* stream);
+int ktir_offsets(const KtirOffsetsDesc* desc, const KtirBuffers* bufs, const int64_t* unit_table,
+                 const int64_t* offsets, void* stream);
+int ktir_indirect(const KtirIndirectDesc* desc, const KtirBuffers* bufs,
+                  const int64_t* unit_table, const int64_t* direct, const int64_t* idx_offs,
+                  int32_t* status, void* stream);
+
+/* tcgen05 GEMM (replaces the linalg.matmul K loop, ktir_cpu/dialects/linalg_ops.py:273-297
+ * with ops/arith_ops.py:403-419, for whole-matrix tilings). */
+int ktir_gemm_f16(const KtirGemmDesc* desc, void* stream);
+
+/* Causal attention (replaces the online-softmax scf.for of matmul / reduce /
+ * exp ops the attention rewrite recognises). */
+int ktir_fmha_f16(const KtirFmhaDesc* desc, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KTIR_B200_H */

@@ -1,0 +1,641 @@
+// B200 execution backend for KTIR: C ABI + CUDA-core kernels.
+//
+//  k_ew            fused elementwise bytecode over an N-d iteration space,
+//                  batched over units (cores x loop iterations)
+//  k_softmax_rows  fused row softmax, one warp per row, f16 rows moved with
+//                  128-bit loads; max and sum fold in the reference's
+//                  pairwise-halving order (ktir_cpu/dialects/linalg_ops.py:86-133)
+//  k_rmw_count / k_rmw_apply
+//                  indirect row gather -> f -> scatter over many units with the
+//                  reference's sequential-unit semantics: a row named by m
+//                  units ends as f applied m times (f16 rounding every time)
+//  k_reduce, k_matmul, k_offsets, k_indirect_*
+//                  generic-path kernels for programs no fused kernel covers
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "ew_ops.cuh"
+
+using namespace ktir;
+
+// ---------------------------------------------------------------------------
+// error plumbing
+// ---------------------------------------------------------------------------
+static thread_local char g_err[512] = "";
+
+static int set_err(int code, const char* msg) {
+  snprintf(g_err, sizeof(g_err), "%s", msg);
+  return code;
+}
+
+static int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    snprintf(g_err, sizeof(g_err), "%s: %s", what, cudaGetErrorString(e));
+    return KTIR_ERR_CUDA;
+  }
+  return KTIR_OK;
+}
+
+extern "C" int ktir_version(void) { return 100; }
+extern "C" const char* ktir_last_error(void) { return g_err; }
+extern "C" int ktir_device_count(int* count) {
+  cudaError_t e = cudaGetDeviceCount(count);
+  if (e != cudaSuccess) return set_err(KTIR_ERR_CUDA, cudaGetErrorString(e));
+  return KTIR_OK;
+}
+
+static inline int grid_x(int64_t work, int threads, int cap) {
+  int64_t g = (work + threads - 1) / threads;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return (int)g;
+}
+
+// ---------------------------------------------------------------------------
+// fused elementwise
+// ---------------------------------------------------------------------------
+template <bool CONTIG>
+__global__ void __launch_bounds__(256) k_ew(const __grid_constant__ KtirEwProgram p,
+                                            const __grid_constant__ KtirBuffers b,
+                                            const int64_t* __restrict__ ut) {
+  __shared__ int64_t base[KTIR_MAX_VIEWS];
+  for (int unit = blockIdx.y; unit < p.n_units; unit += gridDim.y) {
+    __syncthreads();
+    if (threadIdx.x < p.n_views) {
+      const KtirView& v = p.view[threadIdx.x];
+      base[threadIdx.x] =
+          v.off + (v.unit_col >= 0 ? ut[(int64_t)unit * p.unit_cols + v.unit_col] : 0);
+    }
+    __syncthreads();
+    Reg r[KTIR_NREG];
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < p.numel;
+         e += (int64_t)gridDim.x * blockDim.x) {
+      int64_t idx[KTIR_MAX_RANK];
+      if (!CONTIG) {
+        int64_t rem = e;
+        for (int d = p.rank - 1; d >= 0; --d) {
+          idx[d] = rem % p.shape[d];
+          rem /= p.shape[d];
+        }
+      }
+      for (int pc = 0; pc < p.n_instr; ++pc) {
+        const KtirInstr in = p.code[pc];
+        if (in.op == OP_LD || in.op == OP_ST) {
+          const KtirView& v = p.view[in.aux];
+          int64_t off = base[in.aux];
+          if (CONTIG) {
+            off += e;
+          } else {
+            for (int d = 0; d < p.rank; ++d) off += idx[d] * v.stride[d];
+          }
+          if (in.op == OP_LD)
+            r[in.dst] = load_elem(b, v.slot, v.dtype, off);
+          else
+            store_elem(b, v.slot, v.dtype, off, r[in.a], in.dt);
+        } else if (in.op == OP_IOTA) {
+          r[in.dst].i = CONTIG ? 0 : idx[in.aux];
+        } else {
+          exec_arith(in, r);
+        }
+      }
+    }
+  }
+}
+
+extern "C" int ktir_ew(const KtirEwProgram* prog, const KtirBuffers* bufs,
+                       const int64_t* unit_table, void* stream) {
+  if (!prog || !bufs) return set_err(KTIR_ERR_ARG, "ktir_ew: null descriptor");
+  if (prog->n_instr > KTIR_MAX_INSTR || prog->n_views > KTIR_MAX_VIEWS ||
+      prog->rank > KTIR_MAX_RANK || prog->n_units < 1)
+    return set_err(KTIR_ERR_ARG, "ktir_ew: descriptor out of range");
+  if (prog->numel == 0) return KTIR_OK;
+  dim3 grid(grid_x(prog->numel, 256, 148 * 16), prog->n_units < 65535 ? prog->n_units : 65535);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (prog->contiguous)
+    k_ew<true><<<grid, 256, 0, s>>>(*prog, *bufs, unit_table);
+  else
+    k_ew<false><<<grid, 256, 0, s>>>(*prog, *bufs, unit_table);
+  return check_launch("ktir_ew");
+}
+
+// ---------------------------------------------------------------------------
+// fused row softmax
+// ---------------------------------------------------------------------------
+// Layout: lane l holds elements 256*j + 8*l + k (k < 8, j < VPL) of its row,
+// i.e. one 16-byte vector of f16 per j.  With this layout the halving tree
+// of the reference (combine [0,h) with [h,2h), h = n/2, n/4, ..., 1) maps to:
+//   h >= 256      : vector j with vector j + h/256 in the same lane
+//   8 <= h <= 128 : lane l with lane l + h/8 (same j = 0, same k)
+//   h <= 4        : element k with k + h inside lane 0
+// so the fold below is the reference's fold, pair for pair.
+template <int VPL>
+__device__ __forceinline__ float tree_fold(float (&v)[VPL][8], int n, bool is_max, bool f16) {
+  const unsigned full = 0xffffffffu;
+  // in-lane vector rounds
+  for (int h = n / 2; h >= 256; h >>= 1) {
+    const int hv = h / 256;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      if (j < hv) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float a = v[j][k], c = v[j + hv < VPL ? j + hv : j][k];
+          float r = is_max ? fmaxf(a, c) : a + c;
+          v[j][k] = f16 ? __half2float(__float2half_rn(r)) : r;
+        }
+      }
+    }
+  }
+  // cross-lane rounds, h = 128 .. 8 (only those below n)
+  const int top = (n / 2 < 128) ? n / 2 : 128;
+  for (int h = top; h >= 8; h >>= 1) {
+    const int dl = h / 8;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float c = __shfl_down_sync(full, v[0][k], dl);
+      float r = is_max ? fmaxf(v[0][k], c) : v[0][k] + c;
+      r = f16 ? __half2float(__float2half_rn(r)) : r;
+      if ((threadIdx.x & 31) < dl) v[0][k] = r;
+    }
+  }
+  // in-lane element rounds
+  float w[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) w[k] = v[0][k];
+#pragma unroll
+  for (int h = 4; h >= 1; h >>= 1) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (k < h) {
+        float r = is_max ? fmaxf(w[k], w[k + h]) : w[k] + w[k + h];
+        w[k] = f16 ? __half2float(__float2half_rn(r)) : r;
+      }
+    }
+  }
+  return __shfl_sync(full, w[0], 0);
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ KtirSoftmaxDesc d,
+                                                      const __grid_constant__ KtirBuffers b,
+                                                      const int64_t* __restrict__ ut) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t total_rows = (int64_t)d.n_units * d.rows;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const bool f16c = d.compute_f16 != 0;
+  const __half* in = (const __half*)b.base[d.in.slot];
+  __half* out = (__half*)b.base[d.out.slot];
+  for (int64_t row = warp; row < total_rows; row += nwarps) {
+    const int64_t unit = row / d.rows;
+    const int64_t r = row - unit * d.rows;
+    const int64_t ib = d.in.off + (d.in.unit_col >= 0 ? ut[unit * d.unit_cols + d.in.unit_col] : 0)
+                       + r * d.in.stride[0];
+    const int64_t ob = d.out.off +
+                       (d.out.unit_col >= 0 ? ut[unit * d.unit_cols + d.out.unit_col] : 0) +
+                       r * d.out.stride[0];
+    float v[VPL][8];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int64_t e = ib + 256 * j + 8 * lane;
+      if (e >= 0 && e + 8 <= b.numel[d.in.slot]) {
+        uint4 raw = __ldg(reinterpret_cast<const uint4*>(in + e));
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float2 f = __half22float2(h2[k]);
+          v[j][2 * k] = f.x;
+          v[j][2 * k + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          v[j][k] = (e + k >= 0 && e + k < b.numel[d.in.slot]) ? __half2float(in[e + k]) : 0.f;
+      }
+    }
+    float t[VPL][8];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t[j][k] = v[j][k];
+    const float mx = tree_fold<VPL>(t, d.cols, true, f16c);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float x = v[j][k] - mx;
+        if (f16c) x = __half2float(__float2half_rn(x));
+        x = expf(x);
+        if (f16c) x = __half2float(__float2half_rn(x));
+        v[j][k] = x;
+        t[j][k] = x;
+      }
+    const float sum = tree_fold<VPL>(t, d.cols, false, f16c);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int64_t e = ob + 256 * j + 8 * lane;
+      __half2 o2[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        o2[k] = __floats2half2_rn(v[j][2 * k] / sum, v[j][2 * k + 1] / sum);
+      if (e >= 0 && e + 8 <= b.numel[d.out.slot]) {
+        *reinterpret_cast<uint4*>(out + e) = *reinterpret_cast<uint4*>(o2);
+      } else {
+        const __half* oh = reinterpret_cast<const __half*>(o2);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (e + k >= 0 && e + k < b.numel[d.out.slot]) out[e + k] = oh[k];
+      }
+    }
+  }
+}
+
+extern "C" int ktir_softmax_rows(const KtirSoftmaxDesc* d, const KtirBuffers* bufs,
+                                 const int64_t* unit_table, void* stream) {
+  if (!d || !bufs) return set_err(KTIR_ERR_ARG, "ktir_softmax_rows: null descriptor");
+  const int n = d->cols;
+  if (n < 256 || (n & (n - 1)) || n > 8192 || d->in.stride[1] != 1 || d->out.stride[1] != 1 ||
+      d->in.dtype != KTIR_F16 || d->out.dtype != KTIR_F16)
+    return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: needs f16 rows of 2^k >= 256 elements");
+  if (((d->in.off | d->out.off | d->in.stride[0] | d->out.stride[0]) & 7) != 0)
+    return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: rows must be 16-byte aligned");
+  const int64_t rows = (int64_t)d->n_units * d->rows;
+  const int threads = 256;
+  const int blocks = grid_x(rows * 32, threads, 1 << 30);
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (n / 256) {
+    case 1: k_softmax_rows<1><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
+    case 2: k_softmax_rows<2><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
+    case 4: k_softmax_rows<4><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
+    case 8: k_softmax_rows<8><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
+    case 16: k_softmax_rows<16><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
+    case 32: k_softmax_rows<32><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
+    default: return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: row length");
+  }
+  return check_launch("ktir_softmax_rows");
+}
+
+// ---------------------------------------------------------------------------
+// indirect gather -> f -> scatter, sequential-unit semantics
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int64_t read_index(const KtirBuffers& b, int slot, int dt, int64_t pos) {
+  if (pos < 0 || pos >= b.numel[slot]) return 0;  // zero fill past the index tensor
+  if (dt == KTIR_I64) return ((const long long*)b.base[slot])[pos];
+  return ((const int*)b.base[slot])[pos];
+}
+
+// Phase 1: each CTA owns one unit, de-duplicates that unit's rows in a shared
+// hash set and counts, per row, how many units name it.
+__global__ void __launch_bounds__(512) k_rmw_count(const __grid_constant__ KtirGatherRmwDesc d,
+                                                   const __grid_constant__ KtirBuffers b,
+                                                   int* __restrict__ counts, int64_t n_rows,
+                                                   int* __restrict__ status) {
+  extern __shared__ long long set[];
+  int cap = 1;
+  while (cap < 2 * d.unit_len) cap <<= 1;
+  for (int unit = blockIdx.x; unit < d.n_units; unit += gridDim.x) {
+    for (int i = threadIdx.x; i < cap; i += blockDim.x) set[i] = -1;
+    __syncthreads();
+    const int64_t base = d.idx_off + (int64_t)unit * d.idx_unit_stride;
+    for (int i = threadIdx.x; i < d.unit_len; i += blockDim.x) {
+      const int64_t row = read_index(b, d.idx_slot, d.idx_dtype, base + i);
+      if (row < 0) {
+        atomicOr(status, KTIR_STATUS_NEGATIVE_INDEX);
+        continue;
+      }
+      if (row >= n_rows) continue;  // row wholly past the table end: no effect
+      unsigned h = (unsigned)((unsigned long long)row * 0x9E3779B97F4A7C15ull >> 40) & (cap - 1);
+      for (int probe = 0; probe < cap; ++probe) {
+        long long prev = atomicCAS((unsigned long long*)&set[h], (unsigned long long)-1ll,
+                                   (unsigned long long)row);
+        if (prev == -1) {
+          atomicAdd(&counts[row], 1);
+          break;
+        }
+        if (prev == row) break;
+        h = (h + 1) & (cap - 1);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Apply f once to a register holding one element; fast path for y = x op imm.
+__device__ __forceinline__ float apply_f(const KtirEwProgram& f, float x, int simple_op,
+                                         float simple_imm, int out_dt) {
+  if (simple_op) return round_to(binf(simple_op, x, simple_imm), out_dt);
+  Reg r[KTIR_NREG];
+  Reg res;
+  res.f = x;
+  for (int pc = 0; pc < f.n_instr; ++pc) {
+    const KtirInstr in = f.code[pc];
+    if (in.op == OP_LD) {
+      r[in.dst].f = x;
+    } else if (in.op == OP_ST) {
+      res = convert(r[in.a], in.dt, f.view[1].dtype);
+    } else {
+      exec_arith(in, r);
+    }
+  }
+  return res.f;
+}
+
+// Phase 2: the first position to claim a row's count applies f count times.
+// A 16-lane group owns one index position; rows move in 16-byte vectors.
+__global__ void __launch_bounds__(256) k_rmw_apply(const __grid_constant__ KtirGatherRmwDesc d,
+                                                   const __grid_constant__ KtirBuffers b,
+                                                   int* __restrict__ counts, int64_t n_rows,
+                                                   int simple_op, float simple_imm) {
+  const int sub = threadIdx.x & 15;
+  const int64_t group = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int64_t ngroups = ((int64_t)gridDim.x * blockDim.x) >> 4;
+  const int64_t total = (int64_t)d.n_units * d.unit_len;
+  __half* table = (__half*)b.base[d.table_slot];
+  const int64_t tnumel = b.numel[d.table_slot];
+  const int out_dt = d.f.view[1].dtype;
+  for (int64_t g = group; g < total; g += ngroups) {
+    const int64_t unit = g / d.unit_len;
+    const int64_t i = g - unit * d.unit_len;
+    const int64_t row = read_index(b, d.idx_slot, d.idx_dtype,
+                                   d.idx_off + unit * d.idx_unit_stride + i);
+    int m = 0;
+    if (sub == 0 && row >= 0 && row < n_rows) m = atomicExch(&counts[row], 0);
+    m = __shfl_sync(0xffffffffu, m, (threadIdx.x & 31) & ~15);
+    if (m <= 0) continue;
+    const int64_t rb = d.table_off + row * d.row_stride;
+    for (int c = sub * 8; c < d.row_len; c += 128) {
+      const int64_t e = rb + c;
+      const bool vec = (c + 8 <= d.row_len) && ((e & 7) == 0) && (e + 8 <= tnumel) && e >= 0;
+      float x[8];
+      if (vec) {
+        uint4 raw = *reinterpret_cast<const uint4*>(table + e);
+        const __half* h = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = __half2float(h[k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          x[k] = (c + k < d.row_len && e + k >= 0 && e + k < tnumel) ? __half2float(table[e + k])
+                                                                     : 0.f;
+      }
+      for (int rep = 0; rep < m; ++rep) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = apply_f(d.f, x[k], simple_op, simple_imm, out_dt);
+      }
+      if (vec) {
+        __half h[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) h[k] = __float2half_rn(x[k]);
+        *reinterpret_cast<uint4*>(table + e) = *reinterpret_cast<uint4*>(h);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (c + k < d.row_len && e + k >= 0 && e + k < tnumel) table[e + k] = __float2half_rn(x[k]);
+      }
+    }
+  }
+}
+
+extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* d, const KtirBuffers* bufs, int32_t* counts,
+                               int64_t n_rows, int32_t* status, void* stream) {
+  if (!d || !bufs || !counts || !status) return set_err(KTIR_ERR_ARG, "ktir_gather_rmw: null argument");
+  if (d->unit_len <= 0 || d->unit_len > 8192)
+    return set_err(KTIR_ERR_UNSUPPORTED, "ktir_gather_rmw: unit length must be in [1, 8192]");
+  int cap = 1;
+  while (cap < 2 * d->unit_len) cap <<= 1;
+  const size_t smem = (size_t)cap * sizeof(long long);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_rmw_count, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return set_err(KTIR_ERR_CUDA, cudaGetErrorString(e));
+  }
+  k_rmw_count<<<d->n_units, 512, smem, s>>>(*d, *bufs, counts, n_rows, status);
+  int rc = check_launch("ktir_gather_rmw(count)");
+  if (rc) return rc;
+  // recognise y = x op imm (one arithmetic instruction between load and store)
+  int simple_op = 0;
+  float simple_imm = 0.f;
+  const KtirEwProgram& f = d->f;
+  if (f.n_instr == 4 && f.code[0].op == OP_LD && f.code[1].op == OP_IMM &&
+      f.code[2].op >= OP_FADD && f.code[2].op <= OP_FMINIMUM && f.code[3].op == OP_ST &&
+      f.code[2].a == f.code[0].dst && f.code[2].b == f.code[1].dst && f.code[3].a == f.code[2].dst &&
+      f.code[2].dt == f.view[1].dtype && f.code[1].dt == f.code[2].dt) {
+    double dv;
+    memcpy(&dv, &f.code[1].imm, sizeof(dv));
+    simple_op = f.code[2].op;
+    simple_imm = f.code[1].dt == KTIR_F16 ? __half2float(__double2half(dv)) : (float)dv;
+  }
+  const int64_t groups = (int64_t)d->n_units * d->unit_len;
+  const int blocks = grid_x(groups * 16, 256, 148 * 64);
+  k_rmw_apply<<<blocks, 256, 0, s>>>(*d, *bufs, counts, n_rows, simple_op, simple_imm);
+  return check_launch("ktir_gather_rmw(apply)");
+}
+
+// ---------------------------------------------------------------------------
+// generic-path kernels
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ Reg combine(int op, Reg a, Reg c, int dt) {
+  Reg r;
+  if (op >= OP_FADD && op <= OP_FPOW) {
+    r.f = round_to(binf(op, a.f, c.f), dt);
+  } else {
+    r.i = wrap_to(bini(op, a.i, c.i), dt);
+  }
+  return r;
+}
+
+__global__ void k_reduce(const __grid_constant__ KtirReduceDesc d,
+                         const __grid_constant__ KtirBuffers b) {
+  const int64_t cols = d.outer * d.inner;
+  const int dt = d.dt;
+  for (int unit = blockIdx.y; unit < d.n_units; unit += gridDim.y) {
+    const int64_t ustep = (int64_t)unit * d.unit_stride;
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < cols;
+         c += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t o = c / d.inner, i = c - o * d.inner;
+      const int64_t base = o * d.n * d.inner + i;
+      for (int64_t t = 0; t < d.n; ++t) {
+        Reg v = load_elem(b, d.in_slot, dt, d.in_off + ustep + base + t * d.inner);
+        store_elem(b, d.in_slot, dt, d.tmp_off + ustep + base + t * d.inner, v, dt);
+      }
+      int64_t m = d.n;
+      while (m > 1) {
+        const int64_t h = m / 2;
+        for (int64_t t = 0; t < h; ++t) {
+          Reg a = load_elem(b, d.in_slot, dt, d.tmp_off + ustep + base + t * d.inner);
+          Reg q = load_elem(b, d.in_slot, dt, d.tmp_off + ustep + base + (t + h) * d.inner);
+          store_elem(b, d.in_slot, dt, d.tmp_off + ustep + base + t * d.inner,
+                     combine(d.combiner, a, q, dt), dt);
+        }
+        if (m & 1) {
+          Reg tail = load_elem(b, d.in_slot, dt, d.tmp_off + ustep + base + 2 * h * d.inner);
+          store_elem(b, d.in_slot, dt, d.tmp_off + ustep + base + h * d.inner, tail, dt);
+        }
+        m = h + (m & 1);
+      }
+      Reg res = load_elem(b, d.in_slot, dt, d.tmp_off + ustep + base);
+      store_elem(b, d.out_slot, dt, d.out_off + ustep + c, res, dt);
+    }
+  }
+}
+
+extern "C" int ktir_reduce(const KtirReduceDesc* d, const KtirBuffers* bufs, void* stream) {
+  if (!d || !bufs) return set_err(KTIR_ERR_ARG, "ktir_reduce: null descriptor");
+  const int64_t cols = d->outer * d->inner;
+  dim3 grid(grid_x(cols, 128, 4096), d->n_units < 65535 ? d->n_units : 65535);
+  k_reduce<<<grid, 128, 0, (cudaStream_t)stream>>>(*d, *bufs);
+  return check_launch("ktir_reduce");
+}
+
+__global__ void k_matmul(const __grid_constant__ KtirMatmulDesc d,
+                         const __grid_constant__ KtirBuffers b, const int64_t* __restrict__ ut) {
+  const int64_t total = d.batch * d.m * d.n;
+  for (int unit = blockIdx.y; unit < d.n_units; unit += gridDim.y) {
+    const int64_t ao = d.a.off + (d.a.unit_col >= 0 ? ut[(int64_t)unit * d.unit_cols + d.a.unit_col] : 0);
+    const int64_t bo = d.b.off + (d.b.unit_col >= 0 ? ut[(int64_t)unit * d.unit_cols + d.b.unit_col] : 0);
+    const int64_t oo = d.out.off + (d.out.unit_col >= 0 ? ut[(int64_t)unit * d.unit_cols + d.out.unit_col] : 0);
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t bi = e / (d.m * d.n);
+      const int64_t r = (e / d.n) % d.m;
+      const int64_t c = e % d.n;
+      const bool fl = is_float(d.a.dtype);
+      float acc = 0.f;
+      long long iacc = 0;
+      for (int64_t k = 0; k < d.k; ++k) {
+        Reg x = load_elem(b, d.a.slot, d.a.dtype, ao + bi * d.a.stride[0] + r * d.a.stride[1] + k * d.a.stride[2]);
+        Reg y = load_elem(b, d.b.slot, d.b.dtype, bo + bi * d.b.stride[0] + k * d.b.stride[1] + c * d.b.stride[2]);
+        if (fl) acc = fmaf(x.f, y.f, acc);
+        else iacc += x.i * y.i;
+      }
+      Reg out;
+      if (fl) out.f = round_to(acc, d.out.dtype);
+      else out.i = wrap_to(iacc, d.out.dtype);
+      store_elem(b, d.out.slot, d.out.dtype,
+                 oo + bi * d.out.stride[0] + r * d.out.stride[1] + c * d.out.stride[2], out,
+                 fl ? d.out.dtype : KTIR_I64);
+    }
+  }
+}
+
+extern "C" int ktir_matmul(const KtirMatmulDesc* d, const KtirBuffers* bufs,
+                           const int64_t* unit_table, void* stream) {
+  if (!d || !bufs) return set_err(KTIR_ERR_ARG, "ktir_matmul: null descriptor");
+  dim3 grid(grid_x(d->batch * d->m * d->n, 128, 8192), d->n_units < 65535 ? d->n_units : 65535);
+  k_matmul<<<grid, 128, 0, (cudaStream_t)stream>>>(*d, *bufs, unit_table);
+  return check_launch("ktir_matmul");
+}
+
+__global__ void k_offsets(const __grid_constant__ KtirOffsetsDesc d,
+                          const __grid_constant__ KtirBuffers b, const int64_t* __restrict__ ut,
+                          int unit_cols, const int64_t* __restrict__ offs) {
+  for (int unit = blockIdx.y; unit < d.n_units; unit += gridDim.y) {
+    const int64_t bo = d.buf.off + (d.buf.unit_col >= 0 ? ut[(int64_t)unit * unit_cols + d.buf.unit_col] : 0);
+    const int64_t dn = d.dense.off + (d.dense.unit_col >= 0 ? ut[(int64_t)unit * unit_cols + d.dense.unit_col] : 0);
+    if (d.scatter) {
+      // offsets were de-duplicated on the host keeping the last writer
+      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < d.count;
+           i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = offs[(int64_t)unit * d.count + i];
+        if (o < 0) continue;
+        Reg v = load_elem(b, d.dense.slot, d.dense.dtype, dn + i);
+        store_elem(b, d.buf.slot, d.buf.dtype, bo + o, v, d.dense.dtype);
+      }
+    } else {
+      for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < d.count;
+           i += (int64_t)gridDim.x * blockDim.x) {
+        Reg v = load_elem(b, d.buf.slot, d.buf.dtype, bo + offs[(int64_t)unit * d.count + i]);
+        store_elem(b, d.dense.slot, d.dense.dtype, dn + i, v, d.buf.dtype);
+      }
+    }
+  }
+}
+
+extern "C" int ktir_offsets(const KtirOffsetsDesc* d, const KtirBuffers* bufs,
+                            const int64_t* unit_table, const int64_t* offsets, void* stream) {
+  if (!d || !bufs || !offsets) return set_err(KTIR_ERR_ARG, "ktir_offsets: null argument");
+  if (d->count == 0) return KTIR_OK;
+  dim3 grid(grid_x(d->count, 256, 4096), d->n_units < 65535 ? d->n_units : 65535);
+  // the unit table width travels in dense.pad
+  k_offsets<<<grid, 256, 0, (cudaStream_t)stream>>>(*d, *bufs, unit_table, d->dense.pad, offsets);
+  return check_launch("ktir_offsets");
+}
+
+__device__ __forceinline__ int64_t indirect_offset(const KtirIndirectDesc& d, const KtirBuffers& b,
+                                                   const int64_t* direct, const int64_t* idx_offs,
+                                                   int64_t unit, int64_t i, int* status, bool* ok) {
+  const int64_t p = unit * d.count + i;
+  int64_t off = direct[p];
+  *ok = true;
+  for (int k = 0; k < d.n_ind; ++k) {
+    const int64_t v = read_index(b, d.idx_slot[k], d.idx_dtype[k],
+                                 idx_offs[(int64_t)k * d.n_units * d.count + p]);
+    if (v < 0) {
+      atomicOr(status, KTIR_STATUS_NEGATIVE_INDEX);
+      *ok = false;
+    }
+    off += v * d.stride[k];
+  }
+  return off;
+}
+
+__global__ void k_indirect_gather(const __grid_constant__ KtirIndirectDesc d,
+                                  const __grid_constant__ KtirBuffers b,
+                                  const int64_t* __restrict__ ut, int unit_cols,
+                                  const int64_t* __restrict__ direct,
+                                  const int64_t* __restrict__ idx_offs, int* status) {
+  for (int unit = blockIdx.y; unit < d.n_units; unit += gridDim.y) {
+    const int64_t bo = d.buf.off + (d.buf.unit_col >= 0 ? ut[(int64_t)unit * unit_cols + d.buf.unit_col] : 0);
+    const int64_t dn = d.dense.off + (d.dense.unit_col >= 0 ? ut[(int64_t)unit * unit_cols + d.dense.unit_col] : 0);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < d.count;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      bool ok;
+      const int64_t o = indirect_offset(d, b, direct, idx_offs, unit, i, status, &ok);
+      Reg v = load_elem(b, d.buf.slot, d.buf.dtype, ok ? bo + o : -1);
+      store_elem(b, d.dense.slot, d.dense.dtype, dn + i, v, d.buf.dtype);
+    }
+  }
+}
+
+// Scatter in enumeration order (one thread per unit, units in order) so the
+// last writer wins exactly as in the reference's fancy-index assignment.
+__global__ void k_indirect_scatter(const __grid_constant__ KtirIndirectDesc d,
+                                   const __grid_constant__ KtirBuffers b,
+                                   const int64_t* __restrict__ ut, int unit_cols,
+                                   const int64_t* __restrict__ direct,
+                                   const int64_t* __restrict__ idx_offs, int* status) {
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  for (int unit = 0; unit < d.n_units; ++unit) {
+    const int64_t bo = d.buf.off + (d.buf.unit_col >= 0 ? ut[(int64_t)unit * unit_cols + d.buf.unit_col] : 0);
+    const int64_t dn = d.dense.off + (d.dense.unit_col >= 0 ? ut[(int64_t)unit * unit_cols + d.dense.unit_col] : 0);
+    for (int64_t i = 0; i < d.count; ++i) {
+      bool ok;
+      const int64_t o = indirect_offset(d, b, direct, idx_offs, unit, i, status, &ok);
+      if (!ok) continue;
+      Reg v = load_elem(b, d.dense.slot, d.dense.dtype, dn + i);
+      store_elem(b, d.buf.slot, d.buf.dtype, bo + o, v, d.dense.dtype);
+    }
+  }
+}
+
+extern "C" int ktir_indirect(const KtirIndirectDesc* d, const KtirBuffers* bufs,
+                             const int64_t* unit_table, const int64_t* direct,
+                             const int64_t* idx_offs, int32_t* status, void* stream) {
+  if (!d || !bufs || !direct || !status) return set_err(KTIR_ERR_ARG, "ktir_indirect: null argument");
+  if (d->n_ind > 4) return set_err(KTIR_ERR_UNSUPPORTED, "ktir_indirect: more than 4 indirect dims");
+  if (d->count == 0) return KTIR_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int ucols = d->dense.pad;
+  if (d->scatter) {
+    k_indirect_scatter<<<1, 1, 0, s>>>(*d, *bufs, unit_table, ucols, direct, idx_offs, status);
+  } else {
+    dim3 grid(grid_x(d->count, 256, 4096), d->n_units < 65535 ? d->n_units : 65535);
+    k_indirect_gather<<<grid, 256, 0, s>>>(*d, *bufs, unit_table, ucols, direct, idx_offs, status);
+  }
+  return check_launch("ktir_indirect");
+}

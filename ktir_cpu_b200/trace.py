@@ -1,0 +1,1260 @@
+"""Host shadow pass: per-core scalar execution that records tile work as a DAG.
+
+This replaces the reference's execution engine (ktir_cpu/grid.py:471-570
+running every op through the handler registry, dialects/registry.py:87-115)
+for one purpose: it evaluates everything that is *scalar* on the host —
+core ids, loop bounds, index arithmetic, memory views and access tiles,
+exactly as the reference does — and records everything that touches *tile
+data* as nodes of a dataflow graph.  Tile data never exists on the host; the
+graph is lowered onto device kernels by :mod:`ktir_cpu_b200.lower`.
+
+What is replicated here because results depend on it:
+
+* core order and grid coordinates (grid.py:402-416, x fastest);
+* the HBM address space: stick-aligned allocations from 0x10000, access
+  resolution to the allocation holding the start address, zero fill past its
+  end on reads and truncation on writes (memory.py:97-288) — recorded as the
+  bounds every device access is clamped to;
+* LX accounting with scoped frees and the exact MemoryError text
+  (grid.py:204-311, interpreter.py:216-226, control_ops.py:77-167);
+* NumPy dtype promotion for every tile op, including the float16 coercion of
+  scalar operands in float binops (dialects/_helpers.py:35-54) and the
+  float32 evaluation of math ops (ops/math_ops.py:30-268);
+* the error conventions of the reference (ValueError for unknown ops and
+  unmapped reads, IndexError for negative indices — raised after the device
+  run reports them — MemoryError for LX overflow).
+
+Data-dependent control flow or addressing (a scalar extracted from a tile
+steering scf.for / scf.if or an access tile) is rejected with
+NotImplementedError: every supported program has a data-independent schedule.
+"""
+
+from __future__ import annotations
+
+import bisect
+import operator
+from dataclasses import dataclass, field
+from typing import Any, Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from .affine import AffineMap, AffineSet, BoxSet
+from .ir import IRFunction, Operation, Region
+
+STICK = 128
+LX_CAPACITY = 2 * 1024 * 1024
+
+NP = {
+    "f16": np.float16, "fp16": np.float16, "float16": np.float16,
+    "f32": np.float32, "float32": np.float32,
+    "i1": np.bool_, "i32": np.int32, "si32": np.int32, "index": np.int32,
+    "i64": np.int64, "si64": np.int64,
+}
+LABEL = {np.dtype(np.float16): "f16", np.dtype(np.float32): "f32", np.dtype(np.int32): "i32",
+         np.dtype(np.int64): "i64", np.dtype(np.bool_): "i1"}
+
+
+def np_dtype(name: str) -> np.dtype:
+    if name in ("fp8", "mxfp8"):
+        raise NotImplementedError(f"dtype {name!r} is a placeholder")
+    try:
+        return np.dtype(NP[name])
+    except KeyError:
+        raise ValueError(f"Unsupported KTIR dtype: {name!r}")
+
+
+def bpe(name: str) -> int:
+    return np_dtype(name).itemsize
+
+
+# ---------------------------------------------------------------------------
+# host-side model of the simulated HBM address space
+# ---------------------------------------------------------------------------
+
+@dataclass
+class Buffer:
+    index: int
+    name: str
+    byte_base: int
+    nbytes: int
+    dtype: np.dtype
+    shape: Tuple[int, ...]
+
+    @property
+    def numel(self) -> int:
+        return self.nbytes // self.dtype.itemsize
+
+
+class AddressSpace:
+    def __init__(self) -> None:
+        self.buffers: List[Buffer] = []
+        self._starts: List[int] = []
+        self.next_ptr = 0x10000
+
+    def allocate(self, name: str, nbytes: int, dtype, shape) -> int:
+        ptr = self.next_ptr
+        self.next_ptr = (ptr + nbytes + STICK - 1) & ~(STICK - 1)
+        buf = Buffer(len(self.buffers), name, ptr, nbytes, np.dtype(dtype), tuple(shape))
+        self.buffers.append(buf)
+        k = bisect.bisect_right(self._starts, ptr)
+        self._starts.insert(k, ptr)
+        return ptr // STICK
+
+    def add_fixed(self, name: str, byte_addr: int, nbytes: int, dtype, shape) -> Buffer:
+        buf = Buffer(len(self.buffers), name, byte_addr, nbytes, np.dtype(dtype), tuple(shape))
+        self.buffers.append(buf)
+        k = bisect.bisect_right(self._starts, byte_addr)
+        self._starts.insert(k, byte_addr)
+        return buf
+
+    def find(self, addr: int) -> Optional[Buffer]:
+        by_start = {b.byte_base: b for b in self.buffers}
+        if addr in by_start:
+            return by_start[addr]
+        k = bisect.bisect_right(self._starts, addr) - 1
+        if k >= 0:
+            b = by_start[self._starts[k]]
+            if b.byte_base < addr < b.byte_base + b.nbytes:
+                return b
+        return None
+
+
+# ---------------------------------------------------------------------------
+# graph
+# ---------------------------------------------------------------------------
+
+class Node:
+    __slots__ = ("id", "kind", "shape", "dtype", "ins", "attrs", "label", "pyscalar", "core")
+
+    def __init__(self, id, kind, shape, dtype, ins=(), attrs=None, label=None, pyscalar=False,
+                 core=0):
+        self.id = id
+        self.kind = kind
+        self.shape = tuple(int(s) for s in shape)
+        self.dtype = np.dtype(dtype)
+        self.ins = tuple(ins)
+        self.attrs = attrs or {}
+        self.label = label or LABEL.get(self.dtype, "f16")
+        self.pyscalar = pyscalar
+        self.core = core
+
+    @property
+    def numel(self) -> int:
+        return int(np.prod(self.shape)) if self.shape else 1
+
+    @property
+    def nbytes(self) -> int:
+        return self.numel * self.dtype.itemsize
+
+    def proto(self):
+        """A NumPy value with this node's dtype behaviour, for promotion queries."""
+        if self.shape:
+            return np.zeros((1,) * len(self.shape), dtype=self.dtype)
+        if self.pyscalar:
+            return 0.0 if self.dtype.kind == "f" else (False if self.dtype.kind == "b" else 0)
+        return self.dtype.type(0)
+
+    def __repr__(self):
+        return f"<{self.kind}#{self.id} {self.shape} {self.dtype}>"
+
+
+@dataclass
+class Const:
+    """Immediate scalar operand of an elementwise op (already in its final dtype)."""
+    value: Any
+    dtype: np.dtype
+
+
+@dataclass
+class RectTarget:
+    buf: Buffer
+    off: int                    # element offset of the tile origin inside the buffer
+    shape: Tuple[int, ...]
+    strides: Tuple[int, ...]
+    dtype: np.dtype
+
+
+@dataclass
+class CoordTarget:
+    buf: Buffer
+    off: int
+    offsets: np.ndarray         # element offsets relative to off, enumeration order
+    shape: Tuple[int, ...]      # tile shape the values come in
+    dtype: np.dtype
+
+
+@dataclass
+class IndirectTarget:
+    iat: "IATV"
+
+
+@dataclass
+class Store:
+    core: int
+    seq: int
+    value: Node
+    target: Any
+    mark: int = 0               # number of graph nodes created before this store
+
+
+# ---------------------------------------------------------------------------
+# tracer values
+# ---------------------------------------------------------------------------
+
+@dataclass
+class MemRefV:
+    stick: int
+    shape: Tuple[int, ...]
+    strides: List[int]
+    space: str
+    dtype: str
+    cset: Any = None
+
+    @property
+    def byte_address(self) -> int:
+        return self.stick * STICK
+
+
+@dataclass
+class AccessTileV:
+    byte: int
+    shape: Tuple[int, ...]
+    strides: List[int]
+    dtype: str
+    cset: Any
+    order: Optional[AffineMap]
+
+
+@dataclass
+class IATV:
+    parent: MemRefV
+    shape: Tuple[int, ...]
+    dims: List[dict]            # kind: direct(expr) / indirect(view, exprs); refs resolved
+    views: List[MemRefV]
+    vss: Any
+    vso: Optional[AffineMap]
+    consts: Dict[int, int]      # intermediate variable index -> outer SSA scalar value
+    refs: Dict[str, int]
+
+    def signature(self):
+        return (id(self.vss), self.vso.source if self.vso else None, tuple(self.consts.items()),
+                tuple(sorted(self.refs.items())))
+
+
+class _Yield:
+    __slots__ = ("values",)
+
+    def __init__(self, values):
+        self.values = values
+
+
+def _is_scalar(v) -> bool:
+    return isinstance(v, (int, float, bool, np.integer, np.floating, np.bool_)) or \
+        (isinstance(v, Node) and not v.shape)
+
+
+def _is_tile(v) -> bool:
+    return isinstance(v, Node) and bool(v.shape)
+
+
+def _concrete(v) -> bool:
+    return isinstance(v, (int, float, bool, np.integer, np.floating, np.bool_))
+
+
+class DataDependentError(NotImplementedError):
+    pass
+
+
+def _need_int(v, what: str) -> int:
+    if isinstance(v, Node):
+        raise DataDependentError(
+            f"{what} depends on tile data; this backend needs a data-independent schedule")
+    return int(v)
+
+
+# ---------------------------------------------------------------------------
+# the tracer
+# ---------------------------------------------------------------------------
+
+class CoreState:
+    def __init__(self, cid: int, pos: Tuple[int, int, int]):
+        self.core_id = cid
+        self.pos = pos
+        self.scopes: List[Dict[str, Any]] = [{}]
+        self.lx_used = 0
+        self.lx_bytes: Dict[str, int] = {}
+
+    def push(self):
+        self.scopes.append({})
+
+    def pop(self):
+        scope = self.scopes.pop()
+        for n in scope:
+            self.untrack(n)
+
+    def set(self, n, v):
+        self.scopes[-1][n] = v
+
+    def get(self, n):
+        for s in reversed(self.scopes):
+            if n in s:
+                return s[n]
+        raise KeyError(f"Value '{n}' not found in core {self.core_id}")
+
+    def has(self, n) -> bool:
+        return any(n in s for s in self.scopes)
+
+    def track(self, n, size):
+        if self.lx_used + size > LX_CAPACITY:
+            raise MemoryError(
+                f"LX scratchpad overflow on core {self.core_id}: requested {size} bytes, "
+                f"available {LX_CAPACITY - self.lx_used} bytes (capacity {LX_CAPACITY} bytes)")
+        self.lx_bytes[n] = size
+        self.lx_used += size
+
+    def untrack(self, n):
+        if n in self.lx_bytes:
+            self.lx_used -= self.lx_bytes.pop(n)
+
+
+class Trace:
+    """Result of tracing one function call: graph nodes + ordered stores."""
+
+    def __init__(self, space: AddressSpace, grid):
+        self.space = space
+        self.grid = grid
+        self.nodes: List[Node] = []
+        self.stores: List[Store] = []
+        self.lx_peak: Dict[int, int] = {}
+
+
+class Tracer:
+    def __init__(self, func: IRFunction, space: AddressSpace, scalars: Dict[str, Any],
+                 pointers: Dict[str, int], rewrites: Optional[Dict[int, Any]] = None):
+        self.func = func
+        self.space = space
+        self.scalars = scalars
+        self.pointers = pointers
+        self.trace = Trace(space, func.grid)
+        self.core: Optional[CoreState] = None
+        self.seq = 0
+        self.rewrites = rewrites or {}
+
+    # -- node helpers ----------------------------------------------------------
+    def node(self, kind, shape, dtype, ins=(), attrs=None, label=None, pyscalar=False) -> Node:
+        n = Node(len(self.trace.nodes), kind, shape, dtype, ins, attrs, label, pyscalar,
+                 self.core.core_id if self.core else 0)
+        self.trace.nodes.append(n)
+        return n
+
+    def const_tile(self, value, shape, dtype, label=None) -> Node:
+        return self.node("const", shape, dtype, (), {"value": value}, label)
+
+    # -- driver ----------------------------------------------------------------
+    def run(self) -> Trace:
+        nx, ny, nz = self.func.grid
+        for cid in range(nx * ny * nz):
+            z, r = divmod(cid, nx * ny)
+            y, x = divmod(r, nx)
+            self.core = CoreState(cid, (x, y, z))
+            for aname, _ in self.func.arguments:
+                key = aname.lstrip("%")
+                if key in self.pointers:
+                    self.core.set(aname, self.pointers[key])
+                elif key in self.scalars:
+                    self.core.set(aname, self.scalars[key])
+            self.run_ops(self.func.operations)
+        return self.trace
+
+    def run_ops(self, ops: List[Operation]):
+        r = None
+        for op in ops:
+            r = self.run_op(op)
+        return r
+
+    def run_op(self, op: Operation):
+        core = self.core
+        rw = self.rewrites.get(id(op))
+        if rw is not None:
+            res = rw(self, op)
+        else:
+            h = getattr(self, "op_" + op.op_type.replace(".", "_"), None)
+            if h is None:
+                h = _ELEMENTWISE.get(op.op_type)
+                if h is None:
+                    raise ValueError(f"Unknown operation: {op.op_type}")
+                res = h(self, op)
+            else:
+                res = h(op)
+        if op.results and res is not None:
+            vals = res if isinstance(res, tuple) else (res,)
+            if len(vals) != len(op.results):
+                raise RuntimeError(
+                    f"{op.op_type}: expected {len(op.results)} result(s), got {len(vals)}")
+            for name, val in zip(op.results, vals):
+                core.set(name, val)
+                if _is_tile(val):
+                    core.track(name, val.nbytes)
+        return res
+
+    # -- grid / views ------------------------------------------------------------
+    def op_ktdp_get_compute_tile_id(self, op):
+        if len(op.results) <= 1:
+            return self.core.pos[0]
+        return tuple(self.core.pos[d] for d in range(len(op.results)))
+
+    def op_ktdp_construct_memory_view(self, op):
+        a = op.attributes
+        ptr = _need_int(self.core.get(op.operands[0]), "memory view base")
+        shape = tuple(_need_int(self.core.get(s), "view size") if isinstance(s, str) else s
+                      for s in a["shape"])
+        strides = [_need_int(self.core.get(s), "view stride") if isinstance(s, str) else s
+                   for s in a["strides"]]
+        cset = a.get("coordinate_set")
+        if isinstance(cset, BoxSet) and not cset.is_concrete:
+            syms = tuple(int(self.core.get(s)) for s in a["shape"] if isinstance(s, str))
+            cset = cset.specialize(syms)
+        if a["memory_space"] != "HBM":
+            raise NotImplementedError("memory views in LX are not supported by the B200 backend")
+        return MemRefV(ptr, tuple(int(s) for s in shape), [int(s) for s in strides],
+                       a["memory_space"], a["dtype"], cset)
+
+    def op_ktdp_construct_access_tile(self, op):
+        parent = self.core.get(op.operands[0])
+        if not isinstance(parent, MemRefV):
+            raise NotImplementedError("access tiles over distributed views are not supported")
+        idx = [_need_int(self.core.get(o), "access tile index") for o in op.operands[1:]]
+        a = op.attributes
+        base = a["base_map"].eval(idx)
+        off = sum(int(c) * s for c, s in zip(base, parent.strides))
+        cset = a["coordinate_set"]
+        if isinstance(cset, BoxSet) and not cset.is_concrete:
+            raise NotImplementedError("construct_access_tile: symbolic access_tile_set")
+        return AccessTileV(parent.byte_address + off * bpe(parent.dtype), tuple(a["shape"]),
+                           list(parent.strides), parent.dtype, cset, a.get("coordinate_order"))
+
+    def op_ktdp_construct_indirect_access_tile(self, op):
+        a = op.attributes
+        parent = self.core.get(op.operands[0])
+        views = [self.core.get(o) for o in op.operands[1:]]
+        consts: Dict[int, int] = {}
+        for i, v in enumerate(a["var_names"]):
+            if self.core.has("%" + v):
+                val = self.core.get("%" + v)
+                if _concrete(val):
+                    consts[i] = int(val)
+        shape = tuple(a["shape"])
+        vss = a["variables_space_set"]
+        if consts:
+            if isinstance(vss, BoxSet):
+                for i in consts:
+                    if vss.lo[i] != 0 or vss.hi[i] > 1:
+                        raise ValueError(
+                            f"construct_indirect_access_tile: intermediate variable "
+                            f"%{a['var_names'][i]} (index {i}) is an outer SSA value but its "
+                            f"dimension in variables_space_set has a non-zero range.")
+            else:
+                pts = vss.enumerate_array(shape)
+                for i in consts:
+                    if pts.size and np.any(pts[:, i] != 0):
+                        raise ValueError(
+                            f"construct_indirect_access_tile: intermediate variable "
+                            f"%{a['var_names'][i]} (index {i}) is an outer SSA value but its "
+                            f"dimension in variables_space_set has a non-zero range.")
+        refs: Dict[str, int] = {}
+        for d in a["dims"]:
+            for e in (d.get("exprs") or [d.get("expr")]):
+                _collect_refs(e, refs)
+        for r in list(refs):
+            refs[r] = _need_int(self.core.get(r), "indirect subscript")
+        return IATV(parent, shape, list(a["dims"]), views, vss,
+                    a.get("variables_space_order"), consts, refs)
+
+    # -- loads / stores ------------------------------------------------------------
+    def _resolve(self, byte: int, dtype: str, what: str) -> Tuple[Buffer, int]:
+        buf = self.space.find(byte)
+        if buf is None:
+            raise ValueError(f"{what} from unmapped address 0x{byte:x}")
+        if buf.dtype != np_dtype(dtype):
+            raise NotImplementedError(
+                f"access as {dtype} to a buffer holding {buf.dtype}: reinterpreting element "
+                f"types is not supported by the B200 backend")
+        return buf, (byte - buf.byte_base) // bpe(dtype)
+
+    def _coords(self, at: AccessTileV) -> np.ndarray:
+        pts = at.cset.enumerate_array(at.shape)
+        if at.order is not None:
+            out = at.order.eval(list(pts.T))
+            pts = np.stack([np.broadcast_to(np.asarray(o, np.int64), (pts.shape[0],))
+                            for o in out], axis=1)
+        return pts
+
+    def op_ktdp_load(self, op):
+        t = self.core.get(op.operands[0])
+        rshape = op.attributes.get("result_shape")
+        if isinstance(t, IATV):
+            if t.vso is not None and not t.vso.is_permutation():
+                raise ValueError("indirect_load: variables_space_order must permute its input "
+                                 f"dimensions; got non-permutation map: {t.vso.source}")
+            pb, poff = self._resolve(t.parent.byte_address, t.parent.dtype, "Read")
+            shape = tuple(rshape or t.shape)
+            return self.node("load", shape, np_dtype(t.parent.dtype), (),
+                             {"mode": "indirect", "iat": t, "buf": pb, "off": poff})
+        if isinstance(t.cset, BoxSet) and t.order is None:
+            off = sum(lo * s for lo, s in zip(t.cset.lo, t.strides))
+            byte = t.byte + off * bpe(t.dtype)
+            buf, eoff = self._resolve(byte, t.dtype, "Read")
+            shape = t.cset.extent()
+            return self.node("load", shape, np_dtype(t.dtype), (),
+                             {"mode": "rect", "buf": buf, "off": eoff,
+                              "strides": tuple(t.strides[:len(shape)])})
+        buf, eoff = self._resolve(t.byte, t.dtype, "Read")
+        coords = self._coords(t)
+        offs = (coords.astype(np.int64) * np.asarray(t.strides[:coords.shape[1]], np.int64)).sum(1) \
+            if coords.size else np.zeros(0, np.int64)
+        shape = tuple(rshape or t.shape)
+        if int(np.prod(shape)) != offs.size:
+            raise ValueError(f"ktdp.load: access set has {offs.size} points but the result "
+                             f"type holds {int(np.prod(shape))}")
+        return self.node("load", shape, np_dtype(t.dtype), (),
+                         {"mode": "coords", "buf": buf, "off": eoff, "offsets": offs})
+
+    def op_ktdp_store(self, op):
+        val = self.core.get(op.operands[0])
+        if not _is_tile(val):
+            raise TypeError(f"ktdp.store expects a Tile, got {type(val)}")
+        t = self.core.get(op.operands[1])
+        if isinstance(t, IATV):
+            if tuple(val.shape) != tuple(t.shape):
+                raise ValueError(
+                    f"indirect_store: source tile shape {tuple(val.shape)} does not match "
+                    f"IAT shape {tuple(t.shape)}")
+            if t.vso is not None and not t.vso.is_permutation():
+                raise ValueError("indirect_store: variables_space_order must permute its input "
+                                 f"dimensions; got non-permutation map: {t.vso.source}")
+            self._resolve(t.parent.byte_address, t.parent.dtype, "Write")
+            tgt = IndirectTarget(t)
+        elif isinstance(t.cset, BoxSet) and t.order is None:
+            off = sum(lo * s for lo, s in zip(t.cset.lo, t.strides))
+            byte = t.byte + off * bpe(t.dtype)
+            buf, eoff = self._resolve(byte, t.dtype, "Write")
+            shape = t.cset.extent()
+            if int(np.prod(shape)) != val.numel:
+                raise ValueError(f"ktdp.store: tile of {val.numel} elements into a box of "
+                                 f"{int(np.prod(shape))}")
+            tgt = RectTarget(buf, eoff, shape, tuple(t.strides[:len(shape)]), np_dtype(t.dtype))
+        else:
+            buf, eoff = self._resolve(t.byte, t.dtype, "Write")
+            coords = self._coords(t)
+            offs = (coords.astype(np.int64) * np.asarray(t.strides[:coords.shape[1]], np.int64)
+                    ).sum(1) if coords.size else np.zeros(0, np.int64)
+            if offs.size != val.numel:
+                raise ValueError(f"ktdp.store: tile of {val.numel} elements into an access set "
+                                 f"of {offs.size}")
+            tgt = CoordTarget(buf, eoff, offs, val.shape, np_dtype(t.dtype))
+        self.trace.stores.append(Store(self.core.core_id, self.seq, val, tgt,
+                                       len(self.trace.nodes)))
+        self.seq += 1
+        return None
+
+    # -- constants, casts ----------------------------------------------------------
+    def op_arith_constant(self, op):
+        a = op.attributes
+        if a.get("is_tensor"):
+            dt = np_dtype(a["dtype"])
+            if a.get("dense_list"):
+                arr = np.array(a["value"], dtype=dt).reshape(a["shape"])
+                return self.node("dense", arr.shape, dt, (), {"value": arr}, a["dtype"])
+            return self.const_tile(dt.type(a["value"]), a["shape"], dt, a["dtype"])
+        return a.get("value", 0)
+
+    def _cast_to(self, v, target: np.dtype, label: str, floating: bool, name: str):
+        if _is_tile(v):
+            if v.dtype == target:
+                return v
+            cat = "f" if floating else "iu"
+            if v.dtype.kind not in cat:
+                raise TypeError(f"{name} expects {'float' if floating else 'integer'} Tile")
+            return self.node("ew", v.shape, target, (v,), {"op": "cast"}, label)
+        if isinstance(v, Node):
+            if v.dtype == target and not v.pyscalar:
+                return v
+            return self.node("ew", (), target, (v,), {"op": "cast"}, label)
+        if isinstance(v, target.type):
+            return v
+        r = target.type(v)
+        if target.kind == "f" and np.isinf(r) and not np.isinf(float(v)):
+            raise OverflowError(f"{name}: {v} overflows {target}")
+        return r
+
+    def op_arith_extf(self, op):
+        v = self.core.get(op.operands[0])
+        if not isinstance(v, Node):
+            return np.float32(v)
+        return self._cast_to(v, np.dtype(np.float32), "f32", True, "extf")
+
+    def op_arith_truncf(self, op):
+        return self._cast_to(self.core.get(op.operands[0]), np.dtype(np.float16), "f16", True,
+                             "truncf")
+
+    def _int_cast(self, op, target, label):
+        v = self.core.get(op.operands[0])
+        if isinstance(v, Node):
+            return self.node("ew", v.shape, target, (v,), {"op": "cast"}, label)
+        return int(v)
+
+    def op_arith_extsi(self, op):
+        return self._int_cast(op, np.dtype(np.int64), "i64")
+
+    op_arith_extui = op_arith_extsi
+
+    def op_arith_trunci(self, op):
+        return self._int_cast(op, np.dtype(np.int32), "i32")
+
+    def op_arith_fptosi(self, op):
+        return self._int_cast(op, np.dtype(np.int32), "i32")
+
+    op_arith_fptoui = op_arith_fptosi
+
+    def op_arith_sitofp(self, op):
+        v = self.core.get(op.operands[0])
+        dst = op.attributes.get("dst_type") or (op.result_types[0] if op.result_types else "f32")
+        dname = _elem(dst) or "f32"
+        dt = np_dtype(dname)
+        if isinstance(v, Node):
+            return self.node("ew", v.shape, dt, (v,), {"op": "cast"}, dname)
+        return dt.type(v)
+
+    def op_arith_uitofp(self, op):
+        v = self.core.get(op.operands[0])
+        if isinstance(v, Node):
+            return self.node("ew", v.shape, np.float32, (v,), {"op": "cast"}, "f32")
+        return float(v)
+
+    def op_arith_index_cast(self, op):
+        v = self.core.get(op.operands[0])
+        if isinstance(v, Node):
+            raise DataDependentError("arith.index_cast of tile data")
+        return int(v)
+
+    op_arith_index_castui = op_arith_index_cast
+
+    def op_arith_bitcast(self, op):
+        v = self.core.get(op.operands[0])
+        dst = _elem(op.attributes.get("dst_type", "f32")) or "f32"
+        if isinstance(v, Node):
+            return self.node("ew", v.shape, np_dtype(dst), (v,), {"op": "bitcast"}, dst)
+        if dst == "f32":
+            return float(np.frombuffer(int(v).to_bytes(4, "little", signed=(v < 0)),
+                                       dtype=np.float32)[0])
+        return int(np.frombuffer(np.float32(v).tobytes(), dtype=np.int32)[0])
+
+    # -- elementwise arithmetic ------------------------------------------------------
+    def ew(self, opname: str, operands: Sequence[Any], fn, label_from=None, attrs=None):
+        """Record an elementwise op; result dtype/shape from NumPy on prototypes."""
+        protos = [o.proto() if isinstance(o, Node) else o for o in operands]
+        with np.errstate(all="ignore"):
+            r = fn(*protos)
+        rdt = np.asarray(r).dtype if not isinstance(r, (bool,)) else np.dtype(np.bool_)
+        tiles = [o for o in operands if _is_tile(o)]
+        if tiles:
+            shape = np.broadcast_shapes(*[t.shape for t in tiles])
+            pys = False
+        else:
+            shape = ()
+            pys = isinstance(r, (float, int, bool)) and not isinstance(r, np.generic)
+        ins = [o if isinstance(o, Node) else Const(o, np.asarray(o).dtype) for o in operands]
+        lab = label_from.label if isinstance(label_from, Node) else None
+        a = {"op": opname}
+        if attrs:
+            a.update(attrs)
+        return self.node("ew", shape, rdt, ins, a, lab, pys)
+
+
+def _elem(t: Optional[str]) -> Optional[str]:
+    if not t:
+        return None
+    t = t.strip()
+    if t.startswith("tensor<"):
+        return t[len("tensor<"):-1].split("x")[-1]
+    return t
+
+
+def _collect_refs(e, out: dict):
+    if e is None:
+        return
+    if e[0] == "ref":
+        out[e[1]] = None
+        return
+    for c in e[1:]:
+        if isinstance(c, tuple):
+            _collect_refs(c, out)
+
+
+# ---------------------------------------------------------------------------
+# elementwise op handlers (registered by op name)
+# ---------------------------------------------------------------------------
+
+_ELEMENTWISE: Dict[str, Any] = {}
+
+
+def _reg(*names):
+    def deco(fn):
+        for n in names:
+            _ELEMENTWISE[n] = fn
+        return fn
+    return deco
+
+
+_FLOAT_FN = {"arith.addf": ("add", operator.add), "arith.subf": ("sub", operator.sub),
+             "arith.mulf": ("mul", operator.mul), "arith.divf": ("div", operator.truediv),
+             "arith.remf": ("fmod", operator.mod)}
+
+
+def _f16(tr: Tracer, v):
+    """Coerce a scalar operand to float16 as the reference's float binops do."""
+    if isinstance(v, Node):
+        if v.dtype == np.float16 and not v.pyscalar:
+            return v
+        return tr.node("ew", (), np.float16, (v,), {"op": "cast"}, "f16")
+    return np.float16(v)
+
+
+def _float_binop(tr: Tracer, op):
+    name, fn = _FLOAT_FN[op.op_type]
+    a = tr.core.get(op.operands[0])
+    b = tr.core.get(op.operands[1])
+    if _is_scalar(a) and _is_scalar(b):
+        if _concrete(a) and _concrete(b):
+            with np.errstate(all="ignore"):
+                r = fn(np.float16(a), np.float16(b))
+            return r if isinstance(r, np.float16) else np.float16(r)
+        return tr.ew(name, [_f16(tr, a), _f16(tr, b)], lambda x, y: np.float16(fn(x, y)))
+    if _is_tile(a) and _is_tile(b):
+        return tr.ew(name, [a, b], fn, a)
+    if _is_tile(a):
+        return tr.ew(name, [a, _f16(tr, b)], fn, a)
+    return tr.ew(name, [_f16(tr, a), b], fn, b)
+
+
+for _n in _FLOAT_FN:
+    _ELEMENTWISE[_n] = _float_binop
+
+
+def _truncdiv(a, b):
+    return np.trunc(np.asarray(a) / np.asarray(b)).astype(np.asarray(a).dtype)
+
+
+def _truncrem(a, b):
+    return np.asarray(a) - _truncdiv(a, b) * np.asarray(b)
+
+
+def _ceildiv_arr(a, b):
+    return np.ceil(np.asarray(a) / np.asarray(b)).astype(np.result_type(a, b))
+
+
+_INT_FN = {
+    "arith.addi": ("add", operator.add), "arith.subi": ("sub", operator.sub),
+    "arith.muli": ("mul", operator.mul), "arith.divui": ("floordiv", operator.floordiv),
+    "arith.divsi": ("truncdiv", _truncdiv), "arith.floordivsi": ("floordiv", operator.floordiv),
+    "arith.remui": ("mod", operator.mod), "arith.remsi": ("truncrem", _truncrem),
+    "arith.ceildivsi": ("ceildiv", _ceildiv_arr), "arith.ceildivui": ("ceildiv", _ceildiv_arr),
+    "arith.andi": ("and", operator.and_), "arith.ori": ("or", operator.or_),
+    "arith.xori": ("xor", operator.xor), "arith.shli": ("shl", operator.lshift),
+    "arith.shrsi": ("shr", operator.rshift),
+}
+
+_INT_SCALAR = {
+    "arith.divsi": lambda a, b: int(np.trunc(a / b)),
+    "arith.remsi": lambda a, b: a - int(np.trunc(a / b)) * b,
+    "arith.ceildivsi": lambda a, b: -((-a) // b),
+    "arith.ceildivui": lambda a, b: -((-a) // b),
+}
+
+
+def _int_binop(tr: Tracer, op):
+    name, fn = _INT_FN[op.op_type]
+    a = tr.core.get(op.operands[0])
+    b = tr.core.get(op.operands[1])
+    if _concrete(a) and _concrete(b):
+        sfn = _INT_SCALAR.get(op.op_type)
+        if sfn is not None and isinstance(a, int) and isinstance(b, int):
+            return sfn(a, b)
+        return fn(a, b)
+    if isinstance(a, Node) and not _is_tile(a) and _concrete(b):
+        return tr.ew(name, [a, b], fn)
+    if _is_tile(a) and _is_tile(b):
+        return tr.ew(name, [a, b], fn, a)
+    if _is_tile(a):
+        return tr.ew(name, [a, b if isinstance(b, Node) else int(b)], fn, a)
+    if _is_tile(b):
+        return tr.ew(name, [a if isinstance(a, Node) else int(a), b], fn, b)
+    return tr.ew(name, [a, b], fn)
+
+
+for _n in _INT_FN:
+    _ELEMENTWISE[_n] = _int_binop
+
+
+def _shrui(tr: Tracer, op):
+    a = tr.core.get(op.operands[0])
+    b = tr.core.get(op.operands[1])
+    if _concrete(a) and _concrete(b):
+        return (int(a) & 0xFFFFFFFFFFFFFFFF) >> int(b)
+    return tr.ew("shru", [a, b], lambda x, y: x >> y, a if isinstance(a, Node) else None)
+
+
+_ELEMENTWISE["arith.shrui"] = _shrui
+
+
+_MINMAX = {"arith.maxnumf": ("fmax", np.fmax), "arith.minnumf": ("fmin", np.fmin),
+           "arith.maximumf": ("maximum", np.maximum), "arith.maxf": ("maximum", np.maximum),
+           "arith.minimumf": ("minimum", np.minimum), "arith.minf": ("minimum", np.minimum),
+           "arith.maxsi": ("maximum", np.maximum), "arith.minsi": ("minimum", np.minimum),
+           "arith.maxui": ("maximum", np.maximum), "arith.minui": ("minimum", np.minimum)}
+
+
+def _minmax(tr: Tracer, op):
+    name, fn = _MINMAX[op.op_type]
+    a = tr.core.get(op.operands[0])
+    b = tr.core.get(op.operands[1])
+    if _concrete(a) and _concrete(b):
+        if op.op_type in ("arith.maxsi", "arith.maxui"):
+            return max(a, b)
+        if op.op_type in ("arith.minsi", "arith.minui"):
+            return min(a, b)
+        return fn(a, b)
+    ref = a if _is_tile(a) else (b if _is_tile(b) else None)
+    return tr.ew(name, [a, b], fn, ref)
+
+
+for _n in _MINMAX:
+    _ELEMENTWISE[_n] = _minmax
+
+
+@_reg("arith.negf")
+def _negf(tr, op):
+    v = tr.core.get(op.operands[0])
+    if _concrete(v):
+        return -v
+    return tr.ew("neg", [v], operator.neg, v)
+
+
+@_reg("arith.absf", "math.absf", "math.absi")
+def _absf(tr, op):
+    v = tr.core.get(op.operands[0])
+    if _concrete(v):
+        return abs(v)
+    return tr.ew("abs", [v], np.abs, v)
+
+
+_MATH = {"math.exp": "exp", "math.sqrt": "sqrt", "math.rsqrt": "rsqrt", "math.log": "log",
+         "math.log2": "log2", "math.log1p": "log1p", "math.tanh": "tanh", "math.sin": "sin",
+         "math.cos": "cos", "math.ceil": "ceil", "math.floor": "floor", "math.erf": "erf"}
+_MATH_NP = {"exp": np.exp, "sqrt": np.sqrt, "rsqrt": lambda x: 1.0 / np.sqrt(x), "log": np.log,
+            "log2": np.log2, "log1p": np.log1p, "tanh": np.tanh, "sin": np.sin, "cos": np.cos,
+            "ceil": np.ceil, "floor": np.floor}
+
+
+def _erf32(x):
+    a = np.abs(x)
+    t = 1.0 / (1.0 + 0.3275911 * a)
+    poly = t * (0.254829592 + t * (-0.284496736 + t * (1.421413741 + t * (-1.453152027 +
+                                                                            t * 1.061405429))))
+    return np.sign(x) * (1.0 - poly * np.exp(-a * a))
+
+
+@_reg(*_MATH.keys())
+def _math_unary(tr, op):
+    name = _MATH[op.op_type]
+    v = tr.core.get(op.operands[0])
+    if _concrete(v):
+        if name == "erf":
+            return type(v)(_erf32(np.array([float(v)]))[0])
+        return type(v)(_MATH_NP[name](float(v)))
+    if _is_tile(v):
+        # float32 evaluation, cast back to the tile's dtype (ops/math_ops.py:30-268)
+        return tr.node("ew", v.shape, v.dtype, (v,), {"op": name}, v.label)
+    return tr.node("ew", (), v.dtype, (v,), {"op": name}, v.label, v.pyscalar)
+
+
+@_reg("math.powf")
+def _powf(tr, op):
+    a = tr.core.get(op.operands[0])
+    b = tr.core.get(op.operands[1])
+    if _concrete(a) and _concrete(b):
+        return type(a)(float(a) ** float(b))
+    if not _is_tile(a):
+        raise NotImplementedError("math.powf with a scalar base and tile exponent")
+    return tr.node("ew", a.shape, a.dtype, (a, b if isinstance(b, Node) else Const(b, np.dtype(np.float32))),
+                   {"op": "pow"}, a.label)
+
+
+@_reg("math.fma")
+def _fma(tr, op):
+    a, b, c = (tr.core.get(o) for o in op.operands[:3])
+    if _concrete(a) and _concrete(b) and _concrete(c):
+        return type(a)(float(a) * float(b) + float(c))
+    if not (_is_tile(a) and _is_tile(b) and _is_tile(c)):
+        raise NotImplementedError("math.fma needs three tiles")
+    return tr.node("ew", a.shape, a.dtype, (a, b, c), {"op": "fma"}, a.label)
+
+
+def _cmp(tr, op, integer: bool):
+    a = tr.core.get(op.operands[0])
+    b = tr.core.get(op.operands[1])
+    pred = op.attributes["predicate"]
+    valid_i = {"eq", "ne", "slt", "ult", "sle", "ule", "sgt", "ugt", "sge", "uge"}
+    valid_f = {"false", "true", "oeq", "olt", "ole", "ogt", "oge", "one", "ueq", "une", "ult",
+               "ule", "ugt", "uge", "ord", "uno"}
+    if pred not in (valid_i if integer else valid_f):
+        raise NotImplementedError(f"{op.op_type}: unsupported predicate '{pred}'")
+    if _concrete(a) and _concrete(b):
+        return bool(_scalar_cmp(pred, a if integer else float(a), b if integer else float(b)))
+    if not (_is_tile(a) or _is_tile(b)):
+        raise DataDependentError("scalar comparison of tile data")
+    # the reference materialises a scalar side with the tile's dtype (np.full)
+    if not _is_tile(a):
+        a = _splat_like(tr, a, b)
+    if not _is_tile(b):
+        b = _splat_like(tr, b, a)
+    shape = np.broadcast_shapes(a.shape, b.shape)
+    return tr.node("ew", shape, np.bool_, (a, b), {"op": "cmp", "pred": pred,
+                                                   "int": integer}, "i1")
+
+
+def _splat_like(tr, s, like: Node):
+    if isinstance(s, Node):
+        return tr.node("splat", like.shape, like.dtype, (s,), {}, like.label)
+    return tr.const_tile(like.dtype.type(s), like.shape, like.dtype, like.label)
+
+
+def _scalar_cmp(pred, x, y):
+    nan = (x != x) or (y != y)
+    return {
+        "eq": x == y, "ne": x != y, "slt": x < y, "ult": x < y, "sle": x <= y, "ule": x <= y,
+        "sgt": x > y, "ugt": x > y, "sge": x >= y, "uge": x >= y,
+        "false": False, "true": True, "oeq": x == y, "olt": x < y, "ole": x <= y,
+        "ogt": x > y, "oge": x >= y, "one": (x != y) and not nan, "ueq": (x == y) or nan,
+        "une": x != y, "ult_": 0, "ord": not nan, "uno": nan,
+    }.get(pred, None) if pred not in ("ult", "ule", "ugt", "uge") or isinstance(x, int) else \
+        {"ult": (x < y) or nan, "ule": (x <= y) or nan, "ugt": (x > y) or nan,
+         "uge": (x >= y) or nan}[pred]
+
+
+_ELEMENTWISE["arith.cmpi"] = lambda tr, op: _cmp(tr, op, True)
+_ELEMENTWISE["arith.cmpf"] = lambda tr, op: _cmp(tr, op, False)
+
+
+@_reg("arith.select")
+def _select(tr, op):
+    c = tr.core.get(op.operands[0])
+    t = tr.core.get(op.operands[1])
+    f = tr.core.get(op.operands[2])
+    if _concrete(c):
+        return t if c else f
+    if not _is_tile(c):
+        raise DataDependentError("arith.select on a scalar extracted from tile data")
+    ref = t if _is_tile(t) else f
+    lab = ref.label if _is_tile(ref) else "f16"
+    return _select_node(tr, c, t, f, lab)
+
+
+def _select_node(tr, c, t, f, label):
+    protos = [o.proto() if isinstance(o, Node) else o for o in (c, t, f)]
+    rdt = np.asarray(np.where(*protos)).dtype
+    tiles = [o for o in (c, t, f) if _is_tile(o)]
+    shape = np.broadcast_shapes(*[x.shape for x in tiles])
+    ins = [o if isinstance(o, Node) else Const(o, np.asarray(o).dtype) for o in (c, t, f)]
+    return tr.node("ew", shape, rdt, ins, {"op": "select"}, label)
+
+
+# ---------------------------------------------------------------------------
+# tensor / linalg / scf handlers (methods attached to Tracer)
+# ---------------------------------------------------------------------------
+
+def _op_tensor_empty(self, op):
+    a = op.attributes
+    dt = np_dtype(a["dtype"])
+    return self.const_tile(dt.type(0), a["shape"], dt, a["dtype"])
+
+
+def _op_tensor_splat(self, op):
+    s = self.core.get(op.operands[0])
+    shape = tuple(op.attributes.get("shape", ())) or (1,)
+    dname = op.attributes.get("dtype", "f16")
+    if _is_tile(s):
+        s = self.node("extract", (), s.dtype, (s,), {"index": (0,) * len(s.shape)}, s.label)
+    is_int = (isinstance(s, (int, np.integer)) and not isinstance(s, (bool, np.bool_))) or \
+        (isinstance(s, Node) and s.dtype.kind in "iu")
+    dt = np.dtype(np.int32) if is_int else np_dtype(dname)
+    lab = "i32" if is_int else dname
+    if isinstance(s, Node):
+        return self.node("splat", shape, dt, (s,), {}, lab)
+    with np.errstate(all="ignore"):
+        return self.const_tile(np.full((), s, dtype=dt)[()], shape, dt, lab)
+
+
+def _op_tensor_extract(self, op):
+    src = self.core.get(op.operands[0])
+    if _is_tile(src):
+        idx = tuple(_need_int(self.core.get(o), "tensor.extract index") for o in op.operands[1:])
+        if not idx:
+            idx = (0,) * len(src.shape)
+        return self.node("extract", (), src.dtype, (src,), {"index": idx}, src.label)
+    return src
+
+
+def _op_reshape(self, op):
+    src = self.core.get(op.operands[0])
+    ts = op.attributes.get("target_shape")
+    if _is_tile(src) and ts:
+        if int(np.prod(ts)) != src.numel:
+            raise ValueError(f"cannot reshape {src.shape} into {ts}")
+        return self.node("reshape", tuple(ts), src.dtype, (src,), {}, src.label)
+    return src
+
+
+def _op_tensor_from_elements(self, op):
+    vals = [self.core.get(o) for o in op.operands]
+    a = op.attributes
+    if all(_concrete(v) for v in vals):
+        arr = np.array(vals, dtype=np_dtype(a["dtype"])).reshape(a["shape"])
+        return self.node("dense", arr.shape, arr.dtype, (), {"value": arr}, a["dtype"])
+    raise DataDependentError("tensor.from_elements of tile data")
+
+
+def _op_tensor_generate(self, op):
+    a = op.attributes
+    shape = tuple(a["shape"])
+    region = op.regions[0]
+    self.core.push()
+    for d, (name, _) in enumerate(region.args):
+        rs = [1] * len(shape)
+        rs[d] = shape[d]
+        io = self.node("iota", tuple(rs), np.int64, (), {"dim": d}, "index")
+        self.core.set(name, self.node("bcast", shape, np.int64, (io,),
+                                      {"map": tuple(range(len(shape)))}, "index"))
+    r = self.run_ops(region.ops)
+    if isinstance(r, _Yield):
+        r = r.values[0]
+    self.core.pop()
+    dt = np_dtype(a["dtype"])
+    if isinstance(r, Node):
+        if r.shape != shape:
+            r = _bcast_to(self, r, shape)
+        return self.node("ew", shape, dt, (r,), {"op": "cast"}, a["dtype"]) if r.dtype != dt else r
+    return self.const_tile(dt.type(r), shape, dt, a["dtype"])
+
+
+def _yield(self, op):
+    return _Yield([self.core.get(o) for o in op.operands])
+
+
+def _op_return(self, op):
+    return self.core.get(op.operands[0]) if op.operands else None
+
+
+def _bcast_to(tr, v: Node, shape):
+    """NumPy broadcasting of v (aligned right) to shape."""
+    nd = len(shape)
+    off = nd - len(v.shape)
+    return tr.node("bcast", shape, v.dtype, (v,), {"map": tuple(range(off, nd))}, v.label)
+
+
+def _op_linalg_reduce(self, op):
+    t = self.core.get(op.operands[0])
+    a = op.attributes
+    if op.regions and op.regions[0].ops:
+        region = op.regions[0]
+        body = [o for o in region.ops if o.op_type != "linalg.yield"]
+        names = [n for n, _ in region.args] or list(body[0].operands)
+        if len(body) != 1 or list(body[0].operands[:2]) not in (names[:2], names[:2][::-1]):
+            comb = ("region", region, names)
+        else:
+            comb = body[0].op_type
+            if list(body[0].operands[:2]) == names[:2][::-1]:
+                comb = ("swapped", comb)
+    else:
+        comb = a.get("combiner") or "arith.addf"
+    dims = a.get("dims")
+    if not _is_tile(t):
+        res = t
+    else:
+        dim = dims[0] if dims else None
+        if dim is None:
+            flat = self.node("reshape", (t.numel,), t.dtype, (t,), {}, t.label)
+            res = self.node("reduce", (), t.dtype, (flat,), {"dim": 0, "combiner": comb},
+                            t.label, pyscalar=True)
+        else:
+            shape = tuple(s for i, s in enumerate(t.shape) if i != dim)
+            res = self.node("reduce", shape, t.dtype, (t,), {"dim": dim, "combiner": comb},
+                            t.label, pyscalar=not shape)
+    outs = a.get("outs")
+    if outs and res is not None:
+        self.core.set(outs, res)
+    return res
+
+
+def _op_linalg_add(self, op):
+    x = self.core.get(op.operands[0])
+    y = self.core.get(op.operands[1])
+    return self.ew("add", [x, y], operator.add, x)
+
+
+def _op_linalg_fill(self, op):
+    s = self.core.get(op.operands[0])
+    o = self.core.get(op.operands[1])
+    if isinstance(s, Node):
+        return self.node("splat", o.shape, o.dtype, (self.node("ew", (), np.float64, (s,),
+                                                               {"op": "cast"}),), {}, o.label)
+    return self.const_tile(o.dtype.type(float(s)), o.shape, o.dtype, o.label)
+
+
+def _op_linalg_broadcast(self, op):
+    x = self.core.get(op.operands[0])
+    o = self.core.get(op.operands[1])
+    dims = sorted(op.attributes.get("dimensions", []))
+    keep = [d for d in range(len(o.shape)) if d not in dims]
+    return self.node("bcast", o.shape, x.dtype, (x,), {"map": tuple(keep)}, x.label)
+
+
+def _op_linalg_matmul(self, op):
+    x = self.core.get(op.operands[0])
+    y = self.core.get(op.operands[1])
+    if len(x.shape) != 2 or len(y.shape) != 2 or x.shape[1] != y.shape[0]:
+        raise ValueError(f"linalg.matmul shape mismatch {x.shape} @ {y.shape}")
+    rdt = np.matmul(x.proto(), y.proto()).dtype
+    mm = self.node("matmul", (x.shape[0], y.shape[1]), x.dtype, (x, y),
+                   {"acc_dtype": rdt}, x.label)
+    if len(op.operands) > 2:
+        acc = self.core.get(op.operands[2])
+        if _is_tile(acc):
+            r = self.ew("add", [acc, mm], operator.add, acc)
+            r.attrs["matmul_accumulate"] = True
+            return r
+    return mm
+
+
+def _op_linalg_batch_matmul(self, op):
+    x = self.core.get(op.operands[0])
+    y = self.core.get(op.operands[1])
+    rdt = np.matmul(x.proto(), y.proto()).dtype
+    shape = tuple(np.broadcast_shapes(x.shape[:-2], y.shape[:-2])) + (x.shape[-2], y.shape[-1])
+    mm = self.node("matmul", shape, rdt, (x, y), {"acc_dtype": rdt, "batched": True}, x.label)
+    if len(op.operands) > 2:
+        acc = self.core.get(op.operands[2])
+        if _is_tile(acc):
+            return self.ew("add", [acc, mm], operator.add, acc)
+    return mm
+
+
+def _op_linalg_transpose(self, op):
+    x = self.core.get(op.operands[0])
+    perm = tuple(op.attributes["permutation"])
+    return self.node("transpose", tuple(x.shape[i] for i in perm), x.dtype, (x,),
+                     {"perm": perm}, x.label)
+
+
+def _op_linalg_generic(self, op):
+    a = op.attributes
+    n_ins = a["n_ins"]
+    maps = a["indexing_maps"]
+    ins = [self.core.get(o) for o in op.operands[:n_ins]]
+    outs = self.core.get(op.operands[n_ins])
+    region = op.regions[0]
+    names = [n for n, _ in region.args] or list(region.ops[0].operands)
+    shape = outs.shape
+    self.core.push()
+    self.core.set("__linalg_shape__", shape)
+    for i, (v, m) in enumerate(zip(ins, maps[:n_ins])):
+        dims = tuple(e[1] for e in m.exprs if e[0] == "d")
+        if _is_tile(v):
+            if len(dims) != len(v.shape):
+                raise NotImplementedError("linalg.generic indexing map with non-dim results")
+            arg = self.node("bcast", shape, v.dtype, (v,), {"map": dims}, v.label)
+        else:
+            arg = v
+        if i < len(names):
+            self.core.set(names[i], arg)
+    if n_ins < len(names):
+        self.core.set(names[n_ins], outs)
+    r = self.run_ops(region.ops)
+    self.core.pop()
+    if isinstance(r, _Yield):
+        r = r.values[0] if len(r.values) == 1 else r.values[0]
+    if isinstance(r, Node):
+        if r.shape != shape:
+            r = _bcast_to(self, r, shape) if r.shape else self.node("splat", shape, r.dtype, (r,),
+                                                                     {}, r.label)
+        if r.dtype != outs.dtype:
+            r = self.node("ew", shape, outs.dtype, (r,), {"op": "cast"}, outs.label)
+        else:
+            r.label = outs.label
+        return r
+    with np.errstate(all="ignore"):
+        return self.const_tile(np.full((), r, dtype=outs.dtype)[()], shape, outs.dtype, outs.label)
+
+
+def _op_linalg_index(self, op):
+    d = op.attributes["dim"]
+    shape = self.core.get("__linalg_shape__")
+    rs = [1] * len(shape)
+    rs[d] = shape[d]
+    return self.node("iota", tuple(rs), np.int64, (), {"dim": d}, "index")
+
+
+def _op_scf_for(self, op):
+    lb, ub, st = (_need_int(self.core.get(o), "scf.for bound") for o in op.operands[:3])
+    names = op.attributes.get("iter_args", [])
+    cur = [self.core.get(o) for o in op.operands[3:]]
+    for n, v in zip(names, cur):
+        self.core.set(n, v)
+        if _is_tile(v):
+            self.core.track(n, v.nbytes)
+    body = op.regions[0]
+    iv = op.attributes["iter_var"]
+    for i in range(lb, ub, max(st, 1)):
+        self.core.push()
+        self.core.set(iv, i)
+        r = self.run_ops(body.ops)
+        ys = r.values if isinstance(r, _Yield) and names else None
+        self.core.pop()
+        if ys is not None:
+            for n, v in zip(names, ys):
+                self.core.untrack(n)
+                self.core.set(n, v)
+                if _is_tile(v):
+                    self.core.track(n, v.nbytes)
+            cur = list(ys)
+    if not cur:
+        return None
+    return cur[0] if len(cur) == 1 else tuple(cur)
+
+
+def _op_scf_if(self, op):
+    c = self.core.get(op.operands[0])
+    if isinstance(c, Node):
+        raise DataDependentError("scf.if on tile data")
+    region = op.regions[0] if c else (op.regions[1] if len(op.regions) > 1 else None)
+    if region is None or not region.ops:
+        return None
+    self.core.push()
+    r = self.run_ops(region.ops)
+    self.core.pop()
+    if isinstance(r, _Yield):
+        if not r.values:
+            return None
+        return r.values[0] if len(r.values) == 1 else tuple(r.values)
+    return r
+
+
+for _name, _fn in list(globals().items()):
+    if _name.startswith("_op_"):
+        setattr(Tracer, "op_" + _name[4:], _fn)
+Tracer.op_tensor_expand_shape = _op_reshape
+Tracer.op_tensor_collapse_shape = _op_reshape
+Tracer.op_tensor_reshape = _op_reshape
+Tracer.op_tensor_yield = _yield
+Tracer.op_linalg_yield = _yield
+Tracer.op_scf_yield = _yield
