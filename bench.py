@@ -233,6 +233,17 @@ def main():
         dist.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        # keep the GPU busy until the sampler is producing samples, so the
+        # clocks recorded are the clocks under this load
+        t_end = time.time() + 1.5
+        i = 0
+        while time.time() < t_end:
+            for _ in range(20):
+                exe.launch(sets[i % n_sets][0], stream, sets[i % n_sets][1])
+                i += 1
+            torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize(dev)
         ev0.record(stream)
         for i in range(args.steps):
@@ -248,6 +259,12 @@ def main():
             b.record(stream)
             evs.append((a, b))
         torch.cuda.synchronize(dev)
+        t_end = time.time() + 0.3
+        while time.time() < t_end:
+            for _ in range(20):
+                exe.launch(sets[i % n_sets][0], stream, sets[i % n_sets][1])
+                i += 1
+            torch.cuda.synchronize(dev)
     ms = ev0.elapsed_time(ev1)
     kern_ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
     if world > 1:

@@ -169,6 +169,7 @@ typedef struct {
   int64_t m, n, k;             /* full problem */
   int32_t add_zero;            /* epilogue adds +0.0 (normalises -0) as outs-init does */
   int32_t pad;
+  int32_t* status;             /* device status word (KTIR_STATUS_TIMEOUT) */
 } KtirGemmDesc;
 
 /* Causal flash attention over [bh, seq, d] f16 tensors laid out as
@@ -179,6 +180,7 @@ typedef struct {
   float scale;
   int32_t causal;
   int64_t row_stride;          /* elements between consecutive rows (= d for dense) */
+  int32_t* status;             /* device status word (KTIR_STATUS_TIMEOUT) */
 } KtirFmhaDesc;
 
 /* ----------------------------------------------------------------------- */

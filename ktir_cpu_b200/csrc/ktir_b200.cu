@@ -133,50 +133,40 @@ extern "C" int ktir_ew(const KtirEwProgram* prog, const KtirBuffers* bufs,
 //   h <= 4        : element k with k + h inside lane 0
 // so the fold below is the reference's fold, pair for pair.
 template <int VPL>
-__device__ __forceinline__ float tree_fold(float (&v)[VPL][8], int n, bool is_max, bool f16) {
+__device__ __forceinline__ float tree_fold(float (&v)[VPL][8], bool is_max, bool f16) {
   const unsigned full = 0xffffffffu;
-  // in-lane vector rounds
-  for (int h = n / 2; h >= 256; h >>= 1) {
-    const int hv = h / 256;
+  // in-lane vector rounds: h = 128*VPL ... 256, vector j pairs with j + h/256
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      if (j < hv) {
+  for (int hv = VPL / 2; hv >= 1; hv >>= 1) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          float a = v[j][k], c = v[j + hv < VPL ? j + hv : j][k];
-          float r = is_max ? fmaxf(a, c) : a + c;
-          v[j][k] = f16 ? __half2float(__float2half_rn(r)) : r;
-        }
+    for (int j = 0; j < hv; ++j) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float r = is_max ? fmaxf(v[j][k], v[j + hv][k]) : v[j][k] + v[j + hv][k];
+        v[j][k] = f16 ? __half2float(__float2half_rn(r)) : r;
       }
     }
   }
-  // cross-lane rounds, h = 128 .. 8 (only those below n)
-  const int top = (n / 2 < 128) ? n / 2 : 128;
-  for (int h = top; h >= 8; h >>= 1) {
-    const int dl = h / 8;
+  // cross-lane rounds h = 128 .. 8: lane l pairs with lane l + h/8
+#pragma unroll
+  for (int dl = 16; dl >= 1; dl >>= 1) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       float c = __shfl_down_sync(full, v[0][k], dl);
       float r = is_max ? fmaxf(v[0][k], c) : v[0][k] + c;
-      r = f16 ? __half2float(__float2half_rn(r)) : r;
-      if ((threadIdx.x & 31) < dl) v[0][k] = r;
+      v[0][k] = f16 ? __half2float(__float2half_rn(r)) : r;
     }
   }
-  // in-lane element rounds
-  float w[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) w[k] = v[0][k];
+  // in-lane element rounds h = 4, 2, 1 (lane 0 holds the result)
 #pragma unroll
   for (int h = 4; h >= 1; h >>= 1) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (k < h) {
-        float r = is_max ? fmaxf(w[k], w[k + h]) : w[k] + w[k + h];
-        w[k] = f16 ? __half2float(__float2half_rn(r)) : r;
-      }
+    for (int k = 0; k < h; ++k) {
+      float r = is_max ? fmaxf(v[0][k], v[0][k + h]) : v[0][k] + v[0][k + h];
+      v[0][k] = f16 ? __half2float(__float2half_rn(r)) : r;
     }
   }
-  return __shfl_sync(full, w[0], 0);
+  return __shfl_sync(full, v[0][0], 0);
 }
 
 template <int VPL>
@@ -222,7 +212,7 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
     for (int j = 0; j < VPL; ++j)
 #pragma unroll
       for (int k = 0; k < 8; ++k) t[j][k] = v[j][k];
-    const float mx = tree_fold<VPL>(t, d.cols, true, f16c);
+    const float mx = tree_fold<VPL>(t, true, f16c);
 #pragma unroll
     for (int j = 0; j < VPL; ++j)
 #pragma unroll
@@ -234,7 +224,7 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
         v[j][k] = x;
         t[j][k] = x;
       }
-    const float sum = tree_fold<VPL>(t, d.cols, false, f16c);
+    const float sum = tree_fold<VPL>(t, false, f16c);
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int64_t e = ob + 256 * j + 8 * lane;
@@ -258,7 +248,7 @@ extern "C" int ktir_softmax_rows(const KtirSoftmaxDesc* d, const KtirBuffers* bu
                                  const int64_t* unit_table, void* stream) {
   if (!d || !bufs) return set_err(KTIR_ERR_ARG, "ktir_softmax_rows: null descriptor");
   const int n = d->cols;
-  if (n < 256 || (n & (n - 1)) || n > 8192 || d->in.stride[1] != 1 || d->out.stride[1] != 1 ||
+  if (n < 256 || (n & (n - 1)) || n > 4096 || d->in.stride[1] != 1 || d->out.stride[1] != 1 ||
       d->in.dtype != KTIR_F16 || d->out.dtype != KTIR_F16)
     return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: needs f16 rows of 2^k >= 256 elements");
   if (((d->in.off | d->out.off | d->in.stride[0] | d->out.stride[0]) & 7) != 0)
@@ -273,7 +263,6 @@ extern "C" int ktir_softmax_rows(const KtirSoftmaxDesc* d, const KtirBuffers* bu
     case 4: k_softmax_rows<4><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
     case 8: k_softmax_rows<8><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
     case 16: k_softmax_rows<16><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
-    case 32: k_softmax_rows<32><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
     default: return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: row length");
   }
   return check_launch("ktir_softmax_rows");

@@ -107,6 +107,9 @@ class Executable:
         self.grid = grid
         self.lib = R.load_library()
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.dev_tensors = None
+        self.pinned = None
+        self.bufs = None
         self.arena = None
         if plan.arena_bytes:
             self.arena = torch.zeros(plan.arena_bytes + 256, dtype=torch.uint8, device=device)
@@ -259,20 +262,32 @@ class KTIRInterpreter:
         return entry
 
     def run_host(self, exe: Executable, order: List[int]) -> None:
-        """Upload every allocation, run the plan, read every allocation back."""
+        """Upload every allocation, run the plan, read back what the plan writes.
+
+        Device buffers and pinned staging buffers belong to the Executable and
+        are reused by every call with the same signature.
+        """
         torch = exe.torch
         hbm = self.memory.hbm
-        tensors = []
-        for addr in order:
+        if exe.dev_tensors is None:
+            exe.dev_tensors, exe.pinned = [], []
+            for addr in order:
+                nb = hbm.allocs[addr].nbytes
+                exe.dev_tensors.append(torch.empty(nb + 16, dtype=torch.uint8, device=exe.device))
+                exe.pinned.append(torch.empty(nb, dtype=torch.uint8, pin_memory=True))
+            exe.bufs = exe.buffers(exe.dev_tensors)
+        stream = torch.cuda.current_stream(exe.device)
+        for addr, t, pin in zip(order, exe.dev_tensors, exe.pinned):
             arr = hbm.allocs[addr]
-            t = torch.empty(arr.nbytes + 16, dtype=torch.uint8, device=exe.device)
-            t[:arr.nbytes].copy_(torch.from_numpy(arr.view(np.uint8)), non_blocking=False)
-            tensors.append(t)
+            pin.numpy()[:] = arr.view(np.uint8)
+            t[:arr.nbytes].copy_(pin, non_blocking=True)
         exe.status.zero_()
-        exe.launch(tensors)
-        torch.cuda.synchronize(exe.device)
+        exe.launch(exe.dev_tensors, stream, exe.bufs)
+        written = exe.plan.info.get("written")
+        back = [i for i in range(len(order)) if written is None or i in written]
+        for i in back:
+            exe.pinned[i].copy_(exe.dev_tensors[i][:exe.pinned[i].numel()], non_blocking=True)
+        stream.synchronize()
         exe.check_status()
-        for addr, t in zip(order, tensors):
-            arr = hbm.allocs[addr]
-            host = t[:arr.nbytes].cpu().numpy()
-            arr.view(np.uint8)[:] = host
+        for i in back:
+            hbm.allocs[order[i]].view(np.uint8)[:] = exe.pinned[i].numpy()

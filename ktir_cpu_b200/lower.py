@@ -487,9 +487,22 @@ class Lowerer:
             plan = matcher(stores)
             if plan is not None:
                 plan.device_arrays = self.dev.keep
-                return plan
+                return self.finish(plan)
         plan = GenericExecutor(self).build()
         plan.device_arrays = self.dev.keep
+        return self.finish(plan)
+
+    def finish(self, plan: Plan) -> Plan:
+        """Record which call buffers the plan may write (others need no download)."""
+        written = set()
+        for s in self.trace.stores:
+            t = s.target
+            if isinstance(t, IndirectTarget):
+                b = self.trace.space.find(t.iat.parent.byte_address)
+                written.add(b.index)
+            else:
+                written.add(t.buf.index)
+        plan.info["written"] = written
         return plan
 
     # -- gather -> f -> scatter ----------------------------------------------------
@@ -607,7 +620,7 @@ class Lowerer:
                u[1].buf is not t0.buf or u[0].attrs["strides"][0] != ld0.attrs["strides"][0] or
                u[1].strides[0] != t0.strides[0] for u in units):
             return None
-        if cols < 256 or cols & (cols - 1) or cols > 8192:
+        if cols < 256 or cols & (cols - 1) or cols > 4096:
             return None
         items = [([_load_interval(ld)], [_target_interval(t)]) for ld, t in units]
         if not units_independent(items):

@@ -10,3 +10,7 @@ from .ir import IRFunction
 def attention_rewrites(func: IRFunction) -> Dict[int, Any]:
     """Map id(scf.for op) -> tracer handler for recognised attention loops."""
     return {}
+
+
+def match_attention_plan(low, stores):
+    return None

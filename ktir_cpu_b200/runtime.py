@@ -103,13 +103,13 @@ class KtirGemmDesc(C.Structure):
     _fields_ = [("a", C.c_void_p), ("b", C.c_void_p), ("c", C.c_void_p),
                 ("lda", C.c_int64), ("ldb", C.c_int64), ("ldc", C.c_int64),
                 ("m", C.c_int64), ("n", C.c_int64), ("k", C.c_int64),
-                ("add_zero", C.c_int32), ("pad", C.c_int32)]
+                ("add_zero", C.c_int32), ("pad", C.c_int32), ("status", C.c_void_p)]
 
 
 class KtirFmhaDesc(C.Structure):
     _fields_ = [("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("o", C.c_void_p),
                 ("bh", C.c_int64), ("seq", C.c_int64), ("d", C.c_int64), ("scale", C.c_float),
-                ("causal", C.c_int32), ("row_stride", C.c_int64)]
+                ("causal", C.c_int32), ("row_stride", C.c_int64), ("status", C.c_void_p)]
 
 
 EXPORTS = ["ktir_version", "ktir_last_error", "ktir_device_count", "ktir_ew",
