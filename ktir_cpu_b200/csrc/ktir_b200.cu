@@ -213,25 +213,37 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
 #pragma unroll
       for (int k = 0; k < 8; ++k) t[j][k] = v[j][k];
     const float mx = tree_fold<VPL>(t, true, f16c);
+    // exp(x - max): the f32 program folds log2(e) into one FMA feeding ex2;
+    // the f16 program rounds like NumPy's float16 loops (sub, round, exp, round)
+    const float l2e = 1.4426950408889634f;
+    const float mx2 = mx * l2e;
 #pragma unroll
     for (int j = 0; j < VPL; ++j)
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        float x = v[j][k] - mx;
-        if (f16c) x = __half2float(__float2half_rn(x));
-        x = expf(x);
-        if (f16c) x = __half2float(__float2half_rn(x));
+        float x;
+        if (f16c) {
+          x = __half2float(__float2half_rn(v[j][k] - mx));
+          x = __half2float(__float2half_rn(expf(x)));
+        } else {
+          x = exp2f(fmaf(v[j][k], l2e, -mx2));
+        }
         v[j][k] = x;
         t[j][k] = x;
       }
     const float sum = tree_fold<VPL>(t, false, f16c);
+    const float rs = 1.0f / sum;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int64_t e = ob + 256 * j + 8 * lane;
       __half2 o2[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        o2[k] = __floats2half2_rn(v[j][2 * k] / sum, v[j][2 * k + 1] / sum);
+      for (int k = 0; k < 4; ++k) {
+        if (f16c)
+          o2[k] = __floats2half2_rn(v[j][2 * k] / sum, v[j][2 * k + 1] / sum);
+        else
+          o2[k] = __floats2half2_rn(v[j][2 * k] * rs, v[j][2 * k + 1] * rs);
+      }
       if (e >= 0 && e + 8 <= b.numel[d.out.slot]) {
         *reinterpret_cast<uint4*>(out + e) = *reinterpret_cast<uint4*>(o2);
       } else {

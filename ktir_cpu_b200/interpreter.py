@@ -251,10 +251,15 @@ class KTIRInterpreter:
             space.add_fixed(names.get(addr, f"hbm@0x{addr:x}"), addr, arr.nbytes, arr.dtype,
                             arr.shape)
         from .rewrite import attention_rewrites
-        tracer = Tracer(func, space, scalars, ptrs, rewrites=attention_rewrites(func))
-        trace = tracer.run()
         slots = {b.index: b.index for b in space.buffers}
+        rewrites = attention_rewrites(func)
+        trace = Tracer(func, space, scalars, ptrs, rewrites=rewrites).run()
         plan = Lowerer(trace, device, slots).lower()
+        if rewrites and plan.kind != "attention":
+            # the rewritten loops did not form a whole attention problem the
+            # tensor-core kernel covers: trace the loops op by op instead
+            trace = Tracer(func, space, scalars, ptrs).run()
+            plan = Lowerer(trace, device, slots).lower()
         exe = Executable(plan, space, device, func.grid)
         entry = (exe, [a for a, _ in allocs])
         self._cache[key] = entry

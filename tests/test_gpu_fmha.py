@@ -1,0 +1,56 @@
+"""tcgen05 flash attention through the C ABI against a PyTorch float32 reference."""
+
+import ctypes as C
+import math
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+# max relative error tolerated on f16 outputs (P is rounded to f16 for the PV product)
+TOL = 1e-2
+
+
+def _fmha(q, k, v, o, bh, seq, scale, causal):
+    import torch
+    from ktir_cpu_b200 import runtime as R
+    lib = R.load_library()
+    status = torch.zeros(1, dtype=torch.int32, device=q.device)
+    d = R.KtirFmhaDesc()
+    d.q, d.k, d.v, d.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+    d.bh, d.seq, d.d = bh, seq, 128
+    d.scale = scale
+    d.causal = 1 if causal else 0
+    d.row_stride = 128
+    d.status = status.data_ptr()
+    R.check(lib.ktir_fmha_f16(C.byref(d), C.c_void_p(torch.cuda.current_stream().cuda_stream)),
+            "ktir_fmha_f16")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+
+
+def _reference(q, k, v, bh, seq, scale, causal):
+    import torch
+    qf = q.float().view(bh, seq, 128)
+    kf = k.float().view(bh, seq, 128)
+    vf = v.float().view(bh, seq, 128)
+    s = qf @ kf.transpose(1, 2) * scale
+    if causal:
+        mask = torch.triu(torch.ones(seq, seq, dtype=torch.bool, device=q.device), diagonal=1)
+        s = s.masked_fill(mask, float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return (p @ vf).view(bh * seq, 128)
+
+
+@pytest.mark.parametrize("bh,seq,causal", [(1, 128, True), (2, 256, True), (3, 384, False),
+                                           (4, 1024, True)])
+def test_fmha_matches_fp32(bh, seq, causal):
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(bh * 1000 + seq)
+    q, k, v = (torch.randn(bh * seq, 128, generator=g).half().cuda() for _ in range(3))
+    o = torch.full((bh * seq, 128), float("nan"), dtype=torch.float16, device="cuda")
+    scale = float(1.0 / math.sqrt(128))
+    _fmha(q, k, v, o, bh, seq, scale, causal)
+    ref = _reference(q, k, v, bh, seq, scale, causal)
+    err = ((o.float() - ref).abs() / ref.abs().clamp_min(TOL)).max().item()
+    assert err <= TOL, err

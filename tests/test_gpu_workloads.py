@@ -64,3 +64,17 @@ def test_gather_add_negative_index_raises():
     dev.load(W.source("gather_add", **p))
     with pytest.raises(IndexError):
         dev.execute_function("gather_add", **kw)
+
+
+def test_attention_uses_tensor_core_plan():
+    p = dict(batch=2, heads=2, seq=512, dim=128, grid=4)
+    kw, got, want, dev = _run_both("attention", **p)
+    assert dev.last_executable.plan.kind == "attention"
+    assert_matches("o", got["o_ptr"], want["o_ptr"], 1e-2)
+
+
+def test_gemm_uses_tensor_core_plan():
+    p = dict(m=512, n=512, k=512, grid=(4, 2))
+    kw, got, want, dev = _run_both("gemm", **p)
+    assert dev.last_executable.plan.kind == "gemm"
+    assert_matches("c", got["c_ptr"], want["c_ptr"], 1e-2)
