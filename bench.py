@@ -182,6 +182,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--profile", action="store_true",
+                    help="only warmup + steps plain launches on two buffer sets (for ncu)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -215,7 +217,7 @@ def main():
     set_bytes = sum(nbytes)
     L2 = 126 * 1024 * 1024
     n_sets = max(2, int(np.ceil(2 * L2 / max(set_bytes, 1))))
-    n_sets = min(n_sets, 64)
+    n_sets = min(n_sets, 64) if not args.profile else 2
     sets = []
     host = [interp.memory.hbm.allocs[a] for a in sorted(interp.memory.hbm.allocs)]
     for _ in range(n_sets):
@@ -229,6 +231,14 @@ def main():
     for i in range(args.warmup):
         exe.launch(sets[i % n_sets][0], stream, sets[i % n_sets][1])
     torch.cuda.synchronize(dev)
+    if args.profile:
+        for i in range(args.steps):
+            exe.launch(sets[i % n_sets][0], stream, sets[i % n_sets][1])
+        torch.cuda.synchronize(dev)
+        if rank == 0:
+            print(json.dumps({"profile_run": args.config, "plan": plan.kind,
+                              "launches": (args.warmup + args.steps) * plan.kernel_launches}))
+        return
     if world > 1:
         dist.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
