@@ -222,6 +222,13 @@ int ktir_indirect(const KtirIndirectDesc* desc, const KtirBuffers* bufs,
                   const int64_t* unit_table, const int64_t* direct, const int64_t* idx_offs,
                   int32_t* status, void* stream);
 
+/* Failure-detection self test: a single thread waits, with at most
+ * `spin_limit` polls (1 .. 2^20), on a barrier nothing arrives at, then sets
+ * KTIR_STATUS_TIMEOUT in *status and returns — the bounded wait every
+ * tensor-core kernel uses, exercised without faulting or hanging a GPU.
+ * (No counterpart in the reference, whose cores are host generators.) */
+int ktir_wait_selftest(int32_t* status, uint32_t spin_limit, void* stream);
+
 /* tcgen05 GEMM (replaces the linalg.matmul K loop, ktir_cpu/dialects/linalg_ops.py:273-297
  * with ops/arith_ops.py:403-419, for whole-matrix tilings). */
 int ktir_gemm_f16(const KtirGemmDesc* desc, void* stream);

@@ -132,8 +132,9 @@ extern "C" int ktir_ew(const KtirEwProgram* prog, const KtirBuffers* bufs,
 //   8 <= h <= 128 : lane l with lane l + h/8 (same j = 0, same k)
 //   h <= 4        : element k with k + h inside lane 0
 // so the fold below is the reference's fold, pair for pair.
-template <int VPL>
-__device__ __forceinline__ float tree_fold(float (&v)[VPL][8], bool is_max, bool f16) {
+template <int VPL, bool F16>
+__device__ __forceinline__ float tree_fold(float (&v)[VPL][8], bool is_max) {
+  constexpr bool f16 = F16;
   const unsigned full = 0xffffffffu;
   // in-lane vector rounds: h = 128*VPL ... 256, vector j pairs with j + h/256
 #pragma unroll
@@ -169,7 +170,13 @@ __device__ __forceinline__ float tree_fold(float (&v)[VPL][8], bool is_max, bool
   return __shfl_sync(full, v[0][0], 0);
 }
 
-template <int VPL>
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int VPL, bool F16>
 __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ KtirSoftmaxDesc d,
                                                       const __grid_constant__ KtirBuffers b,
                                                       const int64_t* __restrict__ ut) {
@@ -177,7 +184,7 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t total_rows = (int64_t)d.n_units * d.rows;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  const bool f16c = d.compute_f16 != 0;
+  constexpr bool f16c = F16;
   const __half* in = (const __half*)b.base[d.in.slot];
   __half* out = (__half*)b.base[d.out.slot];
   for (int64_t row = warp; row < total_rows; row += nwarps) {
@@ -212,7 +219,7 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
     for (int j = 0; j < VPL; ++j)
 #pragma unroll
       for (int k = 0; k < 8; ++k) t[j][k] = v[j][k];
-    const float mx = tree_fold<VPL>(t, true, f16c);
+    const float mx = tree_fold<VPL, F16>(t, true);
     // exp(x - max): the f32 program folds log2(e) into one FMA feeding ex2;
     // the f16 program rounds like NumPy's float16 loops (sub, round, exp, round)
     const float l2e = 1.4426950408889634f;
@@ -226,12 +233,12 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
           x = __half2float(__float2half_rn(v[j][k] - mx));
           x = __half2float(__float2half_rn(expf(x)));
         } else {
-          x = exp2f(fmaf(v[j][k], l2e, -mx2));
+          x = fast_exp2(fmaf(v[j][k], l2e, -mx2));
         }
         v[j][k] = x;
         t[j][k] = x;
       }
-    const float sum = tree_fold<VPL>(t, false, f16c);
+    const float sum = tree_fold<VPL, F16>(t, false);
     const float rs = 1.0f / sum;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
@@ -269,14 +276,22 @@ extern "C" int ktir_softmax_rows(const KtirSoftmaxDesc* d, const KtirBuffers* bu
   const int threads = 256;
   const int blocks = grid_x(rows * 32, threads, 1 << 30);
   cudaStream_t s = (cudaStream_t)stream;
+#define KTIR_SOFTMAX_CASE(V)                                                         \
+  case V:                                                                            \
+    if (d->compute_f16)                                                              \
+      k_softmax_rows<V, true><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table);     \
+    else                                                                             \
+      k_softmax_rows<V, false><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table);    \
+    break;
   switch (n / 256) {
-    case 1: k_softmax_rows<1><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
-    case 2: k_softmax_rows<2><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
-    case 4: k_softmax_rows<4><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
-    case 8: k_softmax_rows<8><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
-    case 16: k_softmax_rows<16><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table); break;
+    KTIR_SOFTMAX_CASE(1)
+    KTIR_SOFTMAX_CASE(2)
+    KTIR_SOFTMAX_CASE(4)
+    KTIR_SOFTMAX_CASE(8)
+    KTIR_SOFTMAX_CASE(16)
     default: return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: row length");
   }
+#undef KTIR_SOFTMAX_CASE
   return check_launch("ktir_softmax_rows");
 }
 

@@ -114,7 +114,8 @@ class KtirFmhaDesc(C.Structure):
 
 EXPORTS = ["ktir_version", "ktir_last_error", "ktir_device_count", "ktir_ew",
            "ktir_softmax_rows", "ktir_gather_rmw", "ktir_reduce", "ktir_matmul",
-           "ktir_offsets", "ktir_indirect", "ktir_gemm_f16", "ktir_fmha_f16"]
+           "ktir_offsets", "ktir_indirect", "ktir_gemm_f16", "ktir_fmha_f16",
+           "ktir_wait_selftest"]
 
 _LIB: Optional[C.CDLL] = None
 
@@ -151,6 +152,7 @@ def load_library(build_if_missing: bool = False) -> C.CDLL:
                                   vp, vp, vp]
     lib.ktir_gemm_f16.argtypes = [C.POINTER(KtirGemmDesc), vp]
     lib.ktir_fmha_f16.argtypes = [C.POINTER(KtirFmhaDesc), vp]
+    lib.ktir_wait_selftest.argtypes = [vp, C.c_uint32, vp]
     for name in EXPORTS:
         getattr(lib, name).restype = C.c_int if name != "ktir_last_error" else C.c_char_p
     _LIB = lib

@@ -41,6 +41,7 @@ def assert_matches(name, got, want, tol):
                                                   np.isnan(want.astype(np.float64)))))
             raise AssertionError(f"{name}: not bit-exact at {len(bad)} positions, first {bad[:3].tolist()}")
     else:
-        # max relative error with near-zero outputs judged against an absolute floor
-        err = max_rel_err(got, want, floor=max(tol, 1e-3))
+        # max relative error; outputs of magnitude below 1 are judged on their
+        # absolute error (the reference's own numeric tests use rtol = atol = 1e-2)
+        err = max_rel_err(got, want, floor=1.0)
         assert err <= tol, f"{name}: max rel err {err:.3e} > {tol}"
