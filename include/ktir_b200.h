@@ -222,6 +222,20 @@ int ktir_indirect(const KtirIndirectDesc* desc, const KtirBuffers* bufs,
                   const int64_t* unit_table, const int64_t* direct, const int64_t* idx_offs,
                   int32_t* status, void* stream);
 
+/* Allocation-free ktir_gather_rmw for callers that cannot allocate device
+ * memory (no counterpart in the reference, which has no device memory).
+ * The per-row count scratch is a file-scope __device__ array of
+ * KTIR_STATIC_RMW_MAX_ROWS int32 (4 MiB) that every GPU loading this library
+ * holds until the process exits; tables with more rows are rejected with
+ * KTIR_ERR_UNSUPPORTED.  The first call on a device looks up the array's
+ * device address (make that first call before any stream capture); every
+ * call clears the first n_rows counts on `stream`.  All calls share the one
+ * array, so calls that overlap on the GPU (other streams, other threads)
+ * race and give wrong results.  Allocates nothing: no cudaMalloc/cudaFree. */
+#define KTIR_STATIC_RMW_MAX_ROWS (1 << 20)
+int ktir_gather_rmw_static(const KtirGatherRmwDesc* desc, const KtirBuffers* bufs,
+                           int64_t n_rows, int32_t* status, void* stream);
+
 /* Failure-detection self test: a single thread waits, with at most
  * `spin_limit` polls (1 .. 2^20), on a barrier nothing arrives at, then sets
  * KTIR_STATUS_TIMEOUT in *status and returns — the bounded wait every
