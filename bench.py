@@ -276,7 +276,11 @@ def main():
                 i += 1
             torch.cuda.synchronize(dev)
     ms = ev0.elapsed_time(ev1)
-    kern_ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    # average duration of the plan's kernels per step, from the events over
+    # the timed region (one-kernel plans: the kernel itself); per-launch event
+    # pairs are also reported but include the events' own overhead
+    kern_ms = ms / args.steps
+    launch_ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
     if world > 1:
         t = torch.tensor([ms, kern_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -320,7 +324,8 @@ def main():
             "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": src_peak, "kernel": DOMINANT[args.config],
-                         "kernel_ms": kern_ms},
+                         "kernel_ms": kern_ms, "isolated_launch_ms": launch_ms,
+                         "plan_kernels": plan.kernel_launches},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": in_bytes,
                     "d2h_bytes_per_step": in_bytes},
             "gpu_launches": args.steps * plan.kernel_launches,

@@ -176,6 +176,26 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+template <int VPL>
+__device__ __forceinline__ void load_row(const __half* in, int64_t numel, int64_t ib, int lane,
+                                         uint4 (&raw)[VPL]) {
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int64_t e = ib + 256 * j + 8 * lane;
+    if (e >= 0 && e + 8 <= numel) {
+      raw[j] = __ldg(reinterpret_cast<const uint4*>(in + e));
+    } else {
+      __half h[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        h[k] = (e + k >= 0 && e + k < numel) ? in[e + k] : __float2half(0.f);
+      raw[j] = *reinterpret_cast<const uint4*>(h);
+    }
+  }
+}
+
+// One warp per row; a warp walks rows `nwarps` apart and prefetches the next
+// row's vectors before reducing the current one, so loads overlap the math.
 template <int VPL, bool F16>
 __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ KtirSoftmaxDesc d,
                                                       const __grid_constant__ KtirBuffers b,
@@ -187,31 +207,33 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
   constexpr bool f16c = F16;
   const __half* in = (const __half*)b.base[d.in.slot];
   __half* out = (__half*)b.base[d.out.slot];
+  const int64_t in_numel = b.numel[d.in.slot];
+  auto in_base = [&](int64_t row) {
+    const int unit = (int)(row / d.rows);
+    const int r = (int)(row - (int64_t)unit * d.rows);
+    return d.in.off + (d.in.unit_col >= 0 ? ut[(int64_t)unit * d.unit_cols + d.in.unit_col] : 0) +
+           (int64_t)r * d.in.stride[0];
+  };
+  uint4 cur[VPL];
+  if (warp < total_rows) load_row<VPL>(in, in_numel, in_base(warp), lane, cur);
   for (int64_t row = warp; row < total_rows; row += nwarps) {
-    const int64_t unit = row / d.rows;
-    const int64_t r = row - unit * d.rows;
-    const int64_t ib = d.in.off + (d.in.unit_col >= 0 ? ut[unit * d.unit_cols + d.in.unit_col] : 0)
-                       + r * d.in.stride[0];
+    uint4 nxt[VPL];
+    const int64_t nrow = row + nwarps;
+    if (nrow < total_rows) load_row<VPL>(in, in_numel, in_base(nrow), lane, nxt);
+    const int unit = (int)(row / d.rows);
+    const int r = (int)(row - (int64_t)unit * d.rows);
     const int64_t ob = d.out.off +
-                       (d.out.unit_col >= 0 ? ut[unit * d.unit_cols + d.out.unit_col] : 0) +
-                       r * d.out.stride[0];
+                       (d.out.unit_col >= 0 ? ut[(int64_t)unit * d.unit_cols + d.out.unit_col] : 0) +
+                       (int64_t)r * d.out.stride[0];
     float v[VPL][8];
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
-      const int64_t e = ib + 256 * j + 8 * lane;
-      if (e >= 0 && e + 8 <= b.numel[d.in.slot]) {
-        uint4 raw = __ldg(reinterpret_cast<const uint4*>(in + e));
-        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+      const __half2* h2 = reinterpret_cast<const __half2*>(&cur[j]);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          float2 f = __half22float2(h2[k]);
-          v[j][2 * k] = f.x;
-          v[j][2 * k + 1] = f.y;
-        }
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          v[j][k] = (e + k >= 0 && e + k < b.numel[d.in.slot]) ? __half2float(in[e + k]) : 0.f;
+      for (int k = 0; k < 4; ++k) {
+        float2 f = __half22float2(h2[k]);
+        v[j][2 * k] = f.x;
+        v[j][2 * k + 1] = f.y;
       }
     }
     float t[VPL][8];
@@ -260,6 +282,8 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
           if (e + k >= 0 && e + k < b.numel[d.out.slot]) out[e + k] = oh[k];
       }
     }
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) cur[j] = nxt[j];
   }
 }
 
@@ -274,7 +298,9 @@ extern "C" int ktir_softmax_rows(const KtirSoftmaxDesc* d, const KtirBuffers* bu
     return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: rows must be 16-byte aligned");
   const int64_t rows = (int64_t)d->n_units * d->rows;
   const int threads = 256;
-  const int blocks = grid_x(rows * 32, threads, 1 << 30);
+  // rows per warp (descriptor's spare field, 0 = default 2)
+  const int rpw = d->pad > 0 ? d->pad : 2;
+  const int blocks = grid_x((rows + rpw - 1) / rpw * 32, threads, 1 << 30);
   cudaStream_t s = (cudaStream_t)stream;
 #define KTIR_SOFTMAX_CASE(V)                                                         \
   case V:                                                                            \
@@ -340,10 +366,11 @@ __global__ void __launch_bounds__(512) k_rmw_count(const __grid_constant__ KtirG
   }
 }
 
-// Apply f once to a register holding one element; fast path for y = x op imm.
-__device__ __forceinline__ float apply_f(const KtirEwProgram& f, float x, int simple_op,
-                                         float simple_imm, int out_dt) {
-  if (simple_op) return round_to(binf(simple_op, x, simple_imm), out_dt);
+// Apply f once to one element: SOP != 0 is the common y = x op imm with an f16
+// result (op fixed at compile time); SOP == 0 runs the bytecode.
+template <int SOP>
+__device__ __forceinline__ float apply_f(const KtirEwProgram& f, float x, float imm, int out_dt) {
+  if (SOP != 0) return __half2float(__float2half_rn(binf(SOP, x, imm)));
   Reg r[KTIR_NREG];
   Reg res;
   res.f = x;
@@ -352,7 +379,7 @@ __device__ __forceinline__ float apply_f(const KtirEwProgram& f, float x, int si
     if (in.op == OP_LD) {
       r[in.dst].f = x;
     } else if (in.op == OP_ST) {
-      res = convert(r[in.a], in.dt, f.view[1].dtype);
+      res = convert(r[in.a], in.dt, out_dt);
     } else {
       exec_arith(in, r);
     }
@@ -362,22 +389,28 @@ __device__ __forceinline__ float apply_f(const KtirEwProgram& f, float x, int si
 
 // Phase 2: the first position to claim a row's count applies f count times.
 // A 16-lane group owns one index position; rows move in 16-byte vectors.
+template <int SOP>
 __global__ void __launch_bounds__(256) k_rmw_apply(const __grid_constant__ KtirGatherRmwDesc d,
                                                    const __grid_constant__ KtirBuffers b,
                                                    int* __restrict__ counts, int64_t n_rows,
-                                                   int simple_op, float simple_imm) {
+                                                   float simple_imm) {
   const int sub = threadIdx.x & 15;
-  const int64_t group = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
-  const int64_t ngroups = ((int64_t)gridDim.x * blockDim.x) >> 4;
-  const int64_t total = (int64_t)d.n_units * d.unit_len;
+  const int group = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 4);
+  const int ngroups = (int)((gridDim.x * blockDim.x) >> 4);
+  const int total = d.n_units * d.unit_len;
+  const bool dense_units = d.idx_unit_stride == d.unit_len;
   __half* table = (__half*)b.base[d.table_slot];
   const int64_t tnumel = b.numel[d.table_slot];
   const int out_dt = d.f.view[1].dtype;
-  for (int64_t g = group; g < total; g += ngroups) {
-    const int64_t unit = g / d.unit_len;
-    const int64_t i = g - unit * d.unit_len;
-    const int64_t row = read_index(b, d.idx_slot, d.idx_dtype,
-                                   d.idx_off + unit * d.idx_unit_stride + i);
+  for (int g = group; g < total; g += ngroups) {
+    int64_t pos;
+    if (dense_units) {
+      pos = d.idx_off + g;
+    } else {
+      const int unit = g / d.unit_len;
+      pos = d.idx_off + (int64_t)unit * d.idx_unit_stride + (g - unit * d.unit_len);
+    }
+    const int64_t row = read_index(b, d.idx_slot, d.idx_dtype, pos);
     int m = 0;
     if (sub == 0 && row >= 0 && row < n_rows) m = atomicExch(&counts[row], 0);
     m = __shfl_sync(0xffffffffu, m, (threadIdx.x & 31) & ~15);
@@ -400,7 +433,7 @@ __global__ void __launch_bounds__(256) k_rmw_apply(const __grid_constant__ KtirG
       }
       for (int rep = 0; rep < m; ++rep) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) x[k] = apply_f(d.f, x[k], simple_op, simple_imm, out_dt);
+        for (int k = 0; k < 8; ++k) x[k] = apply_f<SOP>(d.f, x[k], simple_imm, out_dt);
       }
       if (vec) {
         __half h[8];
@@ -421,6 +454,8 @@ extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* d, const KtirBuffers* bu
   if (!d || !bufs || !counts || !status) return set_err(KTIR_ERR_ARG, "ktir_gather_rmw: null argument");
   if (d->unit_len <= 0 || d->unit_len > 8192)
     return set_err(KTIR_ERR_UNSUPPORTED, "ktir_gather_rmw: unit length must be in [1, 8192]");
+  if ((int64_t)d->n_units * d->unit_len >= (1ll << 31))
+    return set_err(KTIR_ERR_UNSUPPORTED, "ktir_gather_rmw: more than 2^31 index positions");
   int cap = 1;
   while (cap < 2 * d->unit_len) cap <<= 1;
   const size_t smem = (size_t)cap * sizeof(long long);
@@ -438,7 +473,8 @@ extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* d, const KtirBuffers* bu
   float simple_imm = 0.f;
   const KtirEwProgram& f = d->f;
   if (f.n_instr == 4 && f.code[0].op == OP_LD && f.code[1].op == OP_IMM &&
-      f.code[2].op >= OP_FADD && f.code[2].op <= OP_FMINIMUM && f.code[3].op == OP_ST &&
+      (f.code[2].op == OP_FADD || f.code[2].op == OP_FSUB || f.code[2].op == OP_FMUL) &&
+      f.code[3].op == OP_ST && f.view[1].dtype == KTIR_F16 &&
       f.code[2].a == f.code[0].dst && f.code[2].b == f.code[1].dst && f.code[3].a == f.code[2].dst &&
       f.code[2].dt == f.view[1].dtype && f.code[1].dt == f.code[2].dt) {
     double dv;
@@ -448,7 +484,12 @@ extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* d, const KtirBuffers* bu
   }
   const int64_t groups = (int64_t)d->n_units * d->unit_len;
   const int blocks = grid_x(groups * 16, 256, 148 * 64);
-  k_rmw_apply<<<blocks, 256, 0, s>>>(*d, *bufs, counts, n_rows, simple_op, simple_imm);
+  switch (simple_op) {
+    case OP_FADD: k_rmw_apply<OP_FADD><<<blocks, 256, 0, s>>>(*d, *bufs, counts, n_rows, simple_imm); break;
+    case OP_FSUB: k_rmw_apply<OP_FSUB><<<blocks, 256, 0, s>>>(*d, *bufs, counts, n_rows, simple_imm); break;
+    case OP_FMUL: k_rmw_apply<OP_FMUL><<<blocks, 256, 0, s>>>(*d, *bufs, counts, n_rows, simple_imm); break;
+    default: k_rmw_apply<0><<<blocks, 256, 0, s>>>(*d, *bufs, counts, n_rows, 0.f); break;
+  }
   return check_launch("ktir_gather_rmw(apply)");
 }
 

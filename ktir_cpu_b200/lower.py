@@ -28,6 +28,7 @@ from __future__ import annotations
 
 import ctypes as C
 import operator
+import os
 from dataclasses import dataclass, field
 from typing import Any, Callable, Dict, List, Optional, Sequence, Tuple
 
@@ -631,6 +632,7 @@ class Lowerer:
         d = R.KtirSoftmaxDesc()
         d.rows, d.cols, d.n_units, d.unit_cols = rows, cols, len(units), 2
         d.compute_f16 = 1 if compute_f16 else 0
+        d.pad = int(os.environ.get("KTIR_SOFTMAX_ROWS_PER_WARP", "0"))
         d.in_ = mkview(self.slots[ld0.attrs["buf"].index], np.float16, 0,
                        (ld0.attrs["strides"][0], 1), unit_col=0)
         d.out = mkview(self.slots[t0.buf.index], np.float16, 0, (t0.strides[0], 1), unit_col=1)
