@@ -182,6 +182,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--shard", action="store_true",
+                    help="split one execution's core grid across the ranks (strong scaling)")
     ap.add_argument("--profile", action="store_true",
                     help="only warmup + steps plain launches on two buffer sets (for ncu)")
     args = ap.parse_args()
@@ -204,8 +206,9 @@ def main():
 
     src = W.source(args.config)
     fname = W.FUNC[args.config]
-    kw = W.inputs(args.config, seed=rank)
-    interp = KTIRInterpreter(device=dev)
+    kw = W.inputs(args.config, seed=0 if args.shard else rank)
+    shard = (rank, world, None) if (args.shard and world > 1) else None
+    interp = KTIRInterpreter(device=dev, shard=shard)
     interp.load(src)
     # first call traces + lowers (cached), and checks the path runs
     interp.execute_function(fname, **{k: v.copy() for k, v in kw.items()})
@@ -285,7 +288,8 @@ def main():
         t = torch.tensor([ms, kern_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, kern_ms = float(t[0]), float(t[1])
-    value = world * args.steps / (ms / 1000.0)
+    per_step_execs = 1 if shard else world
+    value = per_step_execs * args.steps / (ms / 1000.0)
 
     # --- end to end through the public API ------------------------------------------
     e2e_steps = args.e2e_steps or max(3, min(args.steps, 20))
@@ -302,11 +306,13 @@ def main():
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t[0])
-    e2e = world * e2e_steps / e2e_s
+    e2e = per_step_execs * e2e_steps / e2e_s
 
     if rank == 0:
         hbm_peak, tc_peak, src_peak = peaks()
         bound, work = WORK[args.config]
+        if shard:
+            work = work / world   # each rank's share of one execution
         if bound == "hbm":
             achieved = work / (kern_ms / 1000.0) / 1e9
             peak, unit = hbm_peak, "GB/s"
@@ -317,10 +323,12 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "scaling": "strong" if shard else "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic",
             "config": dict(config_dict(args), l2=f"{n_sets} rotating buffer sets of "
                            f"{set_bytes / 2**20:.1f} MiB (> 126 MB L2)", plan=plan.kind,
-                           parallelism=f"replicas x{world}"),
+                           parallelism=(f"core grid split over {world} GPUs" if shard
+                                        else f"replicas x{world}")),
             "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": src_peak, "kernel": DOMINANT[args.config],

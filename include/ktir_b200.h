@@ -113,6 +113,9 @@ typedef struct {
   int64_t row_stride;
   int64_t idx_off;     /* element offset of the first index of unit 0 */
   int64_t idx_unit_stride; /* index offset step between consecutive units */
+  int64_t row_lo, row_hi;  /* apply only to table rows in [row_lo, row_hi); row_hi 0 = all */
+  int32_t phases;      /* bit 0: count pass, bit 1: apply pass; 0 = both */
+  int32_t pad2;
   KtirEwProgram f;     /* view 0 = the gathered element (load), view 1 = result (store) */
 } KtirGatherRmwDesc;
 

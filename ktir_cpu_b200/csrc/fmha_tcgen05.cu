@@ -1,16 +1,20 @@
 // Causal / full flash attention on the 5th-generation tensor cores.
 //
 // Q, K, V, O are f16 [bh*seq, 128] row-major (one head = seq consecutive
-// rows).  One CTA owns 128 query rows of one head (thread t of the 4 warps
-// owns query row t, which is also TMEM lane t) and walks the key blocks
-// of 64 rows:
-//   S  = Q K^T        tcgen05.mma M=128 N=64  K=128 (Q and K both K-major)
-//   softmax           thread-local per row from tcgen05.ld of S: running
-//                     max / sum in f32, P = exp(S - m) written to shared
-//                     memory as f16 in the 128-byte swizzled K-major layout
-//   PV = P V          tcgen05.mma M=128 N=128 K=64  (V consumed MN-major)
-//   O  = O*alpha + PV in registers (f32), O / l at the end
-// K/V blocks stream through a 2-stage TMA ring.  Waits are bounded.
+// rows).  One CTA owns 128 query rows of one head; thread t of the 4 warps
+// owns query row t, which is also TMEM lane t.  Key blocks are 64 rows:
+//   S_j  = Q K_j^T    tcgen05.mma M=128 N=64 K=128 into one of two TMEM
+//                     S buffers, issued one block ahead so the tensor cores
+//                     compute S_{j+1} while the threads run softmax on S_j
+//   softmax           thread-local per row (tcgen05.ld of S_j), P_j = 2^(x - m)
+//                     written to shared memory as f16, 128-byte swizzled
+//   O   += P_j V_j    tcgen05.mma M=128 N=128 K=64, O accumulates in TMEM
+// The running max m is only moved when a row's new max exceeds it by more
+// than 2^8 (then O and l are rescaled through tcgen05.ld/st, warp-uniform);
+// otherwise P stays below 2^8, which f16 holds exactly enough, and O / l is
+// unchanged because O and l share the same m.  K/V stream through a 3-stage
+// TMA ring.  Every wait is bounded; after a timed-out wait the CTA skips the
+// remaining work but still runs every barrier and frees its TMEM.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -23,18 +27,20 @@ using namespace ktir::tc;
 
 namespace {
 
-constexpr int D = 128;         // head dim
-constexpr int BQ = 128;        // query rows per CTA
-constexpr int BKV = 64;        // key rows per block
-constexpr int Q_BYTES = BQ * D * 2;            // 32 KiB (two 64-column boxes)
-constexpr int KV_BOX = BKV * 64 * 2;           // 8 KiB: 64 rows x 64 columns
-constexpr int K_BYTES = BKV * D * 2;           // 16 KiB
-constexpr int V_BYTES = BKV * D * 2;           // 16 KiB
-constexpr int STAGE_BYTES = K_BYTES + V_BYTES; // 32 KiB
-constexpr int P_BYTES = BQ * BKV * 2;          // 16 KiB
-constexpr int SMEM_BYTES = Q_BYTES + 2 * STAGE_BYTES + P_BYTES + 1024;
-constexpr uint32_t TMEM_COLS = 256;            // S: 64 columns, PV: 128 columns
-constexpr uint32_t S_COL = 0, PV_COL = 128;
+constexpr int D = 128;          // head dim
+constexpr int BQ = 128;         // query rows per CTA
+constexpr int BKV = 64;         // key rows per block
+constexpr int STAGES = 3;
+constexpr int Q_BYTES = BQ * D * 2;             // 32 KiB (two 64-column boxes)
+constexpr int KV_BOX = BKV * 64 * 2;            // 8 KiB: 64 rows x 64 columns
+constexpr int K_BYTES = BKV * D * 2;            // 16 KiB
+constexpr int V_BYTES = BKV * D * 2;            // 16 KiB
+constexpr int STAGE_BYTES = K_BYTES + V_BYTES;  // 32 KiB
+constexpr int P_BYTES = BQ * BKV * 2;           // 16 KiB
+constexpr int SMEM_BYTES = Q_BYTES + STAGES * STAGE_BYTES + P_BYTES + 1024;
+constexpr uint32_t TMEM_COLS = 256;             // S0: 0..63, S1: 64..127, O: 128..255
+constexpr uint32_t O_COL = 128;
+constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
 
 struct FmhaParams {
   __half* o;
@@ -46,12 +52,10 @@ struct FmhaParams {
   int* status;
 };
 
-__device__ __forceinline__ void tmem_ld32f(uint32_t taddr, float (&f)[32]) {
-  uint32_t r[32];
-  tmem_ld32(taddr, r);
-  tmem_ld_wait();
-#pragma unroll
-  for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(r[i]);
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __global__ void __launch_bounds__(128, 1)
@@ -59,8 +63,8 @@ __global__ void __launch_bounds__(128, 1)
                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ FmhaParams p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_bar;
-  __shared__ __align__(8) uint64_t kv_bar[2];
-  __shared__ __align__(8) uint64_t s_bar;
+  __shared__ __align__(8) uint64_t kv_bar[STAGES];
+  __shared__ __align__(8) uint64_t s_bar[2];
   __shared__ __align__(8) uint64_t pv_bar;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -68,9 +72,7 @@ __global__ void __launch_bounds__(128, 1)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
-  const int lane = tid & 31;
-  // heaviest (last) query tiles first
-  const int qt = p.n_qtiles - 1 - (int)blockIdx.x;
+  const int qt = p.n_qtiles - 1 - (int)blockIdx.x;   // heaviest query tiles first
   const long long head = blockIdx.y;
   const long long row0 = head * p.seq + (long long)qt * BQ;
   const int q0 = qt * BQ;
@@ -78,15 +80,15 @@ __global__ void __launch_bounds__(128, 1)
 
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sQ = base;
-  const uint32_t sKV = base + Q_BYTES;           // stage s at sKV + s * STAGE_BYTES (K then V)
-  const uint32_t sP = sKV + 2 * STAGE_BYTES;
+  const uint32_t sKV = base + Q_BYTES;
+  const uint32_t sP = sKV + STAGES * STAGE_BYTES;
 
   if (tid == 0) {
     abort_flag = 0;
     mbar_init(smem_u32(&q_bar), 1);
-    mbar_init(smem_u32(&kv_bar[0]), 1);
-    mbar_init(smem_u32(&kv_bar[1]), 1);
-    mbar_init(smem_u32(&s_bar), 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(smem_u32(&kv_bar[s]), 1);
+    mbar_init(smem_u32(&s_bar[0]), 1);
+    mbar_init(smem_u32(&s_bar[1]), 1);
     mbar_init(smem_u32(&pv_bar), 1);
     fence_barrier_init();
   }
@@ -98,8 +100,13 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
 
-  auto load_kv = [&](int j, int s) {
+  constexpr uint32_t idesc_s = idesc_f16(BQ, BKV, 0, 0);   // Q, K both K-major
+  constexpr uint32_t idesc_pv = idesc_f16(BQ, D, 0, 1);    // P K-major, V MN-major
+
+  auto load_kv = [&](int j) {
+    const int s = j % STAGES;
     const uint32_t kb = sKV + s * STAGE_BYTES;
     const uint32_t vb = kb + K_BYTES;
     const uint32_t bar = smem_u32(&kv_bar[s]);
@@ -110,6 +117,22 @@ __global__ void __launch_bounds__(128, 1)
     tma_load_2d(vb, &tv, bar, 0, kr);
     tma_load_2d(vb + KV_BOX, &tv, bar, 64, kr);
   };
+  // S_j = Q K_j^T into S buffer j & 1 (thread 0 only)
+  auto issue_s = [&](int j) {
+    const int s = j % STAGES;
+    if (!mbar_wait(smem_u32(&kv_bar[s]), (j / STAGES) & 1, abort)) return;
+    tc_fence_after();
+    const uint32_t kb = sKV + s * STAGE_BYTES;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const uint32_t chunk = kk >> 2;
+      const uint32_t koff = (kk & 3) * 32;
+      const uint64_t ad = sdesc_sw128(sQ + chunk * (Q_BYTES / 2) + koff, 16, 1024);
+      const uint64_t bd = sdesc_sw128(kb + chunk * KV_BOX + koff, 16, 1024);
+      mma_f16(tmem + (uint32_t)((j & 1) * BKV), ad, bd, idesc_s, kk != 0);
+    }
+    mma_commit(smem_u32(&s_bar[j & 1]));
+  };
 
   if (tid == 0) {
     tma_prefetch_desc(&tq);
@@ -119,82 +142,80 @@ __global__ void __launch_bounds__(128, 1)
     mbar_arrive_expect_tx(qb, Q_BYTES);
     tma_load_2d(sQ, &tq, qb, 0, (int)row0);
     tma_load_2d(sQ + Q_BYTES / 2, &tq, qb, 64, (int)row0);
-    load_kv(0, 0);
-    if (n_kv > 1) load_kv(1, 1);
+    for (int j = 0; j < STAGES && j < n_kv; ++j) load_kv(j);
+    if (mbar_wait(qb, 0, abort)) issue_s(0);
   }
 
-  // S: M=128 N=64, A = Q K-major, B = K K-major;  PV: M=128 N=128, A = P K-major, B = V MN-major
-  constexpr uint32_t idesc_s = idesc_f16(BQ, BKV, 0, 0);
-  constexpr uint32_t idesc_pv = idesc_f16(BQ, D, 0, 1);
-
-  float o[D];
-#pragma unroll
-  for (int i = 0; i < D; ++i) o[i] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
+  float m_used = -INFINITY, l_run = 0.f;
   const int qpos = q0 + tid;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-  // Every thread runs every iteration and every barrier; after a timed-out
-  // wait (abort flag set) the remaining work is skipped, never the barriers.
   for (int j = 0; j < n_kv; ++j) {
-    const int s = j & 1;
-    const uint32_t kb = sKV + s * STAGE_BYTES;
-    const uint32_t vb = kb + K_BYTES;
-    if (tid == 0 && !*abort) {
-      bool good = (j > 0 || mbar_wait(smem_u32(&q_bar), 0, abort)) &&
-                  mbar_wait(smem_u32(&kv_bar[s]), (j >> 1) & 1, abort);
-      if (good) {
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t chunk = kk >> 2;          // 64-column chunk of d
-          const uint32_t koff = (kk & 3) * 32;     // 16 d = 32 bytes within a 128-byte row
-          const uint64_t ad = sdesc_sw128(sQ + chunk * (Q_BYTES / 2) + koff, 16, 1024);
-          const uint64_t bd = sdesc_sw128(kb + chunk * KV_BOX + koff, 16, 1024);
-          mma_f16(tmem + S_COL, ad, bd, idesc_s, kk != 0);
-        }
-        mma_commit(smem_u32(&s_bar));
-      }
-    }
     __syncwarp();
-    mbar_wait(smem_u32(&s_bar), j & 1, abort);
+    mbar_wait(smem_u32(&s_bar[j & 1]), (j >> 1) & 1, abort);
     tc_fence_after();
-
-    // ---- softmax on this thread's row ------------------------------------
     float sv[BKV];
     {
-      float t[32];
-      tmem_ld32f(tmem + lane_base + S_COL, t);
+      uint32_t r[32];
+      tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * BKV), r);
+      tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) sv[i] = t[i];
-      tmem_ld32f(tmem + lane_base + S_COL + 32, t);
+      for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(r[i]);
+      tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * BKV) + 32, r);
+      tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) sv[32 + i] = t[i];
+      for (int i = 0; i < 32; ++i) sv[32 + i] = __uint_as_float(r[i]);
     }
+    // the next block's S goes to the other buffer, read last in iteration j-1
+    if (tid == 0 && j + 1 < n_kv && !*abort) issue_s(j + 1);
+
     const int kpos0 = j * BKV;
+    const bool diag = p.causal && kpos0 + BKV - 1 > q0;
     float mx = -INFINITY;
 #pragma unroll
     for (int i = 0; i < BKV; ++i) {
       float x = sv[i] * p.scale_log2;
-      if (p.causal && kpos0 + i > qpos) x = -INFINITY;
+      if (diag && kpos0 + i > qpos) x = -INFINITY;
       sv[i] = x;
       mx = fmaxf(mx, x);
     }
-    const float m_new = fmaxf(m_run, mx);
-    const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m_run - m_new);
+    const float m_new = fmaxf(m_used, mx);
+    float factor = 1.f;
+    bool rescale = false;
+    if (m_used == -INFINITY || m_new > m_used + RESCALE_THRESHOLD) {
+      factor = (m_used == -INFINITY) ? 0.f : ex2(m_used - m_new);
+      rescale = m_used != -INFINITY;
+      l_run *= factor;
+      m_used = m_new;
+    }
     float psum = 0.f;
     __half2 ph[BKV / 2];
 #pragma unroll
     for (int i = 0; i < BKV; i += 2) {
-      const float a = (m_new == -INFINITY) ? 0.f : exp2f(sv[i] - m_new);
-      const float b = (m_new == -INFINITY) ? 0.f : exp2f(sv[i + 1] - m_new);
+      const float a = (m_used == -INFINITY) ? 0.f : ex2(sv[i] - m_used);
+      const float b = (m_used == -INFINITY) ? 0.f : ex2(sv[i + 1] - m_used);
       psum += a + b;
       ph[i / 2] = __floats2half2_rn(a, b);
     }
-    l_run = l_run * alpha + psum;
-    m_run = m_new;
+    l_run += psum;
+
+    // PV_{j-1} done: O is complete up to block j-1, P and K/V stage (j-1)%3 are free
+    if (j > 0) {
+      __syncwarp();
+      mbar_wait(smem_u32(&pv_bar), (j - 1) & 1, abort);
+      tc_fence_after();
+    }
+    if (tid == 0 && j > 0 && j + 2 < n_kv && !*abort) load_kv(j + 2);
+    if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + O_COL + c, r);
+        tmem_ld_wait();
 #pragma unroll
-    for (int i = 0; i < D; ++i) o[i] *= alpha;
-    // P row -> shared memory, 128-byte swizzle: 16-byte unit u of row r lands at u ^ (r & 7)
+        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+        tmem_st32(tmem + lane_base + O_COL + c, r);
+      }
+      tmem_st_wait();
+    }
     {
       const uint32_t rowaddr = sP + tid * 128;
       const uint4* src = reinterpret_cast<const uint4*>(ph);
@@ -209,42 +230,39 @@ __global__ void __launch_bounds__(128, 1)
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
-
     if (tid == 0 && !*abort) {
       tc_fence_after();
+      const uint32_t vb = sKV + (j % STAGES) * STAGE_BYTES + K_BYTES;
 #pragma unroll
       for (int kk = 0; kk < BKV / 16; ++kk) {
         const uint64_t ad = sdesc_sw128(sP + kk * 32, 16, 1024);
         const uint64_t bd = sdesc_sw128(vb + kk * 16 * 128, KV_BOX, 1024);
-        mma_f16(tmem + PV_COL, ad, bd, idesc_pv, kk != 0);
+        mma_f16(tmem + O_COL, ad, bd, idesc_pv, (j | kk) != 0);
       }
       mma_commit(smem_u32(&pv_bar));
     }
-    __syncwarp();
-    mbar_wait(smem_u32(&pv_bar), j & 1, abort);
-    tc_fence_after();
-#pragma unroll
-    for (int c = 0; c < D; c += 32) {
-      float t[32];
-      tmem_ld32f(tmem + lane_base + PV_COL + c, t);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) o[c + i] += t[i];
-    }
-    tc_fence_before();
-    __syncthreads();
-    // stage s is free (its S and PV MMAs are complete): prefetch block j + 2
-    if (tid == 0 && j + 2 < n_kv && !*abort) load_kv(j + 2, s);
   }
 
+  __syncwarp();
+  mbar_wait(smem_u32(&pv_bar), (n_kv - 1) & 1, abort);
+  tc_fence_after();
   if (!*abort) {
     const float inv = 1.f / l_run;
     __half* orow = p.o + (row0 + tid) * p.row_stride;
+#pragma unroll 1
+    for (int c = 0; c < D; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tmem + lane_base + O_COL + c, r);
+      tmem_ld_wait();
 #pragma unroll
-    for (int c = 0; c < D; c += 8) {
-      __half2 h[4];
+      for (int q = 0; q < 4; ++q) {
+        __half2 h[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(o[c + 2 * i] * inv, o[c + 2 * i + 1] * inv);
-      *reinterpret_cast<uint4*>(orow + c) = *reinterpret_cast<const uint4*>(h);
+        for (int i = 0; i < 4; ++i)
+          h[i] = __floats2half2_rn(__uint_as_float(r[8 * q + 2 * i]) * inv,
+                                   __uint_as_float(r[8 * q + 2 * i + 1]) * inv);
+        *reinterpret_cast<uint4*>(orow + c + 8 * q) = *reinterpret_cast<const uint4*>(h);
+      }
     }
   }
   tc_fence_before();

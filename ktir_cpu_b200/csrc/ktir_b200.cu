@@ -208,11 +208,18 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
   const __half* in = (const __half*)b.base[d.in.slot];
   __half* out = (__half*)b.base[d.out.slot];
   const int64_t in_numel = b.numel[d.in.slot];
-  auto in_base = [&](int64_t row) {
-    const int unit = (int)(row / d.rows);
-    const int r = (int)(row - (int64_t)unit * d.rows);
-    return d.in.off + (d.in.unit_col >= 0 ? ut[(int64_t)unit * d.unit_cols + d.in.unit_col] : 0) +
-           (int64_t)r * d.in.stride[0];
+  // units that are consecutive row blocks arrive as one unit (no table)
+  auto in_base = [&](int64_t row) -> int64_t {
+    if (d.in.unit_col < 0) return d.in.off + row * d.in.stride[0];
+    const int unit = (int)row / d.rows;
+    const int r = (int)row - unit * d.rows;
+    return d.in.off + ut[(int64_t)unit * d.unit_cols + d.in.unit_col] + (int64_t)r * d.in.stride[0];
+  };
+  auto out_base = [&](int64_t row) -> int64_t {
+    if (d.out.unit_col < 0) return d.out.off + row * d.out.stride[0];
+    const int unit = (int)row / d.rows;
+    const int r = (int)row - unit * d.rows;
+    return d.out.off + ut[(int64_t)unit * d.unit_cols + d.out.unit_col] + (int64_t)r * d.out.stride[0];
   };
   uint4 cur[VPL];
   if (warp < total_rows) load_row<VPL>(in, in_numel, in_base(warp), lane, cur);
@@ -220,11 +227,7 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
     uint4 nxt[VPL];
     const int64_t nrow = row + nwarps;
     if (nrow < total_rows) load_row<VPL>(in, in_numel, in_base(nrow), lane, nxt);
-    const int unit = (int)(row / d.rows);
-    const int r = (int)(row - (int64_t)unit * d.rows);
-    const int64_t ob = d.out.off +
-                       (d.out.unit_col >= 0 ? ut[(int64_t)unit * d.unit_cols + d.out.unit_col] : 0) +
-                       (int64_t)r * d.out.stride[0];
+    const int64_t ob = out_base(row);
     float v[VPL][8];
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
@@ -296,8 +299,10 @@ extern "C" int ktir_softmax_rows(const KtirSoftmaxDesc* d, const KtirBuffers* bu
     return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: needs f16 rows of 2^k >= 256 elements");
   if (((d->in.off | d->out.off | d->in.stride[0] | d->out.stride[0]) & 7) != 0)
     return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: rows must be 16-byte aligned");
+  if ((int64_t)d->n_units * d->rows >= (1ll << 31))
+    return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: more than 2^31 rows");
   const int64_t rows = (int64_t)d->n_units * d->rows;
-  const int threads = 256;
+  const int threads = 128;
   // rows per warp (descriptor's spare field, 0 = default 2)
   const int rpw = d->pad > 0 ? d->pad : 2;
   const int blocks = grid_x((rows + rpw - 1) / rpw * 32, threads, 1 << 30);
@@ -399,6 +404,8 @@ __global__ void __launch_bounds__(256) k_rmw_apply(const __grid_constant__ KtirG
   const int ngroups = (int)((gridDim.x * blockDim.x) >> 4);
   const int total = d.n_units * d.unit_len;
   const bool dense_units = d.idx_unit_stride == d.unit_len;
+  const int64_t row_lo = d.row_hi > 0 ? d.row_lo : 0;
+  const int64_t row_hi = d.row_hi > 0 ? d.row_hi : n_rows;
   __half* table = (__half*)b.base[d.table_slot];
   const int64_t tnumel = b.numel[d.table_slot];
   const int out_dt = d.f.view[1].dtype;
@@ -414,7 +421,8 @@ __global__ void __launch_bounds__(256) k_rmw_apply(const __grid_constant__ KtirG
     int m = 0;
     if (sub == 0 && row >= 0 && row < n_rows) m = atomicExch(&counts[row], 0);
     m = __shfl_sync(0xffffffffu, m, (threadIdx.x & 31) & ~15);
-    if (m <= 0) continue;
+    // rows owned by another shard are consumed (counts stay zero) but not applied
+    if (m <= 0 || row < row_lo || row >= row_hi) continue;
     const int64_t rb = d.table_off + row * d.row_stride;
     for (int c = sub * 8; c < d.row_len; c += 128) {
       const int64_t e = rb + c;
@@ -465,9 +473,14 @@ extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* d, const KtirBuffers* bu
                                          (int)smem);
     if (e != cudaSuccess) return set_err(KTIR_ERR_CUDA, cudaGetErrorString(e));
   }
-  k_rmw_count<<<d->n_units, 512, smem, s>>>(*d, *bufs, counts, n_rows, status);
-  int rc = check_launch("ktir_gather_rmw(count)");
-  if (rc) return rc;
+  const bool do_count = d->phases == 0 || (d->phases & 1);
+  const bool do_apply = d->phases == 0 || (d->phases & 2);
+  if (do_count) {
+    k_rmw_count<<<d->n_units, 512, smem, s>>>(*d, *bufs, counts, n_rows, status);
+    int rc = check_launch("ktir_gather_rmw(count)");
+    if (rc) return rc;
+  }
+  if (!do_apply) return KTIR_OK;
   // recognise y = x op imm (one arithmetic instruction between load and store)
   int simple_op = 0;
   float simple_imm = 0.f;

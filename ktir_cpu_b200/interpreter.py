@@ -153,7 +153,13 @@ class KTIRInterpreter:
     """KTIR interpreter whose execution runs on a B200 (API of ktir_cpu.KTIRInterpreter)."""
 
     def __init__(self, latency_config: Any = None, trace_latency: bool = False,
-                 parser: Optional[KTIRParserBase] = None, device: Any = None):
+                 parser: Optional[KTIRParserBase] = None, device: Any = None,
+                 shard: Optional[Tuple[int, int, Any]] = None):
+        """`shard=(rank, world, group)` splits every call's core grid across
+        `world` GPUs by contiguous core ranges: this process executes only the
+        cores of `rank` (programs that need an exchange between shards use the
+        torch.distributed `group`).  Tensors this shard does not write come
+        back unchanged."""
         self.module: Optional[IRModule] = None
         self.memory: Optional[DeviceMemory] = None
         self.grid_executor = None
@@ -162,6 +168,7 @@ class KTIRInterpreter:
         self._trace_latency = trace_latency
         self._latency_report = None
         self._device = device
+        self._shard = shard
         self._cache: Dict[Any, Tuple[Executable, AddressSpace]] = {}
         self.last_executable: Optional[Executable] = None
 
@@ -254,12 +261,12 @@ class KTIRInterpreter:
         slots = {b.index: b.index for b in space.buffers}
         rewrites = attention_rewrites(func)
         trace = Tracer(func, space, scalars, ptrs, rewrites=rewrites).run()
-        plan = Lowerer(trace, device, slots).lower()
+        plan = Lowerer(trace, device, slots, self._shard).lower()
         if rewrites and plan.kind != "attention":
             # the rewritten loops did not form a whole attention problem the
             # tensor-core kernel covers: trace the loops op by op instead
             trace = Tracer(func, space, scalars, ptrs).run()
-            plan = Lowerer(trace, device, slots).lower()
+            plan = Lowerer(trace, device, slots, self._shard).lower()
         exe = Executable(plan, space, device, func.grid)
         entry = (exe, [a for a, _ in allocs])
         self._cache[key] = entry

@@ -474,15 +474,31 @@ def units_independent(items: Sequence[Tuple[List[Tuple[int, Tuple[int, int]]],
 # the lowering entry point
 # ---------------------------------------------------------------------------
 
+def core_range(rank: int, world: int, n_cores: int) -> Tuple[int, int]:
+    """Contiguous block of cores owned by `rank` when a grid is split across `world` GPUs."""
+    return (rank * n_cores) // world, ((rank + 1) * n_cores) // world
+
+
 class Lowerer:
-    def __init__(self, trace: Trace, device, slots: Dict[int, int]):
+    """Lower one traced call.  With `shard=(rank, world, group)` only the stores
+    of this rank's contiguous core range are lowered (the grid is split across
+    GPUs); programs that need an exchange between shards get a collective."""
+
+    def __init__(self, trace: Trace, device, slots: Dict[int, int], shard=None):
         self.trace = trace
         self.device = device
         self.slots = slots            # buffer index -> slot
         self.dev = DeviceData(device)
+        self.shard = shard
 
     def lower(self) -> Plan:
         stores = self.trace.stores
+        self.all_stores = stores
+        if self.shard is not None:
+            rank, world = self.shard[0], self.shard[1]
+            nx, ny, nz = self.trace.grid
+            c0, c1 = core_range(rank, world, nx * ny * nz)
+            stores = [s for s in stores if c0 <= s.core < c1]
         for matcher in (self.match_gather_rmw, self.match_gemm, self.match_attention,
                         self.match_softmax, self.match_elementwise):
             plan = matcher(stores)
@@ -508,6 +524,18 @@ class Lowerer:
 
     # -- gather -> f -> scatter ----------------------------------------------------
     def match_gather_rmw(self, stores: List[Store]) -> Optional[Plan]:
+        if self.shard is not None:
+            # every unit's indices are needed to apply the owned rows; the
+            # local units only decide this shard's share of the counts
+            full = self._gather_rmw_desc(self.all_stores)
+            local = self._gather_rmw_desc(stores) if stores else None
+            if full is None or (stores and local is None):
+                return None
+            return self._gather_rmw_plan(full, local)
+        d = self._gather_rmw_desc(stores)
+        return None if d is None else self._gather_rmw_plan(d, None)
+
+    def _gather_rmw_desc(self, stores: List[Store]):
         if not stores or not all(isinstance(s.target, IndirectTarget) for s in stores):
             return None
         table_buf = None
@@ -535,6 +563,7 @@ class Lowerer:
             if fdag is None:
                 fdag = (ld, s.value)
         (R_, C_, row_stride, idx_view, idx_elem), ld0, v0 = units[0]
+        del idx_elem
         if any(u[0][:3] != (R_, C_, row_stride) for u in units):
             return None
         if table_buf.dtype != np.float16 or v0.dtype != np.float16:
@@ -572,17 +601,47 @@ class Lowerer:
         d.idx_unit_stride = step
         d.f = program(bld, (1,), 1, 0, lambda k: mkview(0, np.float16, 0, (0,)))
         n_rows = -(-table_buf.numel // row_stride)
+        return d, n_rows, len(units), R_, C_
+
+    def _gather_rmw_plan(self, full, local) -> Plan:
+        d, n_rows, n_units, R_, C_ = full
         counts = self.dev.zeros_i32(n_rows)
         lib = R.load_library()
-        desc = d
+        cptr = C.c_void_p(counts.data_ptr())
+        if self.shard is None:
+            def run(bufs, stream, status):
+                R.check(lib.ktir_gather_rmw(C.byref(d), C.byref(bufs), cptr, n_rows,
+                                            C.c_void_p(status), stream), "ktir_gather_rmw")
+            launches = [Launch(run, "gather_rmw", 2)]
+        else:
+            rank, world, group = self.shard
+            r0, r1 = core_range(rank, world, n_rows)
+            dl = None
+            if local is not None:
+                dl = local[0]
+                dl.phases = 1
+            d.phases = 2
+            d.row_lo, d.row_hi = r0, r1
 
-        def run(bufs, stream, status):
-            R.check(lib.ktir_gather_rmw(C.byref(desc), C.byref(bufs), C.c_void_p(counts.data_ptr()),
-                                        n_rows, C.c_void_p(status), stream), "ktir_gather_rmw")
-        plan = Plan("gather_rmw", [Launch(run, "gather_rmw", 2)], [], status_check=True)
+            def run_count(bufs, stream, status):
+                if dl is not None:
+                    R.check(lib.ktir_gather_rmw(C.byref(dl), C.byref(bufs), cptr, n_rows,
+                                                C.c_void_p(status), stream), "ktir_gather_rmw(count)")
+
+            def run_exchange(bufs, stream, status):
+                import torch.distributed as dist
+                dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
+
+            def run_apply(bufs, stream, status):
+                R.check(lib.ktir_gather_rmw(C.byref(d), C.byref(bufs), cptr, n_rows,
+                                            C.c_void_p(status), stream), "ktir_gather_rmw(apply)")
+            launches = [Launch(run_count, "gather_rmw_count", 1 if dl is not None else 0),
+                        Launch(run_exchange, "allreduce_counts", 0),
+                        Launch(run_apply, "gather_rmw_apply", 1)]
+        plan = Plan("gather_rmw", launches, [], status_check=True)
         plan.scratch["counts"] = counts
-        plan.info.update(units=len(units), unit_len=R_, row_len=C_,
-                         idx_elems=len(units) * R_, table_rows=n_rows)
+        plan.info.update(units=n_units, unit_len=R_, row_len=C_, idx_elems=n_units * R_,
+                         table_rows=n_rows)
         return plan
 
     # -- GEMM / attention are filled in by the tensor-core modules ---------------------
@@ -631,11 +690,21 @@ class Lowerer:
             return None
         d = R.KtirSoftmaxDesc()
         d.rows, d.cols, d.n_units, d.unit_cols = rows, cols, len(units), 2
+        # units that are consecutive row blocks of both tensors become one
+        # affine row range: the kernel then needs no per-unit table
+        s_in, s_out = ld0.attrs["strides"][0], t0.strides[0]
+        u = np.arange(len(units), dtype=np.int64)
+        affine = bool(np.all(table[:, 0] == table[0, 0] + u * rows * s_in) and
+                      np.all(table[:, 1] == table[0, 1] + u * rows * s_out))
         d.compute_f16 = 1 if compute_f16 else 0
         d.pad = int(os.environ.get("KTIR_SOFTMAX_ROWS_PER_WARP", "0"))
-        d.in_ = mkview(self.slots[ld0.attrs["buf"].index], np.float16, 0,
-                       (ld0.attrs["strides"][0], 1), unit_col=0)
-        d.out = mkview(self.slots[t0.buf.index], np.float16, 0, (t0.strides[0], 1), unit_col=1)
+        if affine:
+            d.rows, d.n_units = rows * len(units), 1
+            d.in_ = mkview(self.slots[ld0.attrs["buf"].index], np.float16, table[0, 0], (s_in, 1))
+            d.out = mkview(self.slots[t0.buf.index], np.float16, table[0, 1], (s_out, 1))
+        else:
+            d.in_ = mkview(self.slots[ld0.attrs["buf"].index], np.float16, 0, (s_in, 1), unit_col=0)
+            d.out = mkview(self.slots[t0.buf.index], np.float16, 0, (s_out, 1), unit_col=1)
         ut = self.dev.i64(table)
         lib = R.load_library()
         desc = d

@@ -372,15 +372,22 @@ def match_attention_plan(low, stores):
                 return None
             seq = seq_u
         seen.add(qrow)
-    if seq is None or seq % 128 or rows % seq or len(seen) * bq != rows:
+    if seq is None or seq % 128 or rows % seq:
         return None
-    bh = rows // seq
+    # the units must cover whole heads [h_lo, h_hi) (all heads, or a shard's)
+    heads = sorted({q // seq for q in seen})
+    h_lo, h_hi = heads[0], heads[-1] + 1
+    if len(seen) * bq != (h_hi - h_lo) * seq or heads != list(range(h_lo, h_hi)):
+        return None
+    bh = h_hi - h_lo
+    off = h_lo * seq * d * 2
     lib = R.load_library()
     sq, sk, sv, so = (low.slots[b.index] for b in (qbuf, kbuf, vbuf, obuf))
 
     def run(bufs, stream, status):
         dsc = R.KtirFmhaDesc()
-        dsc.q, dsc.k, dsc.v, dsc.o = bufs.base[sq], bufs.base[sk], bufs.base[sv], bufs.base[so]
+        dsc.q, dsc.k, dsc.v, dsc.o = (bufs.base[sq] + off, bufs.base[sk] + off,
+                                      bufs.base[sv] + off, bufs.base[so] + off)
         dsc.bh, dsc.seq, dsc.d = bh, seq, d
         dsc.scale = scale
         dsc.causal = 1 if causal else 0

@@ -71,7 +71,8 @@ class KtirGatherRmwDesc(C.Structure):
     _fields_ = [("table_slot", C.c_int32), ("idx_slot", C.c_int32), ("idx_dtype", C.c_int32),
                 ("n_units", C.c_int32), ("unit_len", C.c_int32), ("row_len", C.c_int32),
                 ("table_off", C.c_int64), ("row_stride", C.c_int64), ("idx_off", C.c_int64),
-                ("idx_unit_stride", C.c_int64), ("f", KtirEwProgram)]
+                ("idx_unit_stride", C.c_int64), ("row_lo", C.c_int64), ("row_hi", C.c_int64),
+                ("phases", C.c_int32), ("pad2", C.c_int32), ("f", KtirEwProgram)]
 
 
 class KtirReduceDesc(C.Structure):

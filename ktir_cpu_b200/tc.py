@@ -108,28 +108,36 @@ def match_gemm(low, stores: List[Store]):
         tiles.append((i0, j0, bm, bn))
     if abuf is cbuf or bbuf is cbuf:
         return None
-    M = cbuf.numel // ldc
-    N = ldc
-    if lda != K or abuf.numel != M * K or bbuf.numel != K * N or ldb != N or cbuf.numel != M * N:
+    Mfull = cbuf.numel // ldc
+    Nfull = ldc
+    if lda != K or abuf.numel != Mfull * K or bbuf.numel != K * Nfull or ldb != Nfull:
+        return None
+    # the stores must tile one rectangle of C exactly (all of C, or the block
+    # a shard of the core grid owns)
+    i_lo = min(t[0] for t in tiles)
+    j_lo = min(t[1] for t in tiles)
+    i_hi = max(t[0] + t[2] for t in tiles)
+    j_hi = max(t[1] + t[3] for t in tiles)
+    M, N = i_hi - i_lo, j_hi - j_lo
+    if i_hi > Mfull or j_hi > Nfull:
         return None
     cover = np.zeros((M, N), dtype=np.int8) if M * N <= (1 << 26) else None
     area = 0
     for i0, j0, bm, bn in tiles:
-        if i0 + bm > M or j0 + bn > N:
-            return None
         area += bm * bn
         if cover is not None:
-            cover[i0:i0 + bm, j0:j0 + bn] += 1
+            cover[i0 - i_lo:i0 - i_lo + bm, j0 - j_lo:j0 - j_lo + bn] += 1
     if area != M * N or (cover is not None and not np.all(cover == 1)):
         return None
     if M % GEMM_TILE_M or N % GEMM_TILE_N or K % GEMM_TILE_K:
         return None
     lib = R.load_library()
     sa, sb, sc = low.slots[abuf.index], low.slots[bbuf.index], low.slots[cbuf.index]
+    a_off, b_off, c_off = i_lo * lda * 2, j_lo * 2, (i_lo * ldc + j_lo) * 2
 
     def run(bufs, stream, status):
         d = R.KtirGemmDesc()
-        d.a, d.b, d.c = bufs.base[sa], bufs.base[sb], bufs.base[sc]
+        d.a, d.b, d.c = bufs.base[sa] + a_off, bufs.base[sb] + b_off, bufs.base[sc] + c_off
         d.lda, d.ldb, d.ldc = lda, ldb, ldc
         d.m, d.n, d.k = M, N, K
         d.add_zero = 1
