@@ -6,6 +6,8 @@ through the C ABI in include/ktir_b200.h (libktir_b200.so).
 """
 
 from .interpreter import KTIRInterpreter
+from .latency import HardwareConfig, LatencyCategory, LatencyReport
 from .parser import KTIRParser, KTIRParserBase
 
-__all__ = ["KTIRInterpreter", "KTIRParser", "KTIRParserBase"]
+__all__ = ["KTIRInterpreter", "KTIRParser", "KTIRParserBase", "HardwareConfig",
+           "LatencyCategory", "LatencyReport"]

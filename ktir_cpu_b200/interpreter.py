@@ -108,6 +108,7 @@ class Executable:
         self.lib = R.load_library()
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.dev_tensors = None
+        self.latency_tape = None
         self.pinned = None
         self.bufs = None
         self.arena = None
@@ -198,6 +199,9 @@ class KTIRInterpreter:
 
     def _prepare_execution(self, grid_shape: Tuple[int, int, int]) -> None:
         self.memory = DeviceMemory(grid_shape[0] * grid_shape[1] * grid_shape[2])
+        if self._latency_config is not None:
+            from .latency import LatencyReport
+            self._latency_report = LatencyReport(self._latency_config, {})
 
     # -- execution ----------------------------------------------------------------------
     def _device_obj(self):
@@ -207,7 +211,9 @@ class KTIRInterpreter:
             self._device = torch.device("cuda", torch.cuda.current_device())
         return torch.device(self._device)
 
-    def execute_function(self, func_name: str, **kwargs) -> Dict[str, np.ndarray]:
+    def _bind(self, func_name: str, kwargs: Dict[str, Any]):
+        """Allocate every ndarray argument in the HBM façade (stick-aligned, in
+        argument order, as ktir_cpu/interpreter.py:137-160 does)."""
         if not self.module:
             raise RuntimeError("No module loaded. Call load() first.")
         func = self.module.get_function(func_name)
@@ -230,13 +236,59 @@ class KTIRInterpreter:
                 dts[name] = _KTIR_OF[np.dtype(v.dtype)]
             else:
                 scalars[name] = v
+        return func, kwargs, ptrs, scalars, dts
+
+    def _space(self, ptrs: Dict[str, int]) -> AddressSpace:
+        space = AddressSpace()
+        names = {v * STICK: k for k, v in ptrs.items()}
+        for addr, arr in sorted(self.memory.hbm.allocs.items()):
+            space.add_fixed(names.get(addr, f"hbm@0x{addr:x}"), addr, arr.nbytes, arr.dtype,
+                            arr.shape)
+        return space
+
+    def execute_function(self, func_name: str, **kwargs) -> Dict[str, np.ndarray]:
+        func, kwargs, ptrs, scalars, dts = self._bind(func_name, kwargs)
+        hbm = self.memory.hbm
         exe, order = self._executable(func_name, ptrs, scalars)
+        if self._latency_config is not None:
+            # charged on the call's inputs, before the device writes anything
+            self._latency_report = exe.latency_tape.report(
+                self._latency_config, self._trace_latency, self._index_reader())
         self.run_host(exe, order)
         out = {}
         for name, v in kwargs.items():
             if isinstance(v, np.ndarray):
                 out[name] = hbm.read(ptrs[name], v.size, dts[name]).reshape(v.shape)
         return out
+
+    def estimate_latency(self, func_name: str, **kwargs):
+        """The latency report of one call, computed on the host without running
+        it (no GPU needed); `latency_config` defaults to HardwareConfig()."""
+        from .latency import HardwareConfig, LatencyTape
+        func, kwargs, ptrs, scalars, dts = self._bind(func_name, kwargs)
+        tape = LatencyTape()
+        Tracer(func, self._space(ptrs), scalars, ptrs, latency=tape).run()
+        cfg = self._latency_config if self._latency_config is not None else HardwareConfig()
+        return tape.report(cfg, self._trace_latency, self._index_reader())
+
+    def _index_reader(self):
+        """Values of index tensors at byte addresses, from the host copies of the
+        call's allocations (zero outside every allocation, like a read past the
+        end of one)."""
+        from .trace import np_dtype
+        allocs = [(base, arr.view(np.uint8).reshape(-1))
+                  for base, arr in self.memory.hbm.allocs.items()]
+
+        def read(addrs: np.ndarray, dtype: str) -> np.ndarray:
+            dt = np_dtype(dtype)
+            raw = np.zeros((addrs.size, dt.itemsize), np.uint8)
+            for base, b in allocs:
+                sel = (addrs >= base) & (addrs + dt.itemsize <= base + b.size)
+                if sel.any():
+                    rel = addrs[sel] - base
+                    raw[sel] = b[rel[:, None] + np.arange(dt.itemsize)]
+            return raw.reshape(-1).view(dt)
+        return read
 
     def _executable(self, func_name: str, ptrs: Dict[str, int], scalars: Dict[str, Any]):
         hbm = self.memory.hbm
@@ -252,22 +304,25 @@ class KTIRInterpreter:
             raise NotImplementedError(f"at most {R.ARENA_SLOT - 1} tensors per call")
         device = self._device_obj()
         func = self.module.get_function(func_name)
-        space = AddressSpace()
-        names = {v * STICK: k for k, v in ptrs.items()}
-        for addr, arr in allocs:
-            space.add_fixed(names.get(addr, f"hbm@0x{addr:x}"), addr, arr.nbytes, arr.dtype,
-                            arr.shape)
+        space = self._space(ptrs)
+        from .latency import LatencyTape
         from .rewrite import attention_rewrites
         slots = {b.index: b.index for b in space.buffers}
         rewrites = attention_rewrites(func)
-        trace = Tracer(func, space, scalars, ptrs, rewrites=rewrites).run()
+        tape = LatencyTape() if self._latency_config is not None else None
+        trace = Tracer(func, space, scalars, ptrs, rewrites=rewrites,
+                       latency=None if rewrites else tape).run()
         plan = Lowerer(trace, device, slots, self._shard).lower()
         if rewrites and plan.kind != "attention":
             # the rewritten loops did not form a whole attention problem the
             # tensor-core kernel covers: trace the loops op by op instead
-            trace = Tracer(func, space, scalars, ptrs).run()
+            trace = Tracer(func, space, scalars, ptrs, latency=tape).run()
             plan = Lowerer(trace, device, slots, self._shard).lower()
+        elif rewrites and tape is not None:
+            # rewritten loops are not traced op by op: one more pass for the tape
+            Tracer(func, space, scalars, ptrs, latency=tape).run()
         exe = Executable(plan, space, device, func.grid)
+        exe.latency_tape = tape
         entry = (exe, [a for a, _ in allocs])
         self._cache[key] = entry
         self.last_executable = exe

@@ -257,6 +257,17 @@ def _is_tile(v) -> bool:
     return isinstance(v, Node) and bool(v.shape)
 
 
+def _elements(res, operands) -> int:
+    """Element count an op is charged for: its tile result, else its first
+    tile operand, else 1 (ktir_cpu/latency.py:340-347)."""
+    if isinstance(res, Node) and not res.pyscalar:
+        return int(np.prod(res.shape)) if res.shape else 1
+    for v in operands:
+        if isinstance(v, Node) and not v.pyscalar:
+            return int(np.prod(v.shape)) if v.shape else 1
+    return 1
+
+
 def _concrete(v) -> bool:
     return isinstance(v, (int, float, bool, np.integer, np.floating, np.bool_))
 
@@ -330,7 +341,8 @@ class Trace:
 
 class Tracer:
     def __init__(self, func: IRFunction, space: AddressSpace, scalars: Dict[str, Any],
-                 pointers: Dict[str, int], rewrites: Optional[Dict[int, Any]] = None):
+                 pointers: Dict[str, int], rewrites: Optional[Dict[int, Any]] = None,
+                 latency=None):
         self.func = func
         self.space = space
         self.scalars = scalars
@@ -339,6 +351,8 @@ class Tracer:
         self.core: Optional[CoreState] = None
         self.seq = 0
         self.rewrites = rewrites or {}
+        # LatencyTape receiving one record per executed op (optional)
+        self.lat = latency
 
     # -- node helpers ----------------------------------------------------------
     def node(self, kind, shape, dtype, ins=(), attrs=None, label=None, pyscalar=False) -> Node:
@@ -357,6 +371,8 @@ class Tracer:
             z, r = divmod(cid, nx * ny)
             y, x = divmod(r, nx)
             self.core = CoreState(cid, (x, y, z))
+            if self.lat is not None:
+                self.lat.begin_core(cid)
             for aname, _ in self.func.arguments:
                 key = aname.lstrip("%")
                 if key in self.pointers:
@@ -395,7 +411,56 @@ class Tracer:
                 core.set(name, val)
                 if _is_tile(val):
                     core.track(name, val.nbytes)
+        if self.lat is not None:
+            self._lat_record(op, res)
         return res
+
+    # -- latency records (op-for-op with ktir_cpu/latency.py:175-265) ---------------
+    def _operands(self, op):
+        return [self.core.get(o) if isinstance(o, str) and self.core.has(o) else None
+                for o in op.operands]
+
+    def _lat_record(self, op, res):
+        from . import latency as L
+        cat = L.category(op.op_type)
+        arg = None
+        if cat == "memory":
+            if op.op_type == "ktdp.load":
+                arg = self._load_sticks(res)
+            else:
+                arg = self._store_sticks(self.trace.stores[-1].target)
+        elif cat == "compute_matmul":
+            tiles = [v for v in self._operands(op) if _is_tile(v)]
+            if len(tiles) >= 2:
+                a, b = tiles[0].shape, tiles[1].shape
+                arg = (a[0] if len(a) >= 2 else 1, b[1] if len(b) >= 2 else 1,
+                       a[1] if len(a) >= 2 else a[0])
+            else:
+                arg = (1, 1, 1)
+        elif cat != "zero":
+            arg = _elements(res, self._operands(op))
+        self.lat.add(op.op_type, cat, arg)
+
+    def _load_sticks(self, n: "Node"):
+        from . import latency as L
+        a = n.attrs
+        if a["mode"] == "indirect":
+            return L.IndirectAccess(a["iat"], store=False)
+        buf, isz = a["buf"], n.dtype.itemsize
+        base = buf.byte_base + a["off"] * isz
+        if a["mode"] == "rect":
+            return L.rect_sticks(base, n.shape, a["strides"], isz)
+        return L.coord_sticks(base, a["offsets"], isz)
+
+    def _store_sticks(self, t):
+        from . import latency as L
+        if isinstance(t, IndirectTarget):
+            return L.IndirectAccess(t.iat, store=True)
+        isz = np.dtype(t.dtype).itemsize
+        base = t.buf.byte_base + t.off * isz
+        if isinstance(t, RectTarget):
+            return L.rect_sticks(base, t.shape, t.strides, isz)
+        return L.coord_sticks(base, t.offsets, isz)
 
     # -- grid / views ------------------------------------------------------------
     def op_ktdp_get_compute_tile_id(self, op):
@@ -1090,10 +1155,49 @@ def _op_linalg_reduce(self, op):
             shape = tuple(s for i, s in enumerate(t.shape) if i != dim)
             res = self.node("reduce", shape, t.dtype, (t,), {"dim": dim, "combiner": comb},
                             t.label, pyscalar=not shape)
+    if self.lat is not None and _is_tile(t):
+        _lat_fold(self, op, t, dims[0] if dims else None)
     outs = a.get("outs")
     if outs and res is not None:
         self.core.set(outs, res)
     return res
+
+
+def _lat_fold(self, op, t: Node, dim):
+    """Latency records of the pairwise tree fold: the combiner region runs once
+    per round on halves of the reduced axis (ktir_cpu/dialects/linalg_ops.py:
+    84-133), each of its ops charged on the half-size operands."""
+    from . import latency as L
+    if op.regions and op.regions[0].ops:
+        region = op.regions[0]
+        body = list(region.ops)
+        names = [n for n, _ in region.args] or list(body[0].operands)
+    else:
+        fn = op.attributes.get("combiner") or "arith.addf"
+        body = [Operation(fn, ["__comb__"], ["__in__", "__acc__"], {}),
+                Operation("linalg.yield", [], ["__comb__"], {})]
+        names = ["__in__", "__acc__"]
+    shape = list(t.shape) if dim is not None else [t.numel]
+    d = dim if dim is not None else 0
+    n = shape[d]
+    while n > 1:
+        half = n // 2
+        shape[d] = half
+        elems = int(np.prod(shape))
+        tiles = set(names[:2])
+        for o in body:
+            cat = L.category(o.op_type)
+            on_tile = any(x in tiles for x in o.operands)
+            if on_tile:
+                tiles.update(o.results)
+            if cat == "compute_matmul":
+                arg = (1, 1, 1)
+            elif cat == "zero":
+                arg = None
+            else:
+                arg = elems if on_tile else 1
+            self.lat.add(o.op_type, cat, arg)
+        n = half + n % 2
 
 
 def _op_linalg_add(self, op):

@@ -39,3 +39,24 @@ def test_replay_uses_cached_plan():
     assert interp.last_executable is exe
     for k in a:
         assert np.array_equal(a[k], b[k])
+
+
+@pytest.mark.parametrize("name", ["softmax_rows128_cols1024_grid4_chunk32",
+                                  "gather_add_dups",
+                                  "attention_batch1_heads2_seq256_dim128_grid2_bq64_bk64"])
+def test_latency_report_alongside_gpu_run(name):
+    """With latency_config set, a GPU call leaves the reference's report behind."""
+    import json
+    import os
+    from ktir_cpu_b200 import HardwareConfig, KTIRInterpreter
+    gold = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "latency.json")))
+    g = load_golden(name)
+    interp = KTIRInterpreter(latency_config=HardwareConfig())
+    interp.load(g["src"])
+    out = interp.execute_function(g["func"], **{k: v.copy() for k, v in g["inputs"].items()})
+    for k, want in g["outputs"].items():
+        assert_matches(f"{name}:{k}", out[k], want, g["tol"])
+    rep = interp.get_latency_report()
+    assert rep.kernel_cycles == gold[name]["kernel_cycles"]
+    for cid, w in gold[name]["cores"].items():
+        assert rep.counters[int(cid)].total_bytes == w["total_bytes"]
