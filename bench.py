@@ -184,6 +184,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--shard", action="store_true",
                     help="split one execution's core grid across the ranks (strong scaling)")
+    ap.add_argument("--eager", action="store_true",
+                    help="time per-step host launches instead of one CUDA graph of the K steps")
     ap.add_argument("--profile", action="store_true",
                     help="only warmup + steps plain launches on two buffer sets (for ncu)")
     args = ap.parse_args()
@@ -242,6 +244,14 @@ def main():
             print(json.dumps({"profile_run": args.config, "plan": plan.kind,
                               "launches": (args.warmup + args.steps) * plan.kernel_launches}))
         return
+    # the K timed executions, recorded once as a CUDA graph so the host's
+    # per-launch cost does not pace the device (sharded plans with an NCCL
+    # exchange keep plain launches)
+    graph = None
+    if not shard and not args.eager:
+        graph = exe.capture([sets[i % n_sets][0] for i in range(args.steps)])
+        graph.replay()
+        torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -259,8 +269,11 @@ def main():
             dist.barrier()
         torch.cuda.synchronize(dev)
         ev0.record(stream)
-        for i in range(args.steps):
-            exe.launch(sets[i % n_sets][0], stream, sets[i % n_sets][1])
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                exe.launch(sets[i % n_sets][0], stream, sets[i % n_sets][1])
         ev1.record(stream)
         torch.cuda.synchronize(dev)
         # per-launch durations of the plan's kernels (dominant kernel time)
@@ -302,6 +315,7 @@ def main():
         interp.execute_function(fname, **kw)
     torch.cuda.synchronize(dev)
     e2e_s = time.perf_counter() - t0
+    e2e_exe = interp.last_executable
     if world > 1:
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -333,9 +347,12 @@ def main():
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": src_peak, "kernel": DOMINANT[args.config],
                          "kernel_ms": kern_ms, "isolated_launch_ms": launch_ms,
-                         "plan_kernels": plan.kernel_launches},
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": in_bytes,
-                    "d2h_bytes_per_step": in_bytes},
+                         "plan_kernels": plan.kernel_launches,
+                         "launch": "cuda graph of the K steps" if graph is not None
+                         else "host launch per step"},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": e2e_exe.last_h2d_bytes,
+                    "d2h_bytes_per_step": e2e_exe.last_d2h_bytes,
+                    "arg_bytes": in_bytes},
             "gpu_launches": args.steps * plan.kernel_launches,
             "clocks": clk.summary(),
         }

@@ -1,20 +1,25 @@
 // Causal / full flash attention on the 5th-generation tensor cores.
 //
 // Q, K, V, O are f16 [bh*seq, 128] row-major (one head = seq consecutive
-// rows).  One CTA owns 128 query rows of one head; thread t of the 4 warps
-// owns query row t, which is also TMEM lane t.  Key blocks are 64 rows:
-//   S_j  = Q K_j^T    tcgen05.mma M=128 N=64 K=128 into one of two TMEM
-//                     S buffers, issued one block ahead so the tensor cores
-//                     compute S_{j+1} while the threads run softmax on S_j
-//   softmax           thread-local per row (tcgen05.ld of S_j), P_j = 2^(x - m)
-//                     written to shared memory as f16, 128-byte swizzled
-//   O   += P_j V_j    tcgen05.mma M=128 N=128 K=64, O accumulates in TMEM
-// The running max m is only moved when a row's new max exceeds it by more
-// than 2^8 (then O and l are rescaled through tcgen05.ld/st, warp-uniform);
-// otherwise P stays below 2^8, which f16 holds exactly enough, and O / l is
-// unchanged because O and l share the same m.  K/V stream through a 3-stage
-// TMA ring.  Every wait is bounded; after a timed-out wait the CTA skips the
-// remaining work but still runs every barrier and frees its TMEM.
+// rows).  One CTA owns 128 query rows of one head and walks the key blocks of
+// 128 rows with three warp roles that meet only at mbarriers:
+//   warp 4 (TMA)      Q once; K_j and V_j into their own rings (3 K stages,
+//                     2 V stages), each slot refilled as soon as the MMA that
+//                     read it completes
+//   warp 5 (MMA)      S_j = Q K_j^T (M=128 N=128 K=128) into TMEM S buffer
+//                     j & 1, then O += P_{j-1} V_{j-1} with P read straight
+//                     from TMEM (M=128 N=128 K=128); S_j is issued before
+//                     PV_{j-1} so the tensor cores compute S_{j+1} and PV_j
+//                     while the softmax warps work on S_j
+//   warps 0-3         thread t owns query row t = TMEM lane t: tcgen05.ld of
+//                     S_j, masked scaled max, P = 2^(x - m) packed to f16 and
+//                     tcgen05.st into TMEM P buffer j & 1, row sum l
+// TMEM (512 columns): S0 0..127, S1 128..255, O 256..383, P0 384..447,
+// P1 448..511.  The running max m only moves when a row's max exceeds it by
+// more than 2^8; then the softmax warp waits for the previous PV and rescales
+// its O rows in TMEM (warp-uniform), otherwise O and l keep sharing m.
+// Every wait is bounded; a timed-out wait raises the CTA's abort flag, every
+// role then leaves its loop, and the CTA still frees its TMEM.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -29,17 +34,16 @@ namespace {
 
 constexpr int D = 128;          // head dim
 constexpr int BQ = 128;         // query rows per CTA
-constexpr int BKV = 64;         // key rows per block
-constexpr int STAGES = 3;
-constexpr int Q_BYTES = BQ * D * 2;             // 32 KiB (two 64-column boxes)
-constexpr int KV_BOX = BKV * 64 * 2;            // 8 KiB: 64 rows x 64 columns
-constexpr int K_BYTES = BKV * D * 2;            // 16 KiB
-constexpr int V_BYTES = BKV * D * 2;            // 16 KiB
-constexpr int STAGE_BYTES = K_BYTES + V_BYTES;  // 32 KiB
-constexpr int P_BYTES = BQ * BKV * 2;           // 16 KiB
-constexpr int SMEM_BYTES = Q_BYTES + STAGES * STAGE_BYTES + P_BYTES + 1024;
-constexpr uint32_t TMEM_COLS = 256;             // S0: 0..63, S1: 64..127, O: 128..255
-constexpr uint32_t O_COL = 128;
+constexpr int BKV = 128;        // key rows per block
+constexpr int KST = 3;          // K ring stages
+constexpr int VST = 2;          // V ring stages
+constexpr int THREADS = 192;
+constexpr int HALF_BOX = 128 * 64 * 2;          // 16 KiB: 128 rows x 64 columns
+constexpr int TILE_BYTES = 2 * HALF_BOX;        // 32 KiB: 128 rows x 128 columns
+constexpr int SMEM_BYTES = (1 + KST + VST) * TILE_BYTES + 1024;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t O_COL = 256;
+constexpr uint32_t P_COL = 384;
 constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
 
 struct FmhaParams {
@@ -58,20 +62,26 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__global__ void __launch_bounds__(128, 1)
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
     k_fmha_tcgen05(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ FmhaParams p) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_bar;
-  __shared__ __align__(8) uint64_t kv_bar[STAGES];
-  __shared__ __align__(8) uint64_t s_bar[2];
-  __shared__ __align__(8) uint64_t pv_bar;
+  __shared__ __align__(8) uint64_t q_full;
+  __shared__ __align__(8) uint64_t k_full[KST], k_empty[KST];
+  __shared__ __align__(8) uint64_t v_full[VST], v_empty[VST];
+  __shared__ __align__(8) uint64_t s_full[2], p_full[2], pv_done[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int* abort = &abort_flag;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
+  const int lane = tid & 31;
   const int qt = p.n_qtiles - 1 - (int)blockIdx.x;   // heaviest query tiles first
   const long long head = blockIdx.y;
   const long long row0 = head * p.seq + (long long)qt * BQ;
@@ -80,16 +90,25 @@ __global__ void __launch_bounds__(128, 1)
 
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sQ = base;
-  const uint32_t sKV = base + Q_BYTES;
-  const uint32_t sP = sKV + STAGES * STAGE_BYTES;
+  const uint32_t sK = base + TILE_BYTES;
+  const uint32_t sV = sK + KST * TILE_BYTES;
 
   if (tid == 0) {
     abort_flag = 0;
-    mbar_init(smem_u32(&q_bar), 1);
-    for (int s = 0; s < STAGES; ++s) mbar_init(smem_u32(&kv_bar[s]), 1);
-    mbar_init(smem_u32(&s_bar[0]), 1);
-    mbar_init(smem_u32(&s_bar[1]), 1);
-    mbar_init(smem_u32(&pv_bar), 1);
+    mbar_init(smem_u32(&q_full), 1);
+    for (int s = 0; s < KST; ++s) {
+      mbar_init(smem_u32(&k_full[s]), 1);
+      mbar_init(smem_u32(&k_empty[s]), 1);
+    }
+    for (int s = 0; s < VST; ++s) {
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&s_full[b]), 1);
+      mbar_init(smem_u32(&p_full[b]), BQ);
+      mbar_init(smem_u32(&pv_done[b]), 1);
+    }
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -100,168 +119,185 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
 
-  constexpr uint32_t idesc_s = idesc_f16(BQ, BKV, 0, 0);   // Q, K both K-major
-  constexpr uint32_t idesc_pv = idesc_f16(BQ, D, 0, 1);    // P K-major, V MN-major
-
-  auto load_kv = [&](int j) {
-    const int s = j % STAGES;
-    const uint32_t kb = sKV + s * STAGE_BYTES;
-    const uint32_t vb = kb + K_BYTES;
-    const uint32_t bar = smem_u32(&kv_bar[s]);
-    const int kr = (int)(head * p.seq) + j * BKV;
-    mbar_arrive_expect_tx(bar, STAGE_BYTES);
-    tma_load_2d(kb, &tk, bar, 0, kr);
-    tma_load_2d(kb + KV_BOX, &tk, bar, 64, kr);
-    tma_load_2d(vb, &tv, bar, 0, kr);
-    tma_load_2d(vb + KV_BOX, &tv, bar, 64, kr);
-  };
-  // S_j = Q K_j^T into S buffer j & 1 (thread 0 only)
-  auto issue_s = [&](int j) {
-    const int s = j % STAGES;
-    if (!mbar_wait(smem_u32(&kv_bar[s]), (j / STAGES) & 1, abort)) return;
-    tc_fence_after();
-    const uint32_t kb = sKV + s * STAGE_BYTES;
-#pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      const uint32_t chunk = kk >> 2;
-      const uint32_t koff = (kk & 3) * 32;
-      const uint64_t ad = sdesc_sw128(sQ + chunk * (Q_BYTES / 2) + koff, 16, 1024);
-      const uint64_t bd = sdesc_sw128(kb + chunk * KV_BOX + koff, 16, 1024);
-      mma_f16(tmem + (uint32_t)((j & 1) * BKV), ad, bd, idesc_s, kk != 0);
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      const uint32_t qb = smem_u32(&q_full);
+      mbar_arrive_expect_tx(qb, TILE_BYTES);
+      tma_load_2d(sQ, &tq, qb, 0, (int)row0);
+      tma_load_2d(sQ + HALF_BOX, &tq, qb, 64, (int)row0);
+      const int kv_row0 = (int)(head * p.seq);
+      for (int j = 0; j < n_kv && !*abort; ++j) {
+        const int kr = kv_row0 + j * BKV;
+        const int ks = j % KST;
+        if (j >= KST && !mbar_wait(smem_u32(&k_empty[ks]), ((j / KST) - 1) & 1, abort)) break;
+        const uint32_t kf = smem_u32(&k_full[ks]);
+        const uint32_t kb = sK + ks * TILE_BYTES;
+        mbar_arrive_expect_tx(kf, TILE_BYTES);
+        tma_load_2d(kb, &tk, kf, 0, kr);
+        tma_load_2d(kb + HALF_BOX, &tk, kf, 64, kr);
+        const int vs = j % VST;
+        if (j >= VST && !mbar_wait(smem_u32(&v_empty[vs]), ((j / VST) - 1) & 1, abort)) break;
+        const uint32_t vf = smem_u32(&v_full[vs]);
+        const uint32_t vb = sV + vs * TILE_BYTES;
+        mbar_arrive_expect_tx(vf, TILE_BYTES);
+        tma_load_2d(vb, &tv, vf, 0, kr);
+        tma_load_2d(vb + HALF_BOX, &tv, vf, 64, kr);
+      }
     }
-    mma_commit(smem_u32(&s_bar[j & 1]));
-  };
-
-  if (tid == 0) {
-    tma_prefetch_desc(&tq);
-    tma_prefetch_desc(&tk);
-    tma_prefetch_desc(&tv);
-    const uint32_t qb = smem_u32(&q_bar);
-    mbar_arrive_expect_tx(qb, Q_BYTES);
-    tma_load_2d(sQ, &tq, qb, 0, (int)row0);
-    tma_load_2d(sQ + Q_BYTES / 2, &tq, qb, 64, (int)row0);
-    for (int j = 0; j < STAGES && j < n_kv; ++j) load_kv(j);
-    if (mbar_wait(qb, 0, abort)) issue_s(0);
-  }
-
-  float m_used = -INFINITY, l_run = 0.f;
-  const int qpos = q0 + tid;
-  for (int j = 0; j < n_kv; ++j) {
-    __syncwarp();
-    mbar_wait(smem_u32(&s_bar[j & 1]), (j >> 1) & 1, abort);
-    tc_fence_after();
-    float sv[BKV];
-    {
-      uint32_t r[32];
-      tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * BKV), r);
-      tmem_ld_wait();
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16(BQ, BKV, 0, 0);   // Q, K both K-major
+      constexpr uint32_t idesc_pv = idesc_f16(BQ, D, 0, 1);    // P (TMEM) K-major, V MN-major
+      auto issue_pv = [&](int i) -> bool {
+        if (!mbar_wait(smem_u32(&p_full[i & 1]), (i >> 1) & 1, abort)) return false;
+        const int vs = i % VST;
+        if (!mbar_wait(smem_u32(&v_full[vs]), (i / VST) & 1, abort)) return false;
+        tc_fence_after();
+        const uint32_t vb = sV + vs * TILE_BYTES;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(r[i]);
-      tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * BKV) + 32, r);
-      tmem_ld_wait();
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint64_t bd = sdesc_sw128(vb + kk * 16 * 128, HALF_BOX, 1024);
+          mma_f16_ts(tmem + O_COL, tmem + P_COL + (uint32_t)((i & 1) * 64 + kk * 8), bd,
+                     idesc_pv, (i | kk) != 0);
+        }
+        mma_commit(smem_u32(&pv_done[i & 1]));
+        mma_commit(smem_u32(&v_empty[vs]));
+        return true;
+      };
+      bool ok = mbar_wait(smem_u32(&q_full), 0, abort);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int ks = j % KST;
+        if (!mbar_wait(smem_u32(&k_full[ks]), (j / KST) & 1, abort)) break;
+        // S buffer j & 1 was last read by softmax j - 2
+        if (j >= 2 && !mbar_wait(smem_u32(&p_full[j & 1]), ((j - 2) >> 1) & 1, abort)) break;
+        tc_fence_after();
+        const uint32_t kb = sK + ks * TILE_BYTES;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) sv[32 + i] = __uint_as_float(r[i]);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t chunk = kk >> 2;
+          const uint32_t koff = (kk & 3) * 32;
+          const uint64_t ad = sdesc_sw128(sQ + chunk * HALF_BOX + koff, 16, 1024);
+          const uint64_t bd = sdesc_sw128(kb + chunk * HALF_BOX + koff, 16, 1024);
+          mma_f16(tmem + (uint32_t)((j & 1) * BKV), ad, bd, idesc_s, kk != 0);
+        }
+        mma_commit(smem_u32(&s_full[j & 1]));
+        mma_commit(smem_u32(&k_empty[ks]));
+        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && !*abort) issue_pv(n_kv - 1);
     }
-    // the next block's S goes to the other buffer, read last in iteration j-1
-    if (tid == 0 && j + 1 < n_kv && !*abort) issue_s(j + 1);
-
-    const int kpos0 = j * BKV;
-    const bool diag = p.causal && kpos0 + BKV - 1 > q0;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < BKV; ++i) {
-      float x = sv[i] * p.scale_log2;
-      if (diag && kpos0 + i > qpos) x = -INFINITY;
-      sv[i] = x;
-      mx = fmaxf(mx, x);
-    }
-    const float m_new = fmaxf(m_used, mx);
-    float factor = 1.f;
-    bool rescale = false;
-    if (m_used == -INFINITY || m_new > m_used + RESCALE_THRESHOLD) {
-      factor = (m_used == -INFINITY) ? 0.f : ex2(m_used - m_new);
-      rescale = m_used != -INFINITY;
-      l_run *= factor;
-      m_used = m_new;
-    }
-    float psum = 0.f;
-    __half2 ph[BKV / 2];
-#pragma unroll
-    for (int i = 0; i < BKV; i += 2) {
-      const float a = (m_used == -INFINITY) ? 0.f : ex2(sv[i] - m_used);
-      const float b = (m_used == -INFINITY) ? 0.f : ex2(sv[i + 1] - m_used);
-      psum += a + b;
-      ph[i / 2] = __floats2half2_rn(a, b);
-    }
-    l_run += psum;
-
-    // PV_{j-1} done: O is complete up to block j-1, P and K/V stage (j-1)%3 are free
-    if (j > 0) {
-      __syncwarp();
-      mbar_wait(smem_u32(&pv_bar), (j - 1) & 1, abort);
+  } else {
+    // ---------------- softmax warps 0-3 ----------------
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const int qpos = q0 + tid;
+    float m_used = -INFINITY, l_run = 0.f;
+    // waits are made warp-uniform: tcgen05.ld/st need the whole warp
+    for (int j = 0; j < n_kv; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[j & 1]), (j >> 1) & 1, abort)))
+        break;
       tc_fence_after();
+      float sv[BKV];
+#pragma unroll
+      for (int c = 0; c < BKV; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * BKV + c), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c + i] = __uint_as_float(r[i]);
+      }
+      const int kpos0 = j * BKV;
+      const bool diag = p.causal && kpos0 + BKV - 1 > q0;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BKV; ++i) {
+        float x = sv[i] * p.scale_log2;
+        if (diag && kpos0 + i > qpos) x = -INFINITY;
+        sv[i] = x;
+        mx = fmaxf(mx, x);
+      }
+      const float m_new = fmaxf(m_used, mx);
+      float factor = 1.f;
+      bool rescale = false;
+      if (m_used == -INFINITY || m_new > m_used + RESCALE_THRESHOLD) {
+        factor = (m_used == -INFINITY) ? 0.f : ex2(m_used - m_new);
+        rescale = m_used != -INFINITY;
+        l_run *= factor;
+        m_used = m_new;
+      }
+      const float msub = (m_used == -INFINITY) ? 0.f : m_used;
+      float psum = 0.f;
+      uint32_t ph[BKV / 2];
+#pragma unroll
+      for (int i = 0; i < BKV; i += 2) {
+        const float a = ex2(sv[i] - msub);
+        const float b = ex2(sv[i + 1] - msub);
+        psum += a + b;
+        ph[i / 2] = pack_h2(a, b);
+      }
+      l_run += psum;
+      // O rows move only when PV_{j-1} has landed; P buffer j & 1 is free once
+      // PV_{j-2} has read it
+      bool ok = true;
+      if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(smem_u32(&pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, abort));
+        tc_fence_after();
+        if (ok) {
+#pragma unroll 1
+          for (int c = 0; c < D; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(tmem + lane_base + O_COL + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+            tmem_st32(tmem + lane_base + O_COL + c, r);
+          }
+        }
+      } else if (j >= 2) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(smem_u32(&pv_done[j & 1]), ((j - 2) >> 1) & 1, abort));
+        tc_fence_after();
+      }
+      if (!ok) break;
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = ph[32 * h + i];
+          tmem_st32(tmem + lane_base + P_COL + (uint32_t)((j & 1) * 64 + 32 * h), r);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&p_full[j & 1]));
     }
-    if (tid == 0 && j > 0 && j + 2 < n_kv && !*abort) load_kv(j + 2);
-    if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+    const bool done = !*abort &&
+                      mbar_wait(smem_u32(&pv_done[(n_kv - 1) & 1]), ((n_kv - 1) >> 1) & 1, abort);
+    if (__all_sync(0xffffffffu, done)) {
+      tc_fence_after();
+      const float inv = 1.f / l_run;
+      __half* orow = p.o + (row0 + tid) * p.row_stride;
 #pragma unroll 1
       for (int c = 0; c < D; c += 32) {
         uint32_t r[32];
         tmem_ld32(tmem + lane_base + O_COL + c, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-        tmem_st32(tmem + lane_base + O_COL + c, r);
-      }
-      tmem_st_wait();
-    }
-    {
-      const uint32_t rowaddr = sP + tid * 128;
-      const uint4* src = reinterpret_cast<const uint4*>(ph);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const uint32_t dst = rowaddr + ((u ^ (tid & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(src[u].x),
-                     "r"(src[u].y), "r"(src[u].z), "r"(src[u].w)
-                     : "memory");
-      }
-    }
-    fence_proxy_async();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && !*abort) {
-      tc_fence_after();
-      const uint32_t vb = sKV + (j % STAGES) * STAGE_BYTES + K_BYTES;
-#pragma unroll
-      for (int kk = 0; kk < BKV / 16; ++kk) {
-        const uint64_t ad = sdesc_sw128(sP + kk * 32, 16, 1024);
-        const uint64_t bd = sdesc_sw128(vb + kk * 16 * 128, KV_BOX, 1024);
-        mma_f16(tmem + O_COL, ad, bd, idesc_pv, (j | kk) != 0);
-      }
-      mma_commit(smem_u32(&pv_bar));
-    }
-  }
-
-  __syncwarp();
-  mbar_wait(smem_u32(&pv_bar), (n_kv - 1) & 1, abort);
-  tc_fence_after();
-  if (!*abort) {
-    const float inv = 1.f / l_run;
-    __half* orow = p.o + (row0 + tid) * p.row_stride;
-#pragma unroll 1
-    for (int c = 0; c < D; c += 32) {
-      uint32_t r[32];
-      tmem_ld32(tmem + lane_base + O_COL + c, r);
-      tmem_ld_wait();
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        __half2 h[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          h[i] = __floats2half2_rn(__uint_as_float(r[8 * q + 2 * i]) * inv,
-                                   __uint_as_float(r[8 * q + 2 * i + 1]) * inv);
-        *reinterpret_cast<uint4*>(orow + c + 8 * q) = *reinterpret_cast<const uint4*>(h);
+        for (int q = 0; q < 4; ++q) {
+          uint4 v;
+          v.x = pack_h2(__uint_as_float(r[8 * q + 0]) * inv, __uint_as_float(r[8 * q + 1]) * inv);
+          v.y = pack_h2(__uint_as_float(r[8 * q + 2]) * inv, __uint_as_float(r[8 * q + 3]) * inv);
+          v.z = pack_h2(__uint_as_float(r[8 * q + 4]) * inv, __uint_as_float(r[8 * q + 5]) * inv);
+          v.w = pack_h2(__uint_as_float(r[8 * q + 6]) * inv, __uint_as_float(r[8 * q + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c + 8 * q) = v;
+        }
       }
     }
   }
@@ -336,6 +372,6 @@ extern "C" int ktir_fmha_f16(const KtirFmhaDesc* d, void* stream) {
   p.n_qtiles = (int)(d->seq / BQ);
   p.status = d->status;
   dim3 grid((unsigned)p.n_qtiles, (unsigned)d->bh);
-  k_fmha_tcgen05<<<grid, 128, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  k_fmha_tcgen05<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? KTIR_OK : KTIR_ERR_CUDA;
 }

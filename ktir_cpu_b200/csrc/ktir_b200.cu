@@ -12,6 +12,7 @@
 //  k_reduce, k_matmul, k_offsets, k_indirect_*
 //                  generic-path kernels for programs no fused kernel covers
 #include <cuda_runtime.h>
+#include <utility>
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -48,6 +49,31 @@ extern "C" int ktir_device_count(int* count) {
   return KTIR_OK;
 }
 
+// Programmatic dependent launch: the kernel may be scheduled while the
+// previous kernel on the stream drains; it runs pdl_prologue() before touching
+// global memory, which waits for that kernel to complete and its writes to be
+// visible, then lets the next kernel be scheduled the same way.
+__device__ __forceinline__ void pdl_prologue() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 static inline int grid_x(int64_t work, int threads, int cap) {
   int64_t g = (work + threads - 1) / threads;
   if (g < 1) g = 1;
@@ -63,6 +89,7 @@ __global__ void __launch_bounds__(256) k_ew(const __grid_constant__ KtirEwProgra
                                             const __grid_constant__ KtirBuffers b,
                                             const int64_t* __restrict__ ut) {
   __shared__ int64_t base[KTIR_MAX_VIEWS];
+  pdl_prologue();
   for (int unit = blockIdx.y; unit < p.n_units; unit += gridDim.y) {
     __syncthreads();
     if (threadIdx.x < p.n_views) {
@@ -116,58 +143,59 @@ extern "C" int ktir_ew(const KtirEwProgram* prog, const KtirBuffers* bufs,
   dim3 grid(grid_x(prog->numel, 256, 148 * 16), prog->n_units < 65535 ? prog->n_units : 65535);
   cudaStream_t s = (cudaStream_t)stream;
   if (prog->contiguous)
-    k_ew<true><<<grid, 256, 0, s>>>(*prog, *bufs, unit_table);
+    launch_pdl(k_ew<true>, grid, dim3(256), 0, s, *prog, *bufs, unit_table);
   else
-    k_ew<false><<<grid, 256, 0, s>>>(*prog, *bufs, unit_table);
+    launch_pdl(k_ew<false>, grid, dim3(256), 0, s, *prog, *bufs, unit_table);
   return check_launch("ktir_ew");
 }
 
 // ---------------------------------------------------------------------------
 // fused row softmax
 // ---------------------------------------------------------------------------
-// Layout: lane l holds elements 256*j + 8*l + k (k < 8, j < VPL) of its row,
-// i.e. one 16-byte vector of f16 per j.  With this layout the halving tree
-// of the reference (combine [0,h) with [h,2h), h = n/2, n/4, ..., 1) maps to:
-//   h >= 256      : vector j with vector j + h/256 in the same lane
-//   8 <= h <= 128 : lane l with lane l + h/8 (same j = 0, same k)
-//   h <= 4        : element k with k + h inside lane 0
-// so the fold below is the reference's fold, pair for pair.
-template <int VPL, bool F16>
-__device__ __forceinline__ float tree_fold(float (&v)[VPL][8], bool is_max) {
-  constexpr bool f16 = F16;
+// Layout: lane l holds elements 64*m + 2*l + k (k < 2, m < M = cols/64) of its
+// row, i.e. one f16 pair per m, so each warp load or store moves 128
+// contiguous bytes.  With this layout the halving tree of the reference
+// (combine [0,h) with [h,2h), h = n/2, n/4, ..., 1) maps to:
+//   h >= 64      : pair m with pair m + h/64 in the same lane
+//   2 <= h <= 32 : lane l with lane l + h/2 (m = 0, same k)
+//   h == 1       : k = 0 with k = 1 inside lane 0
+// so the sum below is the reference's fold, pair for pair, with only two
+// values per lane crossing lanes in each of the five shuffle rounds.  The max
+// does not depend on the order (fmax ignores NaN like arith.maxnumf, and a
+// zero's sign cannot change exp(x - max)), so it is an in-lane max and one
+// redux.sync.
+template <int M, bool F16>
+__device__ __forceinline__ float sum_fold(float (&v)[M][2]) {
   const unsigned full = 0xffffffffu;
-  // in-lane vector rounds: h = 128*VPL ... 256, vector j pairs with j + h/256
 #pragma unroll
-  for (int hv = VPL / 2; hv >= 1; hv >>= 1) {
+  for (int hm = M / 2; hm >= 1; hm >>= 1) {
 #pragma unroll
-    for (int j = 0; j < hv; ++j) {
+    for (int m = 0; m < hm; ++m) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        float r = is_max ? fmaxf(v[j][k], v[j + hv][k]) : v[j][k] + v[j + hv][k];
-        v[j][k] = f16 ? __half2float(__float2half_rn(r)) : r;
+      for (int k = 0; k < 2; ++k) {
+        const float r = v[m][k] + v[m + hm][k];
+        v[m][k] = F16 ? __half2float(__float2half_rn(r)) : r;
       }
     }
   }
-  // cross-lane rounds h = 128 .. 8: lane l pairs with lane l + h/8
 #pragma unroll
   for (int dl = 16; dl >= 1; dl >>= 1) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      float c = __shfl_down_sync(full, v[0][k], dl);
-      float r = is_max ? fmaxf(v[0][k], c) : v[0][k] + c;
-      v[0][k] = f16 ? __half2float(__float2half_rn(r)) : r;
+    for (int k = 0; k < 2; ++k) {
+      const float c = __shfl_down_sync(full, v[0][k], dl);
+      const float r = v[0][k] + c;
+      v[0][k] = F16 ? __half2float(__float2half_rn(r)) : r;
     }
   }
-  // in-lane element rounds h = 4, 2, 1 (lane 0 holds the result)
-#pragma unroll
-  for (int h = 4; h >= 1; h >>= 1) {
-#pragma unroll
-    for (int k = 0; k < h; ++k) {
-      float r = is_max ? fmaxf(v[0][k], v[0][k + h]) : v[0][k] + v[0][k + h];
-      v[0][k] = f16 ? __half2float(__float2half_rn(r)) : r;
-    }
-  }
-  return __shfl_sync(full, v[0][0], 0);
+  float r = v[0][0] + v[0][1];
+  r = F16 ? __half2float(__float2half_rn(r)) : r;
+  return __shfl_sync(full, r, 0);
+}
+
+__device__ __forceinline__ float warp_max(float x) {
+  float y;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -176,30 +204,30 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-template <int VPL>
+template <int M>
 __device__ __forceinline__ void load_row(const __half* in, int64_t numel, int64_t ib, int lane,
-                                         uint4 (&raw)[VPL]) {
+                                         uint32_t (&raw)[M]) {
 #pragma unroll
-  for (int j = 0; j < VPL; ++j) {
-    const int64_t e = ib + 256 * j + 8 * lane;
-    if (e >= 0 && e + 8 <= numel) {
-      raw[j] = __ldg(reinterpret_cast<const uint4*>(in + e));
+  for (int m = 0; m < M; ++m) {
+    const int64_t e = ib + 64 * m + 2 * lane;
+    if (e >= 0 && e + 2 <= numel) {
+      raw[m] = __ldg(reinterpret_cast<const unsigned int*>(in + e));
     } else {
-      __half h[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        h[k] = (e + k >= 0 && e + k < numel) ? in[e + k] : __float2half(0.f);
-      raw[j] = *reinterpret_cast<const uint4*>(h);
+      __half2 h;
+      h.x = (e >= 0 && e < numel) ? in[e] : __float2half(0.f);
+      h.y = (e + 1 >= 0 && e + 1 < numel) ? in[e + 1] : __float2half(0.f);
+      raw[m] = *reinterpret_cast<const uint32_t*>(&h);
     }
   }
 }
 
 // One warp per row; a warp walks rows `nwarps` apart and prefetches the next
-// row's vectors before reducing the current one, so loads overlap the math.
-template <int VPL, bool F16>
-__global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ KtirSoftmaxDesc d,
+// row's pairs before reducing the current one, so loads overlap the math.
+template <int M, bool F16>
+__global__ void __launch_bounds__(128) k_softmax_rows(const __grid_constant__ KtirSoftmaxDesc d,
                                                       const __grid_constant__ KtirBuffers b,
                                                       const int64_t* __restrict__ ut) {
+  pdl_prologue();
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t total_rows = (int64_t)d.n_units * d.rows;
@@ -208,6 +236,7 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
   const __half* in = (const __half*)b.base[d.in.slot];
   __half* out = (__half*)b.base[d.out.slot];
   const int64_t in_numel = b.numel[d.in.slot];
+  const int64_t out_numel = b.numel[d.out.slot];
   // units that are consecutive row blocks arrive as one unit (no table)
   auto in_base = [&](int64_t row) -> int64_t {
     if (d.in.unit_col < 0) return d.in.off + row * d.in.stride[0];
@@ -221,72 +250,61 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const __grid_constant__ Kt
     const int r = (int)row - unit * d.rows;
     return d.out.off + ut[(int64_t)unit * d.unit_cols + d.out.unit_col] + (int64_t)r * d.out.stride[0];
   };
-  uint4 cur[VPL];
-  if (warp < total_rows) load_row<VPL>(in, in_numel, in_base(warp), lane, cur);
+  uint32_t cur[M];
+  if (warp < total_rows) load_row<M>(in, in_numel, in_base(warp), lane, cur);
   for (int64_t row = warp; row < total_rows; row += nwarps) {
-    uint4 nxt[VPL];
+    uint32_t nxt[M];
     const int64_t nrow = row + nwarps;
-    if (nrow < total_rows) load_row<VPL>(in, in_numel, in_base(nrow), lane, nxt);
+    if (nrow < total_rows) load_row<M>(in, in_numel, in_base(nrow), lane, nxt);
     const int64_t ob = out_base(row);
-    float v[VPL][8];
+    float v[M][2];
+    float mx = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      const __half2* h2 = reinterpret_cast<const __half2*>(&cur[j]);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float2 f = __half22float2(h2[k]);
-        v[j][2 * k] = f.x;
-        v[j][2 * k + 1] = f.y;
-      }
+    for (int m = 0; m < M; ++m) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&cur[m]));
+      v[m][0] = f.x;
+      v[m][1] = f.y;
+      mx = fmaxf(mx, fmaxf(f.x, f.y));
     }
-    float t[VPL][8];
-#pragma unroll
-    for (int j = 0; j < VPL; ++j)
-#pragma unroll
-      for (int k = 0; k < 8; ++k) t[j][k] = v[j][k];
-    const float mx = tree_fold<VPL, F16>(t, true);
+    mx = warp_max(mx);
     // exp(x - max): the f32 program folds log2(e) into one FMA feeding ex2;
     // the f16 program rounds like NumPy's float16 loops (sub, round, exp, round)
     const float l2e = 1.4426950408889634f;
     const float mx2 = mx * l2e;
+    float t[M][2];
 #pragma unroll
-    for (int j = 0; j < VPL; ++j)
+    for (int m = 0; m < M; ++m)
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < 2; ++k) {
         float x;
         if (f16c) {
-          x = __half2float(__float2half_rn(v[j][k] - mx));
+          x = __half2float(__float2half_rn(v[m][k] - mx));
           x = __half2float(__float2half_rn(expf(x)));
         } else {
-          x = fast_exp2(fmaf(v[j][k], l2e, -mx2));
+          x = fast_exp2(fmaf(v[m][k], l2e, -mx2));
         }
-        v[j][k] = x;
-        t[j][k] = x;
+        v[m][k] = x;
+        t[m][k] = x;
       }
-    const float sum = tree_fold<VPL, F16>(t, false);
+    const float sum = sum_fold<M, F16>(t);
     const float rs = 1.0f / sum;
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      const int64_t e = ob + 256 * j + 8 * lane;
-      __half2 o2[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (f16c)
-          o2[k] = __floats2half2_rn(v[j][2 * k] / sum, v[j][2 * k + 1] / sum);
-        else
-          o2[k] = __floats2half2_rn(v[j][2 * k] * rs, v[j][2 * k + 1] * rs);
-      }
-      if (e >= 0 && e + 8 <= b.numel[d.out.slot]) {
-        *reinterpret_cast<uint4*>(out + e) = *reinterpret_cast<uint4*>(o2);
+    for (int m = 0; m < M; ++m) {
+      const int64_t e = ob + 64 * m + 2 * lane;
+      __half2 o2;
+      if (f16c)
+        o2 = __floats2half2_rn(v[m][0] / sum, v[m][1] / sum);
+      else
+        o2 = __floats2half2_rn(v[m][0] * rs, v[m][1] * rs);
+      if (e >= 0 && e + 2 <= out_numel) {
+        *reinterpret_cast<__half2*>(out + e) = o2;
       } else {
-        const __half* oh = reinterpret_cast<const __half*>(o2);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          if (e + k >= 0 && e + k < b.numel[d.out.slot]) out[e + k] = oh[k];
+        if (e >= 0 && e < out_numel) out[e] = o2.x;
+        if (e + 1 >= 0 && e + 1 < out_numel) out[e + 1] = o2.y;
       }
     }
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) cur[j] = nxt[j];
+    for (int m = 0; m < M; ++m) cur[m] = nxt[m];
   }
 }
 
@@ -294,32 +312,36 @@ extern "C" int ktir_softmax_rows(const KtirSoftmaxDesc* d, const KtirBuffers* bu
                                  const int64_t* unit_table, void* stream) {
   if (!d || !bufs) return set_err(KTIR_ERR_ARG, "ktir_softmax_rows: null descriptor");
   const int n = d->cols;
-  if (n < 256 || (n & (n - 1)) || n > 4096 || d->in.stride[1] != 1 || d->out.stride[1] != 1 ||
+  if (n < 64 || (n & (n - 1)) || n > 4096 || d->in.stride[1] != 1 || d->out.stride[1] != 1 ||
       d->in.dtype != KTIR_F16 || d->out.dtype != KTIR_F16)
-    return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: needs f16 rows of 2^k >= 256 elements");
+    return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: needs f16 rows of 2^k in [64, 4096] elements");
   if (((d->in.off | d->out.off | d->in.stride[0] | d->out.stride[0]) & 7) != 0)
     return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: rows must be 16-byte aligned");
   if ((int64_t)d->n_units * d->rows >= (1ll << 31))
     return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: more than 2^31 rows");
   const int64_t rows = (int64_t)d->n_units * d->rows;
   const int threads = 128;
-  // rows per warp (descriptor's spare field, 0 = default 2)
-  const int rpw = d->pad > 0 ? d->pad : 2;
+  // rows per warp (descriptor's spare field, 0 = default 1)
+  const int rpw = d->pad > 0 ? d->pad : 1;
   const int blocks = grid_x((rows + rpw - 1) / rpw * 32, threads, 1 << 30);
   cudaStream_t s = (cudaStream_t)stream;
 #define KTIR_SOFTMAX_CASE(V)                                                         \
   case V:                                                                            \
     if (d->compute_f16)                                                              \
-      k_softmax_rows<V, true><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table);     \
+      launch_pdl(k_softmax_rows<V, true>, dim3(blocks), dim3(threads), 0, s, *d, *bufs, \
+                 unit_table);                                                        \
     else                                                                             \
-      k_softmax_rows<V, false><<<blocks, threads, 0, s>>>(*d, *bufs, unit_table);    \
+      launch_pdl(k_softmax_rows<V, false>, dim3(blocks), dim3(threads), 0, s, *d, *bufs, \
+                 unit_table);                                                        \
     break;
-  switch (n / 256) {
+  switch (n / 64) {
     KTIR_SOFTMAX_CASE(1)
     KTIR_SOFTMAX_CASE(2)
     KTIR_SOFTMAX_CASE(4)
     KTIR_SOFTMAX_CASE(8)
     KTIR_SOFTMAX_CASE(16)
+    KTIR_SOFTMAX_CASE(32)
+    KTIR_SOFTMAX_CASE(64)
     default: return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: row length");
   }
 #undef KTIR_SOFTMAX_CASE
@@ -342,6 +364,7 @@ __global__ void __launch_bounds__(512) k_rmw_count(const __grid_constant__ KtirG
                                                    int* __restrict__ counts, int64_t n_rows,
                                                    int* __restrict__ status) {
   extern __shared__ long long set[];
+  pdl_prologue();
   int cap = 1;
   while (cap < 2 * d.unit_len) cap <<= 1;
   for (int unit = blockIdx.x; unit < d.n_units; unit += gridDim.x) {
@@ -399,6 +422,7 @@ __global__ void __launch_bounds__(256) k_rmw_apply(const __grid_constant__ KtirG
                                                    const __grid_constant__ KtirBuffers b,
                                                    int* __restrict__ counts, int64_t n_rows,
                                                    float simple_imm) {
+  pdl_prologue();
   const int sub = threadIdx.x & 15;
   const int group = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 4);
   const int ngroups = (int)((gridDim.x * blockDim.x) >> 4);
@@ -476,7 +500,7 @@ extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* d, const KtirBuffers* bu
   const bool do_count = d->phases == 0 || (d->phases & 1);
   const bool do_apply = d->phases == 0 || (d->phases & 2);
   if (do_count) {
-    k_rmw_count<<<d->n_units, 512, smem, s>>>(*d, *bufs, counts, n_rows, status);
+    launch_pdl(k_rmw_count, dim3(d->n_units), dim3(512), smem, s, *d, *bufs, counts, n_rows, status);
     int rc = check_launch("ktir_gather_rmw(count)");
     if (rc) return rc;
   }
@@ -498,10 +522,18 @@ extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* d, const KtirBuffers* bu
   const int64_t groups = (int64_t)d->n_units * d->unit_len;
   const int blocks = grid_x(groups * 16, 256, 148 * 64);
   switch (simple_op) {
-    case OP_FADD: k_rmw_apply<OP_FADD><<<blocks, 256, 0, s>>>(*d, *bufs, counts, n_rows, simple_imm); break;
-    case OP_FSUB: k_rmw_apply<OP_FSUB><<<blocks, 256, 0, s>>>(*d, *bufs, counts, n_rows, simple_imm); break;
-    case OP_FMUL: k_rmw_apply<OP_FMUL><<<blocks, 256, 0, s>>>(*d, *bufs, counts, n_rows, simple_imm); break;
-    default: k_rmw_apply<0><<<blocks, 256, 0, s>>>(*d, *bufs, counts, n_rows, 0.f); break;
+    case OP_FADD:
+      launch_pdl(k_rmw_apply<OP_FADD>, dim3(blocks), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
+      break;
+    case OP_FSUB:
+      launch_pdl(k_rmw_apply<OP_FSUB>, dim3(blocks), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
+      break;
+    case OP_FMUL:
+      launch_pdl(k_rmw_apply<OP_FMUL>, dim3(blocks), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
+      break;
+    default:
+      launch_pdl(k_rmw_apply<0>, dim3(blocks), dim3(256), 0, s, *d, *bufs, counts, n_rows, 0.f);
+      break;
   }
   return check_launch("ktir_gather_rmw(apply)");
 }

@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import os
 from typing import Any, Dict, List, Optional, Tuple
 
 import numpy as np
@@ -45,6 +46,7 @@ class HBMFacade:
 
     def __init__(self) -> None:
         self.allocs: Dict[int, np.ndarray] = {}     # byte address -> flat array
+        self.borrowed: set = set()                  # allocations aliasing caller arrays
         self.next_ptr = 0x10000
 
     def allocate(self, size: int) -> int:
@@ -60,6 +62,13 @@ class HBMFacade:
                 return base, arr
         return None
 
+    def attach(self, stick: int, data: np.ndarray) -> None:
+        """Make `data` the allocation at `stick` without copying it; the façade
+        copies it first if it is ever written through `write`."""
+        addr = stick * STICK
+        self.allocs[addr] = np.ascontiguousarray(data).reshape(-1)
+        self.borrowed.add(addr)
+
     def write(self, stick: int, data: np.ndarray, *, intra_byte: int = 0) -> None:
         addr = stick * STICK + intra_byte
         flat = np.ascontiguousarray(data).reshape(-1)
@@ -68,6 +77,9 @@ class HBMFacade:
             self.allocs[addr] = flat.copy()
             return
         base, arr = found
+        if base in self.borrowed:
+            arr = self.allocs[base] = arr.copy()
+            self.borrowed.discard(base)
         off = (addr - base) // flat.itemsize
         fit = max(0, min(flat.size, arr.size - off))
         arr[off:off + fit] = flat[:fit]
@@ -110,6 +122,8 @@ class Executable:
         self.dev_tensors = None
         self.latency_tape = None
         self.pinned = None
+        self.pinned_np = None
+        self.last_h2d_bytes = self.last_d2h_bytes = 0
         self.bufs = None
         self.arena = None
         if plan.arena_bytes:
@@ -137,6 +151,24 @@ class Executable:
         st = self.status.data_ptr()
         for l in self.plan.launches:
             l.fn(bufs, sp, st)
+
+    def capture(self, tensor_sets: List[List[Any]], stream=None):
+        """Record the plan once per tensor set, in order, into one CUDA graph.
+
+        Replaying the graph runs exactly those executions with a single host
+        launch, for callers that issue many executions back to back (the
+        per-execution host cost of `launch` is then paid once).  Every launch of
+        the plan must already have run once outside capture (one-time kernel
+        attribute setup).  Returns the torch.cuda.CUDAGraph; replay it with
+        `.replay()` on the current stream."""
+        torch = self.torch
+        s = stream if stream is not None else torch.cuda.Stream(self.device)
+        bufs = [self.buffers(ts) for ts in tensor_sets]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for ts, b in zip(tensor_sets, bufs):
+                self.launch(ts, s, b)
+        return g
 
     def check_status(self) -> None:
         if not self.plan.status_check:
@@ -231,7 +263,7 @@ class KTIRInterpreter:
                 if np.dtype(v.dtype) not in _KTIR_OF:
                     raise ValueError(f"No KTIR dtype for NumPy dtype: {v.dtype!r}")
                 stick = hbm.allocate(v.nbytes)
-                hbm.write(stick, v)
+                hbm.attach(stick, v)
                 ptrs[name] = stick
                 dts[name] = _KTIR_OF[np.dtype(v.dtype)]
             else:
@@ -258,7 +290,7 @@ class KTIRInterpreter:
         out = {}
         for name, v in kwargs.items():
             if isinstance(v, np.ndarray):
-                out[name] = hbm.read(ptrs[name], v.size, dts[name]).reshape(v.shape)
+                out[name] = hbm.allocs[ptrs[name] * STICK].reshape(v.shape)
         return out
 
     def estimate_latency(self, func_name: str, **kwargs):
@@ -329,32 +361,86 @@ class KTIRInterpreter:
         return entry
 
     def run_host(self, exe: Executable, order: List[int]) -> None:
-        """Upload every allocation, run the plan, read back what the plan writes.
+        """Upload the allocations, run the plan, read back what the plan writes.
 
-        Device buffers and pinned staging buffers belong to the Executable and
-        are reused by every call with the same signature.
+        Every allocation of the façade is replaced by a new array holding its
+        contents after the call (the caller's input arrays are never written).
+        Host copies run in parallel chunks on a thread pool: into the pinned
+        staging buffers (each chunk's DMA issued as soon as it is staged),
+        out of them after the call, and — overlapped with the device work —
+        the copies of buffers the plan does not write.  Buffers the plan
+        overwrites entirely without reading are not uploaded.  Device and
+        pinned buffers belong to the Executable and are reused by every call
+        with the same signature.
         """
         torch = exe.torch
         hbm = self.memory.hbm
+        pool = _pool()
         if exe.dev_tensors is None:
-            exe.dev_tensors, exe.pinned = [], []
+            exe.dev_tensors, exe.pinned, exe.pinned_np = [], [], []
             for addr in order:
                 nb = hbm.allocs[addr].nbytes
                 exe.dev_tensors.append(torch.empty(nb + 16, dtype=torch.uint8, device=exe.device))
-                exe.pinned.append(torch.empty(nb, dtype=torch.uint8, pin_memory=True))
+                pin = torch.empty(max(nb, 1), dtype=torch.uint8, pin_memory=True)
+                exe.pinned.append(pin)
+                exe.pinned_np.append(pin.numpy()[:nb])
             exe.bufs = exe.buffers(exe.dev_tensors)
         stream = torch.cuda.current_stream(exe.device)
-        for addr, t, pin in zip(order, exe.dev_tensors, exe.pinned):
-            arr = hbm.allocs[addr]
-            pin.numpy()[:] = arr.view(np.uint8)
-            t[:arr.nbytes].copy_(pin, non_blocking=True)
+        written = exe.plan.info.get("written")
+        skip = exe.plan.info.get("overwritten", set())
+        src = [hbm.allocs[a].view(np.uint8).reshape(-1) for a in order]
+        staged = []
+        for i in range(len(order)):
+            if i in skip:
+                continue
+            for a, b in _chunks(src[i].size, _WORKERS):
+                staged.append((i, a, b, pool.submit(np.copyto, exe.pinned_np[i][a:b], src[i][a:b])))
+        h2d = 0
+        for i, a, b, f in staged:
+            f.result()
+            exe.dev_tensors[i][a:b].copy_(exe.pinned[i][a:b], non_blocking=True)
+            h2d += b - a
         exe.status.zero_()
         exe.launch(exe.dev_tensors, stream, exe.bufs)
-        written = exe.plan.info.get("written")
         back = [i for i in range(len(order)) if written is None or i in written]
+        d2h = 0
         for i in back:
-            exe.pinned[i].copy_(exe.dev_tensors[i][:exe.pinned[i].numel()], non_blocking=True)
+            nb = src[i].size
+            exe.pinned[i][:nb].copy_(exe.dev_tensors[i][:nb], non_blocking=True)
+            d2h += nb
+        results = [np.empty(s_.size, np.uint8) for s_ in src]
+        copies = [pool.submit(np.copyto, results[i][a:b], src[i][a:b])
+                  for i in range(len(order)) if i not in back
+                  for a, b in _chunks(src[i].size, _WORKERS)]
         stream.synchronize()
+        for f in copies:
+            f.result()
         exe.check_status()
-        for i in back:
-            hbm.allocs[order[i]].view(np.uint8)[:] = exe.pinned[i].numpy()
+        copies = [pool.submit(np.copyto, results[i][a:b], exe.pinned_np[i][a:b])
+                  for i in back for a, b in _chunks(src[i].size, _WORKERS)]
+        for f in copies:
+            f.result()
+        for i, addr in enumerate(order):
+            hbm.allocs[addr] = results[i].view(hbm.allocs[addr].dtype)
+            hbm.borrowed.add(addr)
+        exe.last_h2d_bytes, exe.last_d2h_bytes = h2d, d2h
+
+
+_WORKERS = max(1, min(16, os.cpu_count() or 1))
+_POOL = None
+
+
+def _pool():
+    """Shared thread pool for host staging copies (NumPy copies release the GIL)."""
+    global _POOL
+    if _POOL is None:
+        from concurrent.futures import ThreadPoolExecutor
+        _POOL = ThreadPoolExecutor(max_workers=_WORKERS, thread_name_prefix="ktir-copy")
+    return _POOL
+
+
+def _chunks(n: int, parts: int, min_chunk: int = 1 << 20) -> List[Tuple[int, int]]:
+    """Split [0, n) into at most `parts` page-aligned chunks of at least min_chunk bytes."""
+    k = max(1, min(parts, n // min_chunk))
+    step = ((-(-n // k)) + 4095) & ~4095
+    return [(a, min(n, a + step)) for a in range(0, n, step)] or [(0, 0)]

@@ -520,7 +520,51 @@ class Lowerer:
             else:
                 written.add(t.buf.index)
         plan.info["written"] = written
+        plan.info["overwritten"] = self._overwritten()
         return plan
+
+    def _overwritten(self) -> set:
+        """Buffers the call never reads and whose every element it stores:
+        their contents before the call cannot show, so they need no upload."""
+        if self.shard is not None:
+            return set()
+        sp = self.trace.space
+        read = set()
+
+        def views_of(iat):
+            for v in [iat.parent] + list(iat.views):
+                b = sp.find(v.byte_address)
+                if b is not None:
+                    read.add(b.index)
+        for n in self.trace.nodes:
+            if n.kind == "load":
+                read.add(n.attrs["buf"].index)
+                if n.attrs["mode"] == "indirect":
+                    views_of(n.attrs["iat"])
+        masks: Dict[int, np.ndarray] = {}
+        for s in self.trace.stores:
+            t = s.target
+            if isinstance(t, IndirectTarget):
+                views_of(t.iat)
+                continue
+            b = t.buf
+            if b.index in read:
+                continue
+            m = masks.get(b.index)
+            if m is None:
+                if b.numel > (1 << 28):
+                    read.add(b.index)
+                    continue
+                m = masks[b.index] = np.zeros(b.numel, dtype=bool)
+            if isinstance(t, RectTarget):
+                offs = np.full((), t.off, np.int64)
+                for n_, st in zip(t.shape, t.strides):
+                    offs = np.add.outer(offs, np.arange(n_, dtype=np.int64) * st)
+                offs = offs.reshape(-1)
+            else:
+                offs = t.off + np.asarray(t.offsets, np.int64)
+            m[offs[(offs >= 0) & (offs < b.numel)]] = True
+        return {i for i, m in masks.items() if i not in read and bool(m.all())}
 
     # -- gather -> f -> scatter ----------------------------------------------------
     def match_gather_rmw(self, stores: List[Store]) -> Optional[Plan]:
@@ -680,7 +724,7 @@ class Lowerer:
                u[1].buf is not t0.buf or u[0].attrs["strides"][0] != ld0.attrs["strides"][0] or
                u[1].strides[0] != t0.strides[0] for u in units):
             return None
-        if cols < 256 or cols & (cols - 1) or cols > 4096:
+        if cols < 64 or cols & (cols - 1) or cols > 4096:
             return None
         items = [([_load_interval(ld)], [_target_interval(t)]) for ld, t in units]
         if not units_independent(items):

@@ -55,3 +55,22 @@ def test_fmha_matches_fp32(bh, seq, causal):
     ref = _reference(q, k, v, bh, seq, scale, causal)
     err = ((o.float() - ref).abs() / ref.abs().clamp_min(1.0)).max().item()
     assert err <= TOL, err
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_fmha_running_max_moves(causal):
+    """Keys whose logits grow along the sequence force the running max (and O, l)
+    to be rescaled many times."""
+    import torch
+    bh, seq = 2, 1024
+    g = torch.Generator(device="cpu").manual_seed(99)
+    q, k, v = (torch.randn(bh * seq, 128, generator=g) for _ in range(3))
+    ramp = 1.0 + 6.0 * torch.arange(seq).repeat(bh).float() / seq
+    k = k * ramp[:, None]
+    q, k, v = q.half().cuda(), k.half().cuda(), v.half().cuda()
+    o = torch.full((bh * seq, 128), float("nan"), dtype=torch.float16, device="cuda")
+    scale = float(1.0 / math.sqrt(128))
+    _fmha(q, k, v, o, bh, seq, scale, causal)
+    ref = _reference(q, k, v, bh, seq, scale, causal)
+    err = ((o.float() - ref).abs() / ref.abs().clamp_min(1.0)).max().item()
+    assert err <= TOL, err

@@ -78,3 +78,13 @@ def test_gemm_uses_tensor_core_plan():
     kw, got, want, dev = _run_both("gemm", **p)
     assert dev.last_executable.plan.kind == "gemm"
     assert_matches("c", got["c_ptr"], want["c_ptr"], 1e-2)
+
+
+@pytest.mark.parametrize("cols", [64, 128, 256, 512, 2048, 4096])
+def test_softmax_row_lengths(cols):
+    """Every row length the fused softmax kernel takes, against the oracle."""
+    kw, got, want, dev = _run_both("softmax", seed=cols, rows=64, cols=cols, grid=2, chunk=16)
+    assert dev.last_executable.plan.kind == "softmax"
+    assert_matches("out", got["out_ptr"], want["out_ptr"], 1e-2)
+    s = got["out_ptr"].astype(np.float64).sum(axis=1)
+    assert np.all(np.abs(s - 1.0) < 1e-2)
