@@ -2,22 +2,26 @@
 //
 // Q, K, V, O are f16 [bh*seq, 128] row-major (one head = seq consecutive
 // rows).  One CTA owns 128 query rows of one head and walks the key blocks of
-// 128 rows with three warp roles that meet only at mbarriers:
-//   warp 4 (TMA)      Q once; K_j and V_j into their own rings (3 K stages,
-//                     2 V stages), each slot refilled as soon as the MMA that
-//                     read it completes
-//   warp 5 (MMA)      S_j = Q K_j^T (M=128 N=128 K=128) into TMEM S buffer
-//                     j & 1, then O += P_{j-1} V_{j-1} with P read straight
-//                     from TMEM (M=128 N=128 K=128); S_j is issued before
+// 64 rows with three warp roles that meet only at mbarriers; two CTAs share
+// an SM, so while one CTA's softmax warps work the other's keep the tensor
+// cores busy:
+//   warp 4 (TMA)      Q once; K_j and V_j into their own 2-stage rings, each
+//                     slot refilled as soon as the MMA that read it completes
+//   warp 5 (MMA)      S_j = Q K_j^T (M=128 N=64 K=128) into TMEM S buffer
+//                     j & 1, then O += P_{j-1} V_{j-1} (M=128 N=128 K=64) with
+//                     P read straight from TMEM; S_j is issued before
 //                     PV_{j-1} so the tensor cores compute S_{j+1} and PV_j
 //                     while the softmax warps work on S_j
 //   warps 0-3         thread t owns query row t = TMEM lane t: tcgen05.ld of
-//                     S_j, masked scaled max, P = 2^(x - m) packed to f16 and
-//                     tcgen05.st into TMEM P buffer j & 1, row sum l
-// TMEM (512 columns): S0 0..127, S1 128..255, O 256..383, P0 384..447,
-// P1 448..511.  The running max m only moves when a row's max exceeds it by
-// more than 2^8; then the softmax warp waits for the previous PV and rescales
-// its O rows in TMEM (warp-uniform), otherwise O and l keep sharing m.
+//                     S_j, masked max of x = s * scale * log2(e), P = 2^(x - m)
+//                     evaluated in f16 pairs (P is f16 in the PV product
+//                     anyway) and tcgen05.st over the first 32 columns of
+//                     S_j's own buffer, row sum l in f32
+// TMEM (256 columns): S0 / P0 0..63, S1 / P1 64..127, O 128..255.  S_{j+2}
+// reuses S_j's buffer only after PV_j (which reads P_j there) has completed.
+// The running max m only moves when a row's max exceeds it by more than 2^8;
+// then the softmax warp waits for the previous PV and rescales its O rows in
+// TMEM (warp-uniform), otherwise O and l keep sharing m.
 // Every wait is bounded; a timed-out wait raises the CTA's abort flag, every
 // role then leaves its loop, and the CTA still frees its TMEM.
 #include <cuda.h>
@@ -34,16 +38,17 @@ namespace {
 
 constexpr int D = 128;          // head dim
 constexpr int BQ = 128;         // query rows per CTA
-constexpr int BKV = 128;        // key rows per block
-constexpr int KST = 3;          // K ring stages
+constexpr int BKV = 64;         // key rows per block
+constexpr int KST = 2;          // K ring stages
 constexpr int VST = 2;          // V ring stages
 constexpr int THREADS = 192;
-constexpr int HALF_BOX = 128 * 64 * 2;          // 16 KiB: 128 rows x 64 columns
-constexpr int TILE_BYTES = 2 * HALF_BOX;        // 32 KiB: 128 rows x 128 columns
-constexpr int SMEM_BYTES = (1 + KST + VST) * TILE_BYTES + 1024;
-constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t O_COL = 256;
-constexpr uint32_t P_COL = 384;
+constexpr int Q_HALF = BQ * 64 * 2;             // 16 KiB: 128 rows x 64 columns
+constexpr int Q_BYTES = 2 * Q_HALF;             // 32 KiB
+constexpr int KV_HALF = BKV * 64 * 2;           // 8 KiB: 64 rows x 64 columns
+constexpr int KV_BYTES = 2 * KV_HALF;           // 16 KiB: 64 rows x 128 columns
+constexpr int SMEM_BYTES = Q_BYTES + (KST + VST) * KV_BYTES + 1024;
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t O_COL = 128;
 constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
 
 struct FmhaParams {
@@ -62,12 +67,20 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x for a pair: x rounded to f16, one MUFU op for both lanes of the pair
+__device__ __forceinline__ uint32_t ex2_pair(float a, float b) {
+  uint32_t h, y;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(h));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, 2)
     k_fmha_tcgen05(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ FmhaParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -90,8 +103,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sQ = base;
-  const uint32_t sK = base + TILE_BYTES;
-  const uint32_t sV = sK + KST * TILE_BYTES;
+  const uint32_t sK = base + Q_BYTES;
+  const uint32_t sV = sK + KST * KV_BYTES;
 
   if (tid == 0) {
     abort_flag = 0;
@@ -127,26 +140,26 @@ __global__ void __launch_bounds__(THREADS, 1)
       tma_prefetch_desc(&tk);
       tma_prefetch_desc(&tv);
       const uint32_t qb = smem_u32(&q_full);
-      mbar_arrive_expect_tx(qb, TILE_BYTES);
+      mbar_arrive_expect_tx(qb, Q_BYTES);
       tma_load_2d(sQ, &tq, qb, 0, (int)row0);
-      tma_load_2d(sQ + HALF_BOX, &tq, qb, 64, (int)row0);
+      tma_load_2d(sQ + Q_HALF, &tq, qb, 64, (int)row0);
       const int kv_row0 = (int)(head * p.seq);
       for (int j = 0; j < n_kv && !*abort; ++j) {
         const int kr = kv_row0 + j * BKV;
         const int ks = j % KST;
         if (j >= KST && !mbar_wait(smem_u32(&k_empty[ks]), ((j / KST) - 1) & 1, abort)) break;
         const uint32_t kf = smem_u32(&k_full[ks]);
-        const uint32_t kb = sK + ks * TILE_BYTES;
-        mbar_arrive_expect_tx(kf, TILE_BYTES);
+        const uint32_t kb = sK + ks * KV_BYTES;
+        mbar_arrive_expect_tx(kf, KV_BYTES);
         tma_load_2d(kb, &tk, kf, 0, kr);
-        tma_load_2d(kb + HALF_BOX, &tk, kf, 64, kr);
+        tma_load_2d(kb + KV_HALF, &tk, kf, 64, kr);
         const int vs = j % VST;
         if (j >= VST && !mbar_wait(smem_u32(&v_empty[vs]), ((j / VST) - 1) & 1, abort)) break;
         const uint32_t vf = smem_u32(&v_full[vs]);
-        const uint32_t vb = sV + vs * TILE_BYTES;
-        mbar_arrive_expect_tx(vf, TILE_BYTES);
+        const uint32_t vb = sV + vs * KV_BYTES;
+        mbar_arrive_expect_tx(vf, KV_BYTES);
         tma_load_2d(vb, &tv, vf, 0, kr);
-        tma_load_2d(vb + HALF_BOX, &tv, vf, 64, kr);
+        tma_load_2d(vb + KV_HALF, &tv, vf, 64, kr);
       }
     }
   } else if (warp == 5) {
@@ -159,12 +172,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int vs = i % VST;
         if (!mbar_wait(smem_u32(&v_full[vs]), (i / VST) & 1, abort)) return false;
         tc_fence_after();
-        const uint32_t vb = sV + vs * TILE_BYTES;
+        const uint32_t vb = sV + vs * KV_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint64_t bd = sdesc_sw128(vb + kk * 16 * 128, HALF_BOX, 1024);
-          mma_f16_ts(tmem + O_COL, tmem + P_COL + (uint32_t)((i & 1) * 64 + kk * 8), bd,
-                     idesc_pv, (i | kk) != 0);
+          const uint64_t bd = sdesc_sw128(vb + kk * 16 * 128, KV_HALF, 1024);
+          mma_f16_ts(tmem + O_COL, tmem + (uint32_t)((i & 1) * BKV + kk * 8), bd, idesc_pv,
+                     (i | kk) != 0);
         }
         mma_commit(smem_u32(&pv_done[i & 1]));
         mma_commit(smem_u32(&v_empty[vs]));
@@ -174,16 +187,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; ok && j < n_kv; ++j) {
         const int ks = j % KST;
         if (!mbar_wait(smem_u32(&k_full[ks]), (j / KST) & 1, abort)) break;
-        // S buffer j & 1 was last read by softmax j - 2
-        if (j >= 2 && !mbar_wait(smem_u32(&p_full[j & 1]), ((j - 2) >> 1) & 1, abort)) break;
+        // S buffer j & 1 holds P_{j-2} until PV_{j-2} has completed
+        if (j >= 2 && !mbar_wait(smem_u32(&pv_done[j & 1]), ((j - 2) >> 1) & 1, abort)) break;
         tc_fence_after();
-        const uint32_t kb = sK + ks * TILE_BYTES;
+        const uint32_t kb = sK + ks * KV_BYTES;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t chunk = kk >> 2;
           const uint32_t koff = (kk & 3) * 32;
-          const uint64_t ad = sdesc_sw128(sQ + chunk * HALF_BOX + koff, 16, 1024);
-          const uint64_t bd = sdesc_sw128(kb + chunk * HALF_BOX + koff, 16, 1024);
+          const uint64_t ad = sdesc_sw128(sQ + chunk * Q_HALF + koff, 16, 1024);
+          const uint64_t bd = sdesc_sw128(kb + chunk * KV_HALF + koff, 16, 1024);
           mma_f16(tmem + (uint32_t)((j & 1) * BKV), ad, bd, idesc_s, kk != 0);
         }
         mma_commit(smem_u32(&s_full[j & 1]));
@@ -213,14 +226,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const int kpos0 = j * BKV;
       const bool diag = p.causal && kpos0 + BKV - 1 > q0;
+      if (diag) {
+#pragma unroll
+        for (int i = 0; i < BKV; ++i)
+          if (kpos0 + i > qpos) sv[i] = -INFINITY;
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < BKV; ++i) {
-        float x = sv[i] * p.scale_log2;
-        if (diag && kpos0 + i > qpos) x = -INFINITY;
-        sv[i] = x;
-        mx = fmaxf(mx, x);
-      }
+      for (int i = 0; i < BKV; ++i) mx = fmaxf(mx, sv[i]);
+      mx *= p.scale_log2;
       const float m_new = fmaxf(m_used, mx);
       float factor = 1.f;
       bool rescale = false;
@@ -231,49 +245,33 @@ __global__ void __launch_bounds__(THREADS, 1)
         m_used = m_new;
       }
       const float msub = (m_used == -INFINITY) ? 0.f : m_used;
-      float psum = 0.f;
       uint32_t ph[BKV / 2];
+      float psum = 0.f;
 #pragma unroll
       for (int i = 0; i < BKV; i += 2) {
-        const float a = ex2(sv[i] - msub);
-        const float b = ex2(sv[i + 1] - msub);
-        psum += a + b;
-        ph[i / 2] = pack_h2(a, b);
+        ph[i / 2] = ex2_pair(fmaf(sv[i], p.scale_log2, -msub), fmaf(sv[i + 1], p.scale_log2, -msub));
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ph[i / 2]));
+        psum += f.x + f.y;
       }
       l_run += psum;
-      // O rows move only when PV_{j-1} has landed; P buffer j & 1 is free once
-      // PV_{j-2} has read it
-      bool ok = true;
+      // O rows move only when PV_{j-1} has landed
       if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(smem_u32(&pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, abort));
+        const bool ok = __all_sync(
+            0xffffffffu, mbar_wait(smem_u32(&pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, abort));
         tc_fence_after();
-        if (ok) {
+        if (!ok) break;
 #pragma unroll 1
-          for (int c = 0; c < D; c += 32) {
-            uint32_t r[32];
-            tmem_ld32(tmem + lane_base + O_COL + c, r);
-            tmem_ld_wait();
+        for (int c = 0; c < D; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + O_COL + c, r);
+          tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-            tmem_st32(tmem + lane_base + O_COL + c, r);
-          }
-        }
-      } else if (j >= 2) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(smem_u32(&pv_done[j & 1]), ((j - 2) >> 1) & 1, abort));
-        tc_fence_after();
-      }
-      if (!ok) break;
-      {
-        uint32_t r[32];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = ph[32 * h + i];
-          tmem_st32(tmem + lane_base + P_COL + (uint32_t)((j & 1) * 64 + 32 * h), r);
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+          tmem_st32(tmem + lane_base + O_COL + c, r);
         }
       }
+      // P_j over the first 32 columns of S_j's buffer (already read above)
+      tmem_st32(tmem + lane_base + (uint32_t)((j & 1) * BKV), ph);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(smem_u32(&p_full[j & 1]));
@@ -345,7 +343,9 @@ bool make_map(CUtensorMap* m, const void* base, long long rows, long long ld, in
 
 extern "C" int ktir_fmha_f16(const KtirFmhaDesc* d, void* stream) {
   if (!d || !d->q || !d->k || !d->v || !d->o || !d->status) return KTIR_ERR_ARG;
-  if (d->d != D || d->seq % BQ || d->bh < 1 || d->row_stride < D || (d->row_stride & 7))
+  // the row max is taken before scaling, which needs a positive scale
+  if (d->d != D || d->seq % BQ || d->bh < 1 || d->row_stride < D || (d->row_stride & 7) ||
+      !(d->scale > 0.f))
     return KTIR_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(d->q) | reinterpret_cast<uintptr_t>(d->k) |
        reinterpret_cast<uintptr_t>(d->v) | reinterpret_cast<uintptr_t>(d->o)) & 15)

@@ -372,7 +372,7 @@ def match_attention_plan(low, stores):
                 return None
             seq = seq_u
         seen.add(qrow)
-    if seq is None or seq % 128 or rows % seq:
+    if seq is None or seq % 128 or rows % seq or not scale > 0:
         return None
     # the units must cover whole heads [h_lo, h_hi) (all heads, or a shard's)
     heads = sorted({q // seq for q in seen})
