@@ -231,10 +231,17 @@ __global__ void __launch_bounds__(THREADS, 2)
         for (int i = 0; i < BKV; ++i)
           if (kpos0 + i > qpos) sv[i] = -INFINITY;
       }
-      float mx = -INFINITY;
+      // eight independent partial maxima / sums keep the dependency chains short
+      float m8[8];
 #pragma unroll
-      for (int i = 0; i < BKV; ++i) mx = fmaxf(mx, sv[i]);
-      mx *= p.scale_log2;
+      for (int i = 0; i < 8; ++i) m8[i] = sv[i];
+#pragma unroll
+      for (int i = 8; i < BKV; ++i) m8[i & 7] = fmaxf(m8[i & 7], sv[i]);
+#pragma unroll
+      for (int h = 4; h >= 1; h >>= 1)
+#pragma unroll
+        for (int i = 0; i < h; ++i) m8[i] = fmaxf(m8[i], m8[i + h]);
+      const float mx = m8[0] * p.scale_log2;
       const float m_new = fmaxf(m_used, mx);
       float factor = 1.f;
       bool rescale = false;
@@ -246,14 +253,20 @@ __global__ void __launch_bounds__(THREADS, 2)
       }
       const float msub = (m_used == -INFINITY) ? 0.f : m_used;
       uint32_t ph[BKV / 2];
-      float psum = 0.f;
+      float s8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s8[i] = 0.f;
 #pragma unroll
       for (int i = 0; i < BKV; i += 2) {
         ph[i / 2] = ex2_pair(fmaf(sv[i], p.scale_log2, -msub), fmaf(sv[i + 1], p.scale_log2, -msub));
         const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ph[i / 2]));
-        psum += f.x + f.y;
+        s8[(i / 2) & 7] += f.x + f.y;
       }
-      l_run += psum;
+#pragma unroll
+      for (int h = 4; h >= 1; h >>= 1)
+#pragma unroll
+        for (int i = 0; i < h; ++i) s8[i] += s8[i + h];
+      l_run += s8[0];
       // O rows move only when PV_{j-1} has landed
       if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
         const bool ok = __all_sync(

@@ -3,14 +3,19 @@
 // lay them out: A is consumed K-major, B is consumed MN-major (no transpose
 // pass over B).
 //
-// One CTA computes a 128x256 tile of C:
+// Persistent: one CTA per SM walks 128x256 output tiles (tile t, t + grid,
+// ...).  The accumulator is double-buffered in TMEM (2 x 256 columns), so the
+// epilogue of one tile overlaps the main loop of the next:
 //   warp 0      one thread issues TMA loads: A box 64(k) x 128(m), four B
 //               boxes 64(n) x 64(k), 128-byte swizzle, into a 4-stage ring
-//   warp 1      allocates 256 TMEM columns; one thread issues tcgen05.mma
-//               (M=128, N=256, K=16) four times per 64-wide k step and
-//               commits each stage back to the producer
+//               that runs continuously across tiles
+//   warp 1      allocates 512 TMEM columns; one thread issues tcgen05.mma
+//               (M=128, N=256, K=16) four times per 64-wide k step into the
+//               tile's accumulator buffer, commits each stage back to the
+//               producer and the finished accumulator to the epilogue
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, convert
-//               to f16, 128-bit stores
+//               to f16, 128-bit stores; the accumulator buffer is handed back
+//               to the MMA warp as soon as the last column is read
 // Every wait is bounded (tc_common.cuh); a wait that runs out raises
 // KTIR_STATUS_TIMEOUT in the caller's status word instead of hanging.
 #include <cuda.h>
@@ -31,7 +36,7 @@ constexpr int B_BOX_BYTES = 64 * BK * 2;        // 8 KiB per 64-column box
 constexpr int B_BYTES = BK * BN * 2;            // 32 KiB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KiB
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
-constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TMEM_COLS = 512;             // two 256-column accumulators
 
 struct GemmParams {
   __half* c;
@@ -47,7 +52,8 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t acc_bar;
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -55,8 +61,8 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t smem = (raw + 1023u) & ~1023u;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM;
-  const int n0 = blockIdx.x * BN;
+  const int MT = p.m / BM;
+  const int n_tiles = MT * (p.n / BN);
   const int KT = p.k / BK;
   volatile int* abort = &abort_flag;
 
@@ -66,7 +72,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(smem_u32(&full_bar[s]), 1);
       mbar_init(smem_u32(&empty_bar[s]), 1);
     }
-    mbar_init(smem_u32(&acc_bar), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), 128);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -82,68 +91,93 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       tma_prefetch_desc(&ta);
       tma_prefetch_desc(&tb);
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
-        if (!mbar_wait(smem_u32(&empty_bar[s]), ph ^ 1, abort)) break;
-        const uint32_t fb = smem_u32(&full_bar[s]);
-        mbar_arrive_expect_tx(fb, STAGE_BYTES);
-        const uint32_t a_dst = smem + s * STAGE_BYTES;
-        const uint32_t b_dst = a_dst + A_BYTES;
-        tma_load_2d(a_dst, &ta, fb, kt * BK, m0);
+      uint32_t g = 0;   // k steps issued so far, across tiles
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+        const int m0 = (t % MT) * BM;
+        const int n0 = (t / MT) * BN;
+        for (int kt = 0; kt < KT; ++kt, ++g) {
+          const int s = g % STAGES;
+          if (!mbar_wait(smem_u32(&empty_bar[s]), ((g / STAGES) & 1) ^ 1, abort)) break;
+          const uint32_t fb = smem_u32(&full_bar[s]);
+          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          const uint32_t a_dst = smem + s * STAGE_BYTES;
+          const uint32_t b_dst = a_dst + A_BYTES;
+          tma_load_2d(a_dst, &ta, fb, kt * BK, m0);
 #pragma unroll
-        for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * B_BOX_BYTES, &tb, fb, n0 + 64 * j, kt * BK);
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(b_dst + j * B_BOX_BYTES, &tb, fb, n0 + 64 * j, kt * BK);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(BM, BN, 0, 1);
-      bool ok = true;
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
-        if (!mbar_wait(smem_u32(&full_bar[s]), ph, abort)) {
-          ok = false;
-          break;
-        }
+      uint32_t g = 0;
+      int i = 0;   // local tile count
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++i) {
+        const int b = i & 1;
+        // accumulator b was last drained by the epilogue of local tile i - 2
+        if (i >= 2 && !mbar_wait(smem_u32(&acc_empty[b]), ((i - 2) >> 1) & 1, abort)) break;
         tc_fence_after();
-        const uint32_t a_addr = smem + s * STAGE_BYTES;
-        const uint32_t b_addr = a_addr + A_BYTES;
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
+        bool ok = true;
+        for (int kt = 0; kt < KT; ++kt, ++g) {
+          const int s = g % STAGES;
+          if (!mbar_wait(smem_u32(&full_bar[s]), (g / STAGES) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem + s * STAGE_BYTES;
+          const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          // A: K-major, 16 k = 32 bytes further along each 128-byte row
-          const uint64_t ad = sdesc_sw128(a_addr + kk * 32, 16, 1024);
-          // B: MN-major, 16 k = 16 rows of 128 bytes further; 64-column
-          // groups 8 KiB apart (LBO), 8-row groups 1 KiB apart (SBO)
-          const uint64_t bd = sdesc_sw128(b_addr + kk * 16 * 128, B_BOX_BYTES, 1024);
-          mma_f16(tmem, ad, bd, idesc, (kt | kk) != 0);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // A: K-major, 16 k = 32 bytes further along each 128-byte row
+            const uint64_t ad = sdesc_sw128(a_addr + kk * 32, 16, 1024);
+            // B: MN-major, 16 k = 16 rows of 128 bytes further; 64-column
+            // groups 8 KiB apart (LBO), 8-row groups 1 KiB apart (SBO)
+            const uint64_t bd = sdesc_sw128(b_addr + kk * 16 * 128, B_BOX_BYTES, 1024);
+            mma_f16(acc, ad, bd, idesc, (kt | kk) != 0);
+          }
+          mma_commit(smem_u32(&empty_bar[s]));
         }
-        mma_commit(smem_u32(&empty_bar[s]));
+        if (!ok) break;
+        mma_commit(smem_u32(&acc_full[b]));
       }
-      if (ok) mma_commit(smem_u32(&acc_bar));
     }
   } else {
     // epilogue warps 2..5: warp w reads TMEM lanes 32*(w%4) .. +31
-    const bool ok = mbar_wait(smem_u32(&acc_bar), 0, abort);
-    tc_fence_after();
-    if (ok) {
-      const int q = warp & 3;
-      const int row = 32 * q + lane;
+    const int q = warp & 3;
+    const int row = 32 * q + lane;
+    const float z = p.add_zero ? 0.0f : -0.0f;
+    int i = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
+      const int b = i & 1;
+      const bool ok = mbar_wait(smem_u32(&acc_full[b]), (i >> 1) & 1, abort);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int m0 = (t % MT) * BM;
+      const int n0 = (t / MT) * BN;
       __half* crow = p.c + (long long)(m0 + row) * p.ldc + n0;
-      const float z = p.add_zero ? 0.0f : -0.0f;
+      const uint32_t acc = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BN);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + c, r);
+        tmem_ld32(acc + c, r);
         tmem_ld_wait();
+        if (c + 32 == BN) {
+          // every column of this accumulator is in registers: hand it back
+          tc_fence_before();
+          mbar_arrive(smem_u32(&acc_empty[b]));
+        }
         __half2 h[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          h[i] = __floats2half2_rn(__uint_as_float(r[2 * i]) + z, __uint_as_float(r[2 * i + 1]) + z);
+        for (int j = 0; j < 16; ++j)
+          h[j] = __floats2half2_rn(__uint_as_float(r[2 * j]) + z, __uint_as_float(r[2 * j + 1]) + z);
         uint4* dst = reinterpret_cast<uint4*>(crow + c);
         const uint4* src = reinterpret_cast<const uint4*>(h);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = src[i];
+        for (int j = 0; j < 4; ++j) dst[j] = src[j];
       }
     }
   }
@@ -221,7 +255,16 @@ extern "C" int ktir_gemm_f16(const KtirGemmDesc* d, void* stream) {
   p.k = (int)d->k;
   p.add_zero = d->add_zero;
   p.status = static_cast<int*>(d->status);
-  dim3 grid((unsigned)(d->n / BN), (unsigned)(d->m / BM));
+  static int n_sm = 0;
+  if (!n_sm) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm < 1)
+      return KTIR_ERR_CUDA;
+  }
+  const long long tiles = (d->m / BM) * (d->n / BN);
+  if (tiles > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
+  const unsigned grid = (unsigned)(tiles < n_sm ? tiles : n_sm);
   k_gemm_tcgen05<<<grid, 192, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   return cudaGetLastError() == cudaSuccess ? KTIR_OK : KTIR_ERR_CUDA;
 }
