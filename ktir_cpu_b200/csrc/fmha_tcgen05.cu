@@ -5,8 +5,9 @@
 // 64 rows with three warp roles that meet only at mbarriers; two CTAs share
 // an SM, so while one CTA's softmax warps work the other's keep the tensor
 // cores busy:
-//   warp 4 (TMA)      Q once; K_j and V_j into their own 2-stage rings, each
-//                     slot refilled as soon as the MMA that read it completes
+//   warps 4, 6 (TMA)  warp 4 loads Q once and K_j, warp 6 loads V_j, each into
+//                     its own 2-stage ring, every slot refilled as soon as the
+//                     MMA that read it completes
 //   warp 5 (MMA)      S_j = Q K_j^T (M=128 N=64 K=128) into TMEM S buffer
 //                     j & 1, then O += P_{j-1} V_{j-1} (M=128 N=128 K=64) with
 //                     P read straight from TMEM; S_j is issued before
@@ -16,7 +17,7 @@
 //                     S_j, masked max of x = s * scale * log2(e), P = 2^(x - m)
 //                     evaluated in f16 pairs (P is f16 in the PV product
 //                     anyway) and tcgen05.st over the first 32 columns of
-//                     S_j's own buffer, row sum l in f32
+//                     S_j's own buffer, row sum l from f16 pair partials
 // TMEM (256 columns): S0 / P0 0..63, S1 / P1 64..127, O 128..255.  S_{j+2}
 // reuses S_j's buffer only after PV_j (which reads P_j there) has completed.
 // The running max m only moves when a row's max exceeds it by more than 2^8;
@@ -41,7 +42,7 @@ constexpr int BQ = 128;         // query rows per CTA
 constexpr int BKV = 64;         // key rows per block
 constexpr int KST = 2;          // K ring stages
 constexpr int VST = 2;          // V ring stages
-constexpr int THREADS = 192;
+constexpr int THREADS = 224;
 constexpr int Q_HALF = BQ * 64 * 2;             // 16 KiB: 128 rows x 64 columns
 constexpr int Q_BYTES = 2 * Q_HALF;             // 32 KiB
 constexpr int KV_HALF = BKV * 64 * 2;           // 8 KiB: 64 rows x 64 columns
@@ -133,33 +134,35 @@ __global__ void __launch_bounds__(THREADS, 2)
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  if (warp == 4) {
-    // ---------------- TMA producer ----------------
+  if (warp == 4 || warp == 6) {
+    // ---------------- TMA producers: warp 4 Q and K, warp 6 V ----------------
     if (lane == 0) {
-      tma_prefetch_desc(&tq);
-      tma_prefetch_desc(&tk);
-      tma_prefetch_desc(&tv);
-      const uint32_t qb = smem_u32(&q_full);
-      mbar_arrive_expect_tx(qb, Q_BYTES);
-      tma_load_2d(sQ, &tq, qb, 0, (int)row0);
-      tma_load_2d(sQ + Q_HALF, &tq, qb, 64, (int)row0);
+      const bool is_k = warp == 4;
       const int kv_row0 = (int)(head * p.seq);
+      if (is_k) {
+        tma_prefetch_desc(&tq);
+        tma_prefetch_desc(&tk);
+        const uint32_t qb = smem_u32(&q_full);
+        mbar_arrive_expect_tx(qb, Q_BYTES);
+        tma_load_2d(sQ, &tq, qb, 0, (int)row0);
+        tma_load_2d(sQ + Q_HALF, &tq, qb, 64, (int)row0);
+      } else {
+        tma_prefetch_desc(&tv);
+      }
+      const CUtensorMap* map = is_k ? &tk : &tv;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      const int stages = is_k ? KST : VST;
+      const uint32_t ring = is_k ? sK : sV;
       for (int j = 0; j < n_kv && !*abort; ++j) {
         const int kr = kv_row0 + j * BKV;
-        const int ks = j % KST;
-        if (j >= KST && !mbar_wait(smem_u32(&k_empty[ks]), ((j / KST) - 1) & 1, abort)) break;
-        const uint32_t kf = smem_u32(&k_full[ks]);
-        const uint32_t kb = sK + ks * KV_BYTES;
-        mbar_arrive_expect_tx(kf, KV_BYTES);
-        tma_load_2d(kb, &tk, kf, 0, kr);
-        tma_load_2d(kb + KV_HALF, &tk, kf, 64, kr);
-        const int vs = j % VST;
-        if (j >= VST && !mbar_wait(smem_u32(&v_empty[vs]), ((j / VST) - 1) & 1, abort)) break;
-        const uint32_t vf = smem_u32(&v_full[vs]);
-        const uint32_t vb = sV + vs * KV_BYTES;
-        mbar_arrive_expect_tx(vf, KV_BYTES);
-        tma_load_2d(vb, &tv, vf, 0, kr);
-        tma_load_2d(vb + KV_HALF, &tv, vf, 64, kr);
+        const int st = j % stages;
+        if (j >= stages && !mbar_wait(smem_u32(&empty[st]), ((j / stages) - 1) & 1, abort)) break;
+        const uint32_t fb = smem_u32(&full[st]);
+        const uint32_t dst = ring + st * KV_BYTES;
+        mbar_arrive_expect_tx(fb, KV_BYTES);
+        tma_load_2d(dst, map, fb, 0, kr);
+        tma_load_2d(dst + KV_HALF, map, fb, 64, kr);
       }
     }
   } else if (warp == 5) {
@@ -253,14 +256,21 @@ __global__ void __launch_bounds__(THREADS, 2)
       }
       const float msub = (m_used == -INFINITY) ? 0.f : m_used;
       uint32_t ph[BKV / 2];
-      float s8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) s8[i] = 0.f;
+      // the row sum adds P in f16 pairs four at a time (each P <= 2^8, so a
+      // partial stays below 2^11 and keeps 2^-11 relative precision), then
+      // in f32
+      __half2 h8[8];
 #pragma unroll
       for (int i = 0; i < BKV; i += 2) {
         ph[i / 2] = ex2_pair(fmaf(sv[i], p.scale_log2, -msub), fmaf(sv[i + 1], p.scale_log2, -msub));
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ph[i / 2]));
-        s8[(i / 2) & 7] += f.x + f.y;
+        const __half2 v2 = *reinterpret_cast<const __half2*>(&ph[i / 2]);
+        h8[(i / 2) & 7] = (i < 16) ? v2 : __hadd2(h8[(i / 2) & 7], v2);
+      }
+      float s8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 f = __half22float2(h8[i]);
+        s8[i] = f.x + f.y;
       }
 #pragma unroll
       for (int h = 4; h >= 1; h >>= 1)

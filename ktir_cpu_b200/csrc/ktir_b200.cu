@@ -258,15 +258,19 @@ __global__ void __launch_bounds__(128) k_softmax_rows(const __grid_constant__ Kt
     if (nrow < total_rows) load_row<M>(in, in_numel, in_base(nrow), lane, nxt);
     const int64_t ob = out_base(row);
     float v[M][2];
-    float mx = -INFINITY;
+    float pm[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&cur[m]));
       v[m][0] = f.x;
       v[m][1] = f.y;
-      mx = fmaxf(mx, fmaxf(f.x, f.y));
+      pm[m] = fmaxf(f.x, f.y);
     }
-    mx = warp_max(mx);
+#pragma unroll
+    for (int h = M / 2; h >= 1; h >>= 1)
+#pragma unroll
+      for (int m = 0; m < h; ++m) pm[m] = fmaxf(pm[m], pm[m + h]);
+    const float mx = warp_max(pm[0]);
     // exp(x - max): the f32 program folds log2(e) into one FMA feeding ex2;
     // the f16 program rounds like NumPy's float16 loops (sub, round, exp, round)
     const float l2e = 1.4426950408889634f;
@@ -444,7 +448,9 @@ __global__ void __launch_bounds__(256) k_rmw_apply(const __grid_constant__ KtirG
     const int64_t row = read_index(b, d.idx_slot, d.idx_dtype, pos);
     int m = 0;
     if (sub == 0 && row >= 0 && row < n_rows) m = atomicExch(&counts[row], 0);
-    m = __shfl_sync(0xffffffffu, m, (threadIdx.x & 31) & ~15);
+    // the 16 lanes of this position's group (the other half-warp may be on
+    // a different trip of the loop)
+    m = __shfl_sync(0xffffu << (threadIdx.x & 16), m, 0, 16);
     // rows owned by another shard are consumed (counts stay zero) but not applied
     if (m <= 0 || row < row_lo || row >= row_hi) continue;
     const int64_t rb = d.table_off + row * d.row_stride;
