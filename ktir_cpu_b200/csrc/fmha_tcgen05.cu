@@ -9,20 +9,23 @@
 //                     its own 2-stage ring, every slot refilled as soon as the
 //                     MMA that read it completes
 //   warp 5 (MMA)      S_j = Q K_j^T (M=128 N=64 K=128) into TMEM S buffer
-//                     j & 1, then O += P_{j-1} V_{j-1} (M=128 N=128 K=64) with
-//                     P read straight from TMEM; S_j is issued before
-//                     PV_{j-1} so the tensor cores compute S_{j+1} and PV_j
-//                     while the softmax warps work on S_j
+//                     j & 1; as soon as the softmax warps hand over P_j it
+//                     issues O += P_j V_j (M=128 N=128 K=64) and S_{j+2} into
+//                     the buffer S_j has just left, so the next two S blocks
+//                     are always computed ahead of the softmax
 //   warps 0-3         thread t owns query row t = TMEM lane t: tcgen05.ld of
 //                     S_j, masked max of x = s * scale * log2(e), P = 2^(x - m)
 //                     evaluated in f16 pairs (P is f16 in the PV product
-//                     anyway) and tcgen05.st over the first 32 columns of
-//                     S_j's own buffer, row sum l from f16 pair partials
-// TMEM (256 columns): S0 / P0 0..63, S1 / P1 64..127, O 128..255.  S_{j+2}
-// reuses S_j's buffer only after PV_j (which reads P_j there) has completed.
-// The running max m only moves when a row's max exceeds it by more than 2^8;
-// then the softmax warp waits for the previous PV and rescales its O rows in
-// TMEM (warp-uniform), otherwise O and l keep sharing m.
+//                     anyway), written as one 128-byte swizzled row of the P
+//                     tile in shared memory; row sum l from f16 pair partials
+// TMEM (256 columns): S0 0..63, S1 64..127, O 128..255.  The running max m
+// only moves when a row's max exceeds it by more than 2^8; then the softmax
+// warp waits for the previous PV and rescales its O rows in TMEM
+// (warp-uniform), otherwise O and l keep sharing m.
+// Shared memory (Q, K and V rings, P, mbarriers) fills exactly half an SM, so
+// the dynamic allocation keeps only 896 bytes for aligning the tiles to the
+// 1024 bytes the 128-byte swizzle needs; a CTA whose window cannot be aligned
+// within that reports KTIR_STATUS_TIMEOUT and does nothing.
 // Every wait is bounded; a timed-out wait raises the CTA's abort flag, every
 // role then leaves its loop, and the CTA still frees its TMEM.
 #include <cuda.h>
@@ -47,7 +50,22 @@ constexpr int Q_HALF = BQ * 64 * 2;             // 16 KiB: 128 rows x 64 columns
 constexpr int Q_BYTES = 2 * Q_HALF;             // 32 KiB
 constexpr int KV_HALF = BKV * 64 * 2;           // 8 KiB: 64 rows x 64 columns
 constexpr int KV_BYTES = 2 * KV_HALF;           // 16 KiB: 64 rows x 128 columns
-constexpr int SMEM_BYTES = Q_BYTES + (KST + VST) * KV_BYTES + 1024;
+constexpr int P_BYTES = BQ * BKV * 2;           // 16 KiB: 128 rows x 64 keys
+constexpr int TILE_BYTES = Q_BYTES + (KST + VST) * KV_BYTES + P_BYTES;
+constexpr int ALIGN_SLACK = 896;
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[KST], k_empty[KST];
+  uint64_t v_full[VST], v_empty[VST];
+  uint64_t s_full[2];
+  uint64_t p_full, pv_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr int SMEM_BYTES = TILE_BYTES + (int)sizeof(Bars) + ALIGN_SLACK;
+static_assert(2 * (SMEM_BYTES + 1024) <= 228 * 1024, "two CTAs per SM");
+
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t O_COL = 128;
 constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
@@ -76,6 +94,13 @@ __device__ __forceinline__ uint32_t ex2_pair(float a, float b) {
   return y;
 }
 
+// three-input max (NaN inputs ignored, like fmaxf)
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -85,54 +110,52 @@ __global__ void __launch_bounds__(THREADS, 2)
     k_fmha_tcgen05(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ FmhaParams p) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full;
-  __shared__ __align__(8) uint64_t k_full[KST], k_empty[KST];
-  __shared__ __align__(8) uint64_t v_full[VST], v_empty[VST];
-  __shared__ __align__(8) uint64_t s_full[2], p_full[2], pv_done[2];
-  __shared__ uint32_t tmem_base;
-  __shared__ int abort_flag;
-  volatile int* abort = &abort_flag;
-
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  if (base - raw > (uint32_t)ALIGN_SLACK) {
+    if (tid == 0) atomicOr(p.status, KTIR_STATUS_TIMEOUT);
+    return;   // uniform: every thread sees the same window
+  }
+  const uint32_t sQ = base;
+  const uint32_t sK = base + Q_BYTES;
+  const uint32_t sV = sK + KST * KV_BYTES;
+  const uint32_t sP = sV + VST * KV_BYTES;
+  Bars& B = *reinterpret_cast<Bars*>(smem_raw + (base - raw) + TILE_BYTES);
+  volatile int* abort = &B.abort_flag;
+
   const int qt = p.n_qtiles - 1 - (int)blockIdx.x;   // heaviest query tiles first
   const long long head = blockIdx.y;
   const long long row0 = head * p.seq + (long long)qt * BQ;
   const int q0 = qt * BQ;
   const int n_kv = p.causal ? (q0 + BQ) / BKV : (int)(p.seq / BKV);
 
-  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t sQ = base;
-  const uint32_t sK = base + Q_BYTES;
-  const uint32_t sV = sK + KST * KV_BYTES;
-
   if (tid == 0) {
-    abort_flag = 0;
-    mbar_init(smem_u32(&q_full), 1);
+    B.abort_flag = 0;
+    mbar_init(smem_u32(&B.q_full), 1);
     for (int s = 0; s < KST; ++s) {
-      mbar_init(smem_u32(&k_full[s]), 1);
-      mbar_init(smem_u32(&k_empty[s]), 1);
+      mbar_init(smem_u32(&B.k_full[s]), 1);
+      mbar_init(smem_u32(&B.k_empty[s]), 1);
     }
     for (int s = 0; s < VST; ++s) {
-      mbar_init(smem_u32(&v_full[s]), 1);
-      mbar_init(smem_u32(&v_empty[s]), 1);
+      mbar_init(smem_u32(&B.v_full[s]), 1);
+      mbar_init(smem_u32(&B.v_empty[s]), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&s_full[b]), 1);
-      mbar_init(smem_u32(&p_full[b]), BQ);
-      mbar_init(smem_u32(&pv_done[b]), 1);
-    }
+    for (int b = 0; b < 2; ++b) mbar_init(smem_u32(&B.s_full[b]), 1);
+    mbar_init(smem_u32(&B.p_full), BQ);
+    mbar_init(smem_u32(&B.pv_done), 1);
     fence_barrier_init();
   }
   if (warp == 0) {
-    tmem_alloc(smem_u32(&tmem_base), TMEM_COLS);
+    tmem_alloc(smem_u32(&B.tmem_base), TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = tmem_base;
+  const uint32_t tmem = B.tmem_base;
 
   if (warp == 4 || warp == 6) {
     // ---------------- TMA producers: warp 4 Q and K, warp 6 V ----------------
@@ -142,7 +165,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       if (is_k) {
         tma_prefetch_desc(&tq);
         tma_prefetch_desc(&tk);
-        const uint32_t qb = smem_u32(&q_full);
+        const uint32_t qb = smem_u32(&B.q_full);
         mbar_arrive_expect_tx(qb, Q_BYTES);
         tma_load_2d(sQ, &tq, qb, 0, (int)row0);
         tma_load_2d(sQ + Q_HALF, &tq, qb, 64, (int)row0);
@@ -150,8 +173,8 @@ __global__ void __launch_bounds__(THREADS, 2)
         tma_prefetch_desc(&tv);
       }
       const CUtensorMap* map = is_k ? &tk : &tv;
-      uint64_t* full = is_k ? k_full : v_full;
-      uint64_t* empty = is_k ? k_empty : v_empty;
+      uint64_t* full = is_k ? B.k_full : B.v_full;
+      uint64_t* empty = is_k ? B.k_empty : B.v_empty;
       const int stages = is_k ? KST : VST;
       const uint32_t ring = is_k ? sK : sV;
       for (int j = 0; j < n_kv && !*abort; ++j) {
@@ -169,29 +192,10 @@ __global__ void __launch_bounds__(THREADS, 2)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(BQ, BKV, 0, 0);   // Q, K both K-major
-      constexpr uint32_t idesc_pv = idesc_f16(BQ, D, 0, 1);    // P (TMEM) K-major, V MN-major
-      auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(smem_u32(&p_full[i & 1]), (i >> 1) & 1, abort)) return false;
-        const int vs = i % VST;
-        if (!mbar_wait(smem_u32(&v_full[vs]), (i / VST) & 1, abort)) return false;
-        tc_fence_after();
-        const uint32_t vb = sV + vs * KV_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint64_t bd = sdesc_sw128(vb + kk * 16 * 128, KV_HALF, 1024);
-          mma_f16_ts(tmem + O_COL, tmem + (uint32_t)((i & 1) * BKV + kk * 8), bd, idesc_pv,
-                     (i | kk) != 0);
-        }
-        mma_commit(smem_u32(&pv_done[i & 1]));
-        mma_commit(smem_u32(&v_empty[vs]));
-        return true;
-      };
-      bool ok = mbar_wait(smem_u32(&q_full), 0, abort);
-      for (int j = 0; ok && j < n_kv; ++j) {
+      constexpr uint32_t idesc_pv = idesc_f16(BQ, D, 0, 1);    // P K-major, V MN-major
+      auto issue_s = [&](int j) -> bool {
         const int ks = j % KST;
-        if (!mbar_wait(smem_u32(&k_full[ks]), (j / KST) & 1, abort)) break;
-        // S buffer j & 1 holds P_{j-2} until PV_{j-2} has completed
-        if (j >= 2 && !mbar_wait(smem_u32(&pv_done[j & 1]), ((j - 2) >> 1) & 1, abort)) break;
+        if (!mbar_wait(smem_u32(&B.k_full[ks]), (j / KST) & 1, abort)) return false;
         tc_fence_after();
         const uint32_t kb = sK + ks * KV_BYTES;
 #pragma unroll
@@ -202,11 +206,29 @@ __global__ void __launch_bounds__(THREADS, 2)
           const uint64_t bd = sdesc_sw128(kb + chunk * KV_HALF + koff, 16, 1024);
           mma_f16(tmem + (uint32_t)((j & 1) * BKV), ad, bd, idesc_s, kk != 0);
         }
-        mma_commit(smem_u32(&s_full[j & 1]));
-        mma_commit(smem_u32(&k_empty[ks]));
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        mma_commit(smem_u32(&B.s_full[j & 1]));
+        mma_commit(smem_u32(&B.k_empty[ks]));
+        return true;
+      };
+      bool ok = mbar_wait(smem_u32(&B.q_full), 0, abort);
+      for (int j = 0; ok && j < 2 && j < n_kv; ++j) ok = issue_s(j);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        // softmax j has read S_j and written P_j
+        if (!mbar_wait(smem_u32(&B.p_full), j & 1, abort)) break;
+        const int vs = j % VST;
+        if (!mbar_wait(smem_u32(&B.v_full[vs]), (j / VST) & 1, abort)) break;
+        tc_fence_after();
+        const uint32_t vb = sV + vs * KV_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint64_t ad = sdesc_sw128(sP + kk * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(vb + kk * 16 * 128, KV_HALF, 1024);
+          mma_f16(tmem + O_COL, ad, bd, idesc_pv, (j | kk) != 0);
+        }
+        mma_commit(smem_u32(&B.pv_done));
+        mma_commit(smem_u32(&B.v_empty[vs]));
+        if (j + 2 < n_kv) ok = issue_s(j + 2);
       }
-      if (ok && !*abort) issue_pv(n_kv - 1);
     }
   } else {
     // ---------------- softmax warps 0-3 ----------------
@@ -215,17 +237,20 @@ __global__ void __launch_bounds__(THREADS, 2)
     float m_used = -INFINITY, l_run = 0.f;
     // waits are made warp-uniform: tcgen05.ld/st need the whole warp
     for (int j = 0; j < n_kv; ++j) {
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&s_full[j & 1]), (j >> 1) & 1, abort)))
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&B.s_full[j & 1]), (j >> 1) & 1, abort)))
         break;
       tc_fence_after();
       float sv[BKV];
-#pragma unroll
-      for (int c = 0; c < BKV; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * BKV + c), r);
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * BKV), r0);
+        tmem_ld32(tmem + lane_base + (uint32_t)((j & 1) * BKV + 32), r1);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c + i] = __uint_as_float(r[i]);
+        for (int i = 0; i < 32; ++i) {
+          sv[i] = __uint_as_float(r0[i]);
+          sv[32 + i] = __uint_as_float(r1[i]);
+        }
       }
       const int kpos0 = j * BKV;
       const bool diag = p.causal && kpos0 + BKV - 1 > q0;
@@ -237,9 +262,12 @@ __global__ void __launch_bounds__(THREADS, 2)
       // eight independent partial maxima / sums keep the dependency chains short
       float m8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = sv[i];
+      for (int i = 0; i < 8; ++i) m8[i] = fmaxf(sv[i], sv[8 + i]);
 #pragma unroll
-      for (int i = 8; i < BKV; ++i) m8[i & 7] = fmaxf(m8[i & 7], sv[i]);
+      for (int i = 16; i < BKV; i += 16) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = max3(m8[k], sv[i + k], sv[i + 8 + k]);
+      }
 #pragma unroll
       for (int h = 4; h >= 1; h >>= 1)
 #pragma unroll
@@ -277,30 +305,41 @@ __global__ void __launch_bounds__(THREADS, 2)
 #pragma unroll
         for (int i = 0; i < h; ++i) s8[i] += s8[i + h];
       l_run += s8[0];
-      // O rows move only when PV_{j-1} has landed
-      if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
-        const bool ok = __all_sync(
-            0xffffffffu, mbar_wait(smem_u32(&pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, abort));
+      // PV_{j-1} has read the P tile and finished adding into O
+      if (j >= 1) {
+        const bool ok = __all_sync(0xffffffffu,
+                                   mbar_wait(smem_u32(&B.pv_done), (j - 1) & 1, abort));
         tc_fence_after();
         if (!ok) break;
+        if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tmem + lane_base + O_COL + c, r);
-          tmem_ld_wait();
+          for (int c = 0; c < D; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(tmem + lane_base + O_COL + c, r);
+            tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-          tmem_st32(tmem + lane_base + O_COL + c, r);
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+            tmem_st32(tmem + lane_base + O_COL + c, r);
+          }
+          tmem_st_wait();
         }
       }
-      // P_j over the first 32 columns of S_j's buffer (already read above)
-      tmem_st32(tmem + lane_base + (uint32_t)((j & 1) * BKV), ph);
-      tmem_st_wait();
+      // P_j: row tid of the K-major tile, 128-byte swizzle (chunk u at u ^ (row & 7))
+      {
+        const uint32_t rowaddr = sP + tid * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint32_t dst = rowaddr + ((u ^ (tid & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(ph[4 * u]),
+                       "r"(ph[4 * u + 1]), "r"(ph[4 * u + 2]), "r"(ph[4 * u + 3])
+                       : "memory");
+        }
+      }
+      fence_proxy_async();
       tc_fence_before();
-      mbar_arrive(smem_u32(&p_full[j & 1]));
+      mbar_arrive(smem_u32(&B.p_full));
     }
-    const bool done = !*abort &&
-                      mbar_wait(smem_u32(&pv_done[(n_kv - 1) & 1]), ((n_kv - 1) >> 1) & 1, abort);
+    const bool done = !*abort && mbar_wait(smem_u32(&B.pv_done), (n_kv - 1) & 1, abort);
     if (__all_sync(0xffffffffu, done)) {
       tc_fence_after();
       const float inv = 1.f / l_run;
@@ -329,7 +368,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
-  if (tid == 0 && abort_flag) atomicOr(p.status, KTIR_STATUS_TIMEOUT);
+  if (tid == 0 && B.abort_flag) atomicOr(p.status, KTIR_STATUS_TIMEOUT);
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -381,8 +420,11 @@ extern "C" int ktir_fmha_f16(const KtirFmhaDesc* d, void* stream) {
     return KTIR_ERR_CUDA;
   static bool attr = false;
   if (!attr) {
+    // two CTAs per SM need the whole shared-memory carve-out
     if (cudaFuncSetAttribute(k_fmha_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES) != cudaSuccess)
+                             SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(k_fmha_tcgen05, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       return KTIR_ERR_CUDA;
     attr = true;
   }

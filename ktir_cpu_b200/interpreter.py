@@ -99,12 +99,41 @@ class HBMFacade:
         return out
 
 
+class LXFacade(HBMFacade):
+    """Host view of one core's LX scratchpad: byte-addressed allocations, read
+    and written like ktir_cpu/memory.py:304-331 (reads past an allocation
+    return zeros, writes are truncated), so tests can seed it before a call."""
+
+    def write(self, ptr: int, data: np.ndarray) -> None:  # type: ignore[override]
+        super().write(0, data, intra_byte=ptr)
+
+    def read(self, ptr: int, n_elements: int, dtype: str) -> np.ndarray:  # type: ignore[override]
+        return super().read(0, n_elements, dtype, intra_byte=ptr)
+
+
 class DeviceMemory:
-    """The interpreter's `memory` attribute: holds the HBM façade."""
+    """The interpreter's `memory` attribute: the HBM façade and per-core LX
+    scratchpads (`get_lx(core)`).  Every allocation of either becomes one
+    device buffer of a call; LX allocations live in the address space at
+    `lx_address(core, byte)`, apart from HBM."""
 
     def __init__(self, num_cores: int) -> None:
         self.num_cores = num_cores
         self.hbm = HBMFacade()
+        self.lx: Dict[int, LXFacade] = {}
+
+    def get_lx(self, core_id: int) -> LXFacade:
+        if core_id < 0 or core_id >= self.num_cores:
+            raise ValueError(f"core {core_id} is out of range [0, {self.num_cores})")
+        return self.lx.setdefault(core_id, LXFacade())
+
+    def allocations(self) -> List[Tuple[int, Any, int]]:
+        """(address in the trace's address space, façade, façade key), sorted."""
+        from .trace import lx_address
+        out = [(a, self.hbm, a) for a in self.hbm.allocs]
+        for core, lx in self.lx.items():
+            out += [(lx_address(core, a), lx, a) for a in lx.allocs]
+        return sorted(out, key=lambda t: t[0])
 
 
 class Executable:
@@ -273,9 +302,11 @@ class KTIRInterpreter:
     def _space(self, ptrs: Dict[str, int]) -> AddressSpace:
         space = AddressSpace()
         names = {v * STICK: k for k, v in ptrs.items()}
-        for addr, arr in sorted(self.memory.hbm.allocs.items()):
-            space.add_fixed(names.get(addr, f"hbm@0x{addr:x}"), addr, arr.nbytes, arr.dtype,
-                            arr.shape)
+        for addr, fac, key in self.memory.allocations():
+            arr = fac.allocs[key]
+            label = names.get(addr, f"hbm@0x{addr:x}" if fac is self.memory.hbm else
+                              f"lx@0x{key:x}")
+            space.add_fixed(label, addr, arr.nbytes, arr.dtype, arr.shape)
         return space
 
     def execute_function(self, func_name: str, **kwargs) -> Dict[str, np.ndarray]:
@@ -308,8 +339,8 @@ class KTIRInterpreter:
         call's allocations (zero outside every allocation, like a read past the
         end of one)."""
         from .trace import np_dtype
-        allocs = [(base, arr.view(np.uint8).reshape(-1))
-                  for base, arr in self.memory.hbm.allocs.items()]
+        allocs = [(addr, fac.allocs[key].view(np.uint8).reshape(-1))
+                  for addr, fac, key in self.memory.allocations()]
 
         def read(addrs: np.ndarray, dtype: str) -> np.ndarray:
             dt = np_dtype(dtype)
@@ -323,8 +354,7 @@ class KTIRInterpreter:
         return read
 
     def _executable(self, func_name: str, ptrs: Dict[str, int], scalars: Dict[str, Any]):
-        hbm = self.memory.hbm
-        allocs = sorted(hbm.allocs.items())
+        allocs = [(a, fac.allocs[k]) for a, fac, k in self.memory.allocations()]
         key = (func_name, tuple((a, arr.nbytes, str(arr.dtype)) for a, arr in allocs),
                tuple(sorted((k, repr(v)) for k, v in scalars.items())),
                tuple(sorted(ptrs.items())))
@@ -374,12 +404,13 @@ class KTIRInterpreter:
         with the same signature.
         """
         torch = exe.torch
-        hbm = self.memory.hbm
+        where = {a: (fac, k) for a, fac, k in self.memory.allocations()}
+        arrays = [where[a][0].allocs[where[a][1]] for a in order]
         pool = _pool()
         if exe.dev_tensors is None:
             exe.dev_tensors, exe.pinned, exe.pinned_np = [], [], []
-            for addr in order:
-                nb = hbm.allocs[addr].nbytes
+            for arr in arrays:
+                nb = arr.nbytes
                 exe.dev_tensors.append(torch.empty(nb + 16, dtype=torch.uint8, device=exe.device))
                 pin = torch.empty(max(nb, 1), dtype=torch.uint8, pin_memory=True)
                 exe.pinned.append(pin)
@@ -388,7 +419,7 @@ class KTIRInterpreter:
         stream = torch.cuda.current_stream(exe.device)
         written = exe.plan.info.get("written")
         skip = exe.plan.info.get("overwritten", set())
-        src = [hbm.allocs[a].view(np.uint8).reshape(-1) for a in order]
+        src = [arr.view(np.uint8).reshape(-1) for arr in arrays]
         staged = []
         for i in range(len(order)):
             if i in skip:
@@ -421,8 +452,9 @@ class KTIRInterpreter:
         for f in copies:
             f.result()
         for i, addr in enumerate(order):
-            hbm.allocs[addr] = results[i].view(hbm.allocs[addr].dtype)
-            hbm.borrowed.add(addr)
+            fac, k = where[addr]
+            fac.allocs[k] = results[i].view(arrays[i].dtype)
+            fac.borrowed.add(k)
         exe.last_h2d_bytes, exe.last_d2h_bytes = h2d, d2h
 
 

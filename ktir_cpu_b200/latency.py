@@ -329,6 +329,12 @@ class LatencyTape:
                         c.record(cat, 0.0, op_type, flops=0.0)
                     else:
                         c.record(cat, arg / simd, op_type, flops=float(arg))
+                elif cat == "comm":
+                    if arg is None:
+                        raise RuntimeError("_comm_size: comm op result must be a Tile, "
+                                           "got NoneType")
+                    rb = config.ring_bytes_per_cycle
+                    c.record("comm", arg / rb if rb > 0 else 0.0, op_type, nbytes=int(arg))
                 else:
                     raise NotImplementedError(f"latency category {cat}")
         return LatencyReport(config=config, counters=counters)

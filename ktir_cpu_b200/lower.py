@@ -1041,32 +1041,26 @@ class GenericExecutor:
 
     def build(self) -> Plan:
         tr = self.trace
-        by_core: Dict[int, List[Store]] = {}
-        for s in tr.stores:
-            by_core.setdefault(s.core, []).append(s)
-        node_core: Dict[int, List[Node]] = {}
-        for n in tr.nodes:
-            node_core.setdefault(n.core, []).append(n)
-        for core in sorted(set(list(by_core) + list(node_core))):
-            stores = by_core.get(core, [])
-            needed = self._needed(stores)
-            nodes = [n for n in node_core.get(core, []) if n.id in needed]
-            # interleave nodes and stores in program order: a store precedes
-            # every node created after it
-            si = 0
-            order: List[Any] = []
-            store_pos = [(s, self._created_before(s)) for s in stores]
-            for n in nodes:
-                while si < len(store_pos) and store_pos[si][1] <= n.id:
-                    order.append(store_pos[si][0])
-                    si += 1
-                order.append(n)
-            order.extend(s for s, _ in store_pos[si:])
-            for item in order:
-                if isinstance(item, Node):
-                    self.node(item)
-                else:
-                    self.store(item)
+        # the trace lists nodes and stores in the order the call executes them
+        # (core after core, and across a collective every core's part before
+        # it, then every core's part after it); replay that order, a store
+        # preceding every node created after it
+        needed = self._needed(tr.stores)
+        nodes = [n for n in tr.nodes if n.id in needed]
+        stores = sorted(tr.stores, key=lambda s: (self._created_before(s), s.seq))
+        order: List[Any] = []
+        si = 0
+        for n in nodes:
+            while si < len(stores) and self._created_before(stores[si]) <= n.id:
+                order.append(stores[si])
+                si += 1
+            order.append(n)
+        order.extend(stores[si:])
+        for item in order:
+            if isinstance(item, Node):
+                self.node(item)
+            else:
+                self.store(item)
         plan = Plan("generic", self.launches, [], arena_bytes=self.arena_bytes, status_check=True)
         plan.info["dense_uploads"] = self.dense_uploads
         return plan
@@ -1157,8 +1151,17 @@ class GenericExecutor:
             self._launch_ew(program(b, n.shape, 1, 0,
                                     lambda key: mkview(R.ARENA_SLOT, n.dtype, out.off, out.strides)))
             self.vals[n.id] = out
-        elif k in ("bcast", "transpose", "reshape", "splat", "extract"):
+        elif k in ("bcast", "transpose", "reshape", "splat", "extract", "slice"):
             self.view_node(n)
+        elif k == "assemble":
+            # zero tile with each piece copied in at its offset (distributed load)
+            out = self.arena_dense(n)
+            self._ew_copy(n, _Val(imm=n.dtype.type(0), dtype=n.dtype), out)
+            for piece, at in zip(n.ins, n.attrs["at"]):
+                off = out.off + sum(a * st for a, st in zip(at, out.strides))
+                self._ew_copy(piece, self.view_of(piece), _Val(R.ARENA_SLOT, off, out.strides,
+                                                               n.dtype))
+            self.vals[n.id] = out
         elif k == "reduce":
             self.reduce(n)
         elif k == "matmul":
@@ -1172,6 +1175,13 @@ class GenericExecutor:
         k = n.kind
         if sv.imm is not None and k != "extract":
             self.vals[n.id] = _Val(imm=sv.imm, dtype=n.dtype)
+            return
+        if k == "slice":
+            if sv.imm is not None:
+                self.vals[n.id] = _Val(imm=sv.imm, dtype=n.dtype)
+                return
+            off = sv.off + sum(a * st for a, st in zip(n.attrs["at"], sv.strides))
+            self.vals[n.id] = _Val(sv.slot, off, sv.strides, sv.dtype)
             return
         if k == "extract":
             if sv.imm is not None:

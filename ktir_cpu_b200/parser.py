@@ -19,7 +19,8 @@ from __future__ import annotations
 import re
 from typing import Any, Callable, Dict, List, Optional, Tuple
 
-from .affine import AffineMap, BoxSet, parse_affine_map, parse_affine_set, parse_expr
+from .affine import (AffineMap, BoxSet, parse_affine_map, parse_affine_set, parse_affine_set_raw,
+                     parse_expr)
 from .ir import IRFunction, IRModule, Operation, Region
 
 SSA = r"%[A-Za-z0-9_$.#]+"
@@ -816,6 +817,83 @@ def _p_index(p, op_type, results, rest, regions):
 
 @_op("linalg.yield", "scf.yield", "tensor.yield", "return")
 def _p_yield(p, op_type, results, rest, regions):
+    return _mk(op_type, results, ssa_names(rest.split(":")[0]), {}, [])
+
+
+def _named_set(p, rest: str, key: str):
+    """The affine set written as `key = #alias` or `key = affine_set<...>`."""
+    m = re.search(rf"\b{key}\s*=\s*", rest)
+    if not m:
+        return None
+    tail = rest[m.end():].lstrip()
+    if tail.startswith("#"):
+        name = re.match(r"#[\w$.]+", tail).group(0)
+        text = p.alias(name)
+    else:
+        i = tail.index("<")
+        text = tail[:find_close(tail, i) + 1]
+    return parse_affine_set_raw(text)
+
+
+@_op("ktdp.construct_distributed_memory_view")
+def _p_dist_view(p, op_type, results, rest, regions):
+    """`(%a, %b : memref<..>, memref<..>) : memref<global>` (ktir_cpu/dialects/
+    ktdp_ops.py:418-470): partitions, global shape and dtype."""
+    body = rest.lstrip()
+    if not body.startswith("("):
+        raise KTIRParseError("construct_distributed_memory_view: missing operand parenthesis")
+    j = find_close(body, 0)
+    inner, tail = body[1:j], body[j + 1:]
+    operands = ssa_names(inner.split(":")[0])
+    m = re.search(r"memref<([^>]+)>", tail)
+    if not m:
+        raise KTIRParseError("construct_distributed_memory_view: missing result memref type")
+    t = parse_type("memref<" + m.group(1) + ">")
+    if any(d is None for d in t["shape"]):
+        raise KTIRParseError("construct_distributed_memory_view: dynamic global shape")
+    return _mk(op_type, results, operands, {"shape": tuple(t["shape"]), "dtype": t["dtype"]},
+               ["memref<" + m.group(1) + ">"])
+
+
+@_op("ktdp.inter_tile_produce")
+def _p_inter_produce(p, op_type, results, rest, regions):
+    """ktdp.inter_tile_produce (ktir_cpu/dialects/ktdp_ops.py:998-1038)."""
+    prod = _named_set(p, rest, "producer_tiles_per_group")
+    groups = _named_set(p, rest, "groups")
+    if prod is None or groups is None:
+        raise KTIRParseError("ktdp.inter_tile_produce: needs producer_tiles_per_group and groups")
+    return _mk(op_type, results, [], {"producer_tiles_per_group": prod, "groups": groups}, [],
+               regions)
+
+
+@_op("ktdp.inter_tile_reduce")
+def _p_inter_reduce(p, op_type, results, rest, regions):
+    """ktdp.inter_tile_reduce (ktir_cpu/dialects/ktdp_ops.py:1171-1227): the future
+    operand, the identity operands and the result shape (within-group axes
+    collapsed)."""
+    m = re.match(r"^\(\s*(%[\w$.]+)\s*\)", rest)
+    if not m:
+        raise KTIRParseError(f"ktdp.inter_tile_reduce: cannot parse {rest!r}")
+    cons = _named_set(p, rest, "consumer_tiles_per_group")
+    groups = _named_set(p, rest, "groups")
+    if cons is None or groups is None:
+        raise KTIRParseError("ktdp.inter_tile_reduce: needs consumer_tiles_per_group and groups")
+    attrs: Dict[str, Any] = {"consumer_tiles_per_group": cons, "groups": groups}
+    dep = _named_set(p, rest, "producer_dependency_per_consumer")
+    if dep is not None:
+        attrs["producer_dependency_per_consumer"] = dep
+    ident = paren_after(rest, "identity")
+    operands = [m.group(1)] + (ssa_names(ident.split(":")[0]) if ident else [])
+    arr = arrow_type(rest)
+    if arr:
+        t = parse_type(arr)
+        if t.get("shape") is not None:
+            attrs["result_shape"] = tuple(t["shape"])
+    return _mk(op_type, results, operands, attrs, [arr] if arr else [], regions)
+
+
+@_op("ktdp.yield_partial", "ktdp.yield_reduced")
+def _p_inter_yield(p, op_type, results, rest, regions):
     return _mk(op_type, results, ssa_names(rest.split(":")[0]), {}, [])
 
 

@@ -39,10 +39,18 @@ from typing import Any, Dict, List, Optional, Sequence, Tuple
 import numpy as np
 
 from .affine import AffineMap, AffineSet, BoxSet
-from .ir import IRFunction, Operation, Region
+from .ir import IRFunction, Operation, Region, iter_ops
 
 STICK = 128
 LX_CAPACITY = 2 * 1024 * 1024
+# LX scratchpads live in the trace's address space apart from HBM: core c's
+# byte b is at LX_BASE + c * LX_SPAN + b
+LX_BASE = 1 << 50
+LX_SPAN = 1 << 36
+
+
+def lx_address(core: int, byte: int) -> int:
+    return LX_BASE + core * LX_SPAN + byte
 
 NP = {
     "f16": np.float16, "fp16": np.float16, "float16": np.float16,
@@ -203,16 +211,37 @@ class Store:
 
 @dataclass
 class MemRefV:
-    stick: int
+    stick: int                  # HBM: stick index; LX: byte address in its scratchpad
     shape: Tuple[int, ...]
     strides: List[int]
     space: str
     dtype: str
     cset: Any = None
+    lx_core: Optional[int] = None
 
     @property
     def byte_address(self) -> int:
+        if self.space == "LX":
+            return lx_address(self.lx_core, self.stick)
         return self.stick * STICK
+
+
+@dataclass
+class DistMemRefV:
+    """ktdp.construct_distributed_memory_view: partitions in global coordinates."""
+    parts: List[MemRefV]
+    shape: Tuple[int, ...]
+    dtype: str
+
+
+@dataclass
+class DistAccessV:
+    """An access tile over a distributed view, resolved to the partitions it
+    touches: (partition, covered box in global coordinates, partition origin)."""
+    base: Tuple[int, ...]
+    shape: Tuple[int, ...]
+    dtype: str
+    pieces: List[Tuple[MemRefV, Any, Tuple[int, ...]]]
 
 
 @dataclass
@@ -239,6 +268,15 @@ class IATV:
     def signature(self):
         return (id(self.vss), self.vso.source if self.vso else None, tuple(self.consts.items()),
                 tuple(sorted(self.refs.items())))
+
+
+@dataclass
+class FutureV:
+    """A core's ktdp.tile_future: its partial and the sets naming its group."""
+    partial: Any
+    producer_set: Any
+    groups_set: Any
+    group: int
 
 
 class _Yield:
@@ -367,19 +405,45 @@ class Tracer:
     # -- driver ----------------------------------------------------------------
     def run(self) -> Trace:
         nx, ny, nz = self.func.grid
-        for cid in range(nx * ny * nz):
+        n = nx * ny * nz
+        states = []
+        for cid in range(n):
             z, r = divmod(cid, nx * ny)
             y, x = divmod(r, nx)
-            self.core = CoreState(cid, (x, y, z))
-            if self.lat is not None:
-                self.lat.begin_core(cid)
+            st = CoreState(cid, (x, y, z))
             for aname, _ in self.func.arguments:
                 key = aname.lstrip("%")
                 if key in self.pointers:
-                    self.core.set(aname, self.pointers[key])
+                    st.set(aname, self.pointers[key])
                 elif key in self.scalars:
-                    self.core.set(aname, self.scalars[key])
-            self.run_ops(self.func.operations)
+                    st.set(aname, self.scalars[key])
+            states.append(st)
+        # Cores run one after another.  A ktdp.inter_tile_reduce is a
+        # collective over the whole grid: every core runs up to it, then the
+        # ring result of every consumer is formed, then every core runs on to
+        # the next one (the reference's scheduler observes the same order:
+        # no core passes the ring before all cores reached it).
+        segments: List[List[Operation]] = [[]]
+        collectives: List[Operation] = []
+        for op in self.func.operations:
+            if op.op_type == "ktdp.inter_tile_reduce":
+                collectives.append(op)
+                segments.append([])
+            else:
+                for o in iter_ops([op]):
+                    if o.op_type == "ktdp.inter_tile_reduce":
+                        raise NotImplementedError(
+                            "ktdp.inter_tile_reduce inside a region is not supported by the "
+                            "B200 backend (only at the top level of the function)")
+                segments[-1].append(op)
+        for si, seg in enumerate(segments):
+            for st in states:
+                self.core = st
+                if self.lat is not None:
+                    self.lat.begin_core(st.core_id)
+                self.run_ops(seg)
+            if si < len(collectives):
+                self._ring_reduce(collectives[si], states)
         return self.trace
 
     def run_ops(self, ops: List[Operation]):
@@ -426,9 +490,17 @@ class Tracer:
         arg = None
         if cat == "memory":
             if op.op_type == "ktdp.load":
-                arg = self._load_sticks(res)
+                if res.kind == "assemble":
+                    arg = sum(self._load_sticks(p) for p in res.ins)
+                else:
+                    arg = self._load_sticks(res)
             else:
-                arg = self._store_sticks(self.trace.stores[-1].target)
+                t = self.core.get(op.operands[1])
+                if isinstance(t, DistAccessV):
+                    arg = sum(self._store_sticks(s.target)
+                              for s in self.trace.stores[len(self.trace.stores) - len(t.pieces):])
+                else:
+                    arg = self._store_sticks(self.trace.stores[-1].target)
         elif cat == "compute_matmul":
             tiles = [v for v in self._operands(op) if _is_tile(v)]
             if len(tiles) >= 2:
@@ -447,6 +519,8 @@ class Tracer:
         if a["mode"] == "indirect":
             return L.IndirectAccess(a["iat"], store=False)
         buf, isz = a["buf"], n.dtype.itemsize
+        if buf.byte_base >= LX_BASE:
+            return 0   # LX: no HBM traffic (ktir_cpu/latency.py:232-233)
         base = buf.byte_base + a["off"] * isz
         if a["mode"] == "rect":
             return L.rect_sticks(base, n.shape, a["strides"], isz)
@@ -457,10 +531,108 @@ class Tracer:
         if isinstance(t, IndirectTarget):
             return L.IndirectAccess(t.iat, store=True)
         isz = np.dtype(t.dtype).itemsize
+        if t.buf.byte_base >= LX_BASE:
+            return 0
         base = t.buf.byte_base + t.off * isz
         if isinstance(t, RectTarget):
             return L.rect_sticks(base, t.shape, t.strides, isz)
         return L.coord_sticks(base, t.offsets, isz)
+
+    # -- inter-tile collectives ----------------------------------------------------
+    def op_ktdp_inter_tile_produce(self, op):
+        """This core's partial and its group (ktir_cpu/dialects/ktdp_ops.py:947-995,
+        group lookup :913-940)."""
+        a = op.attributes
+        n = self.func.num_cores
+        cid = self.core.core_id
+        groups = [g for g in range(n) if a["groups"].contains([g])
+                  and a["producer_tiles_per_group"].contains([cid], [g])]
+        if not groups:
+            raise RuntimeError(
+                f"tile {cid} is not contained in any producer group "
+                f"(producer_set={a['producer_tiles_per_group'].source!r}, "
+                f"groups_set={a['groups'].source!r})")
+        if len(groups) > 1:
+            raise RuntimeError(f"tile {cid} matched multiple groups {groups} — "
+                               f"violates the disjointness invariant")
+        gid = groups[0]
+        region = op.regions[0] if op.regions else None
+        partial = None
+        if region is not None:
+            self.core.push()
+            if region.args:
+                self.core.set(region.args[0][0], gid)
+            r = self.run_ops(region.ops)
+            self.core.pop()
+            vals = r.values if isinstance(r, _Yield) else ([r] if r is not None else [])
+            partial = vals[0] if vals else None
+        return FutureV(partial, a["producer_tiles_per_group"], a["groups"], gid)
+
+    def _ring_reduce(self, op, states):
+        """ktdp.inter_tile_reduce on every core at once, with the ring's fold order
+        (ktir_cpu/ops/comm_ops.py:325-345): consumer c starts from its own seed
+        (its partial if it produces, else its identity) and folds the seeds of
+        cores c-1, c-2, ... (mod n) that produce in c's group, left to right."""
+        n = len(states)
+        a = op.attributes
+        futs, seeds, plans = [], [], []
+        for st in states:
+            fut = st.get(op.operands[0])
+            if not isinstance(fut, FutureV):
+                raise TypeError(f"ktdp.inter_tile_reduce: operand 0 must be a TileFuture, "
+                                f"got {type(fut)}")
+            ident = st.get(op.operands[1]) if len(op.operands) > 1 else None
+            prod = {i for i in range(n) if fut.producer_set.contains([i], [fut.group])}
+            cons = {i for i in range(n) if a["consumer_tiles_per_group"].contains([i], [fut.group])}
+            futs.append(fut)
+            plans.append((prod, cons))
+            seeds.append(fut.partial if st.core_id in prod else ident)
+        region = op.regions[0] if op.regions else None
+        if region is None or len(region.args) < 2:
+            raise ValueError("ktdp.inter_tile_reduce: combiner region missing ^bb0 args")
+        lhs, rhs = region.args[0][0], region.args[1][0]
+        body = list(region.ops)
+        target = a.get("result_shape")
+        for st in states:
+            c = st.core_id
+            prod, cons = plans[c]
+            self.core = st
+            if self.lat is not None:
+                self.lat.begin_core(c)
+            acc = seeds[c]
+            folds = 0
+            for k in range(1, n):
+                o = (c - k) % n
+                if o not in prod:
+                    continue
+                st.push()
+                st.set(lhs, acc)
+                st.set(rhs, seeds[o])
+                r = self.run_ops(body)
+                st.pop()
+                acc = r.values[0] if isinstance(r, _Yield) else r
+                if not _is_tile(acc):
+                    raise TypeError(f"ktdp.inter_tile_reduce: combiner did not yield a Tile, "
+                                    f"got {type(acc)}")
+                folds += 1
+            if self.lat is not None:
+                wire = (n - 1) * seeds[c].nbytes if (c in cons and _is_tile(seeds[c])) else None
+                self.lat.add(op.op_type, "comm", wire)
+            if c not in cons:
+                # the reference hands such a core None and then fails to reshape it
+                # (ktir_cpu/dialects/ktdp_helpers.py:186-189)
+                raise TypeError("reshape_tile_to_target: expected Tile, got NoneType")
+            if target is not None and tuple(target) != tuple(acc.shape):
+                if int(np.prod(target)) != acc.numel:
+                    raise ValueError(f"reshape_tile_to_target: result shape {acc.shape} and "
+                                     f"declared shape {tuple(target)} have different element counts")
+                acc = self.node("reshape", tuple(target), acc.dtype, (acc,), {}, acc.label)
+            elif folds == 0:
+                # a lone consumer gets its own seed: give the result its own node
+                acc = self.node("ew", acc.shape, acc.dtype, (acc,), {"op": "cast"}, acc.label)
+            if op.results:
+                st.set(op.results[0], acc)
+                st.track(op.results[0], acc.nbytes)
 
     # -- grid / views ------------------------------------------------------------
     def op_ktdp_get_compute_tile_id(self, op):
@@ -479,17 +651,32 @@ class Tracer:
         if isinstance(cset, BoxSet) and not cset.is_concrete:
             syms = tuple(int(self.core.get(s)) for s in a["shape"] if isinstance(s, str))
             cset = cset.specialize(syms)
-        if a["memory_space"] != "HBM":
-            raise NotImplementedError("memory views in LX are not supported by the B200 backend")
+        lx_core = None
+        if a["memory_space"] == "LX":
+            # a core's own scratchpad unless the view names another core's
+            lx_core = a.get("lx_core_id", self.core.core_id)
+        elif a["memory_space"] != "HBM":
+            raise ValueError(f"Invalid memory_space {a['memory_space']!r}")
         return MemRefV(ptr, tuple(int(s) for s in shape), [int(s) for s in strides],
-                       a["memory_space"], a["dtype"], cset)
+                       a["memory_space"], a["dtype"], cset, lx_core)
+
+    def op_ktdp_construct_distributed_memory_view(self, op):
+        """ktir_cpu/dialects/ktdp_ops.py:97-121."""
+        parts = [self.core.get(o) for o in op.operands]
+        for i, part in enumerate(parts):
+            if not isinstance(part, MemRefV):
+                raise ValueError(f"construct_distributed_memory_view: operand {i} is "
+                                 f"{type(part).__name__}, expected MemRef")
+        return DistMemRefV(parts, tuple(op.attributes["shape"]), op.attributes["dtype"])
 
     def op_ktdp_construct_access_tile(self, op):
         parent = self.core.get(op.operands[0])
-        if not isinstance(parent, MemRefV):
-            raise NotImplementedError("access tiles over distributed views are not supported")
         idx = [_need_int(self.core.get(o), "access tile index") for o in op.operands[1:]]
         a = op.attributes
+        if isinstance(parent, DistMemRefV):
+            return self._dist_access(parent, idx, a)
+        if not isinstance(parent, MemRefV):
+            raise TypeError(f"construct_access_tile: parent is {type(parent).__name__}")
         base = a["base_map"].eval(idx)
         off = sum(int(c) * s for c, s in zip(base, parent.strides))
         cset = a["coordinate_set"]
@@ -497,6 +684,42 @@ class Tracer:
             raise NotImplementedError("construct_access_tile: symbolic access_tile_set")
         return AccessTileV(parent.byte_address + off * bpe(parent.dtype), tuple(a["shape"]),
                            list(parent.strides), parent.dtype, cset, a.get("coordinate_order"))
+
+    def _dist_access(self, dist: DistMemRefV, idx, a):
+        """Partition routing of MemoryOps.distributed_tile_access
+        (ktir_cpu/ops/memory_ops.py:651-756): C_i = B_i ∩ (x + A) per partition,
+        empty intersections dropped.  Rectangular partitions and access sets."""
+        x = tuple(int(v) for v in a["base_map"].eval(idx))
+        shape = tuple(a["shape"])
+        acc = a["coordinate_set"]
+        if acc is None:
+            lo, hi = x, tuple(x[d] + shape[d] for d in range(len(shape)))
+        elif isinstance(acc, BoxSet) and acc.is_concrete:
+            lo = tuple(x[d] + acc.lo[d] for d in range(len(shape)))
+            hi = tuple(x[d] + acc.hi[d] for d in range(len(shape)))
+        else:
+            raise NotImplementedError("distributed access with a non-rectangular access set")
+        pieces = []
+        for part in dist.parts:
+            b = part.cset
+            if not (isinstance(b, BoxSet) and b.is_concrete):
+                raise NotImplementedError("distributed view with a non-rectangular partition")
+            clo = tuple(max(lo[d], b.lo[d]) for d in range(len(lo)))
+            chi = tuple(min(hi[d], b.hi[d]) for d in range(len(lo)))
+            if any(clo[d] >= chi[d] for d in range(len(lo))):
+                continue
+            pieces.append((part, BoxSet(clo, chi), tuple(b.lo)))
+        if not pieces:
+            raise ValueError(f"distributed_tile_access: no partition covers access region "
+                             f"global_base={x} shape={shape}")
+        return DistAccessV(x, shape, dist.dtype, pieces)
+
+    def _piece(self, part: MemRefV, box: BoxSet, origin, what: str):
+        """(buffer, element offset, shape, strides) of one partition's sub-box."""
+        local = [box.lo[d] - origin[d] for d in range(len(origin))]
+        off = sum(l * s for l, s in zip(local, part.strides))
+        buf, eoff = self._resolve(part.byte_address + off * bpe(part.dtype), part.dtype, what)
+        return buf, eoff, box.extent(), tuple(part.strides[:len(origin)])
 
     def op_ktdp_construct_indirect_access_tile(self, op):
         a = op.attributes
@@ -557,6 +780,18 @@ class Tracer:
     def op_ktdp_load(self, op):
         t = self.core.get(op.operands[0])
         rshape = op.attributes.get("result_shape")
+        if isinstance(t, DistAccessV):
+            # MemoryOps.distributed_load (ktir_cpu/ops/memory_ops.py:782-846): each
+            # covered box read from its partition, placed into a zero tile
+            shape = tuple(rshape or t.shape)
+            dt = np_dtype(t.dtype)
+            parts, places = [], []
+            for part, box, origin in t.pieces:
+                buf, eoff, ext, strides = self._piece(part, box, origin, "Read")
+                parts.append(self.node("load", ext, dt, (), {"mode": "rect", "buf": buf,
+                                                             "off": eoff, "strides": strides}))
+                places.append(tuple(box.lo[d] - t.base[d] for d in range(len(shape))))
+            return self.node("assemble", shape, dt, tuple(parts), {"at": places})
         if isinstance(t, IATV):
             if t.vso is not None and not t.vso.is_permutation():
                 raise ValueError("indirect_load: variables_space_order must permute its input "
@@ -589,6 +824,18 @@ class Tracer:
         if not _is_tile(val):
             raise TypeError(f"ktdp.store expects a Tile, got {type(val)}")
         t = self.core.get(op.operands[1])
+        if isinstance(t, DistAccessV):
+            # MemoryOps.distributed_store (ktir_cpu/ops/memory_ops.py:848-912): the
+            # tile's slice over each covered box written to its partition
+            for part, box, origin in t.pieces:
+                buf, eoff, ext, strides = self._piece(part, box, origin, "Write")
+                at = tuple(box.lo[d] - t.base[d] for d in range(len(ext)))
+                sub = self.node("slice", ext, val.dtype, (val,), {"at": at}, val.label)
+                self.trace.stores.append(Store(self.core.core_id, self.seq, sub,
+                                               RectTarget(buf, eoff, ext, strides, np_dtype(t.dtype)),
+                                               len(self.trace.nodes)))
+                self.seq += 1
+            return None
         if isinstance(t, IATV):
             if tuple(val.shape) != tuple(t.shape):
                 raise ValueError(
@@ -1362,3 +1609,5 @@ Tracer.op_tensor_reshape = _op_reshape
 Tracer.op_tensor_yield = _yield
 Tracer.op_linalg_yield = _yield
 Tracer.op_scf_yield = _yield
+Tracer.op_ktdp_yield_partial = _yield
+Tracer.op_ktdp_yield_reduced = _yield

@@ -134,6 +134,13 @@ class IndirectTile:
     consts: Dict[int, int]    # intermediate-variable index -> bound outer SSA value
 
 
+@dataclass
+class _Future:
+    partial: Any
+    producer_set: Any
+    group: int
+
+
 class _Yield:
     __slots__ = ("values",)
 
@@ -329,7 +336,9 @@ class OracleInterpreter:
                 ptrs[name] = v
         nx, ny, nz = fn.grid
         n = nx * ny * nz
+        self.n_cores = n
         limit = n if self.core_limit is None else min(n, self.core_limit)
+        cores = []
         for cid in range(limit):
             z, r = divmod(cid, nx * ny)
             y, x = divmod(r, nx)
@@ -338,7 +347,22 @@ class OracleInterpreter:
                 key = aname.lstrip("%")
                 if key in ptrs:
                     core.set(aname, ptrs[key])
-            self.run_ops(core, fn.operations)
+            cores.append(core)
+        # Top-level ktdp.inter_tile_reduce ops are collectives: every core runs
+        # up to one, the ring runs, every core continues (the order the
+        # reference's scheduler produces, ktir_cpu/grid.py:471-570).
+        segments, collectives = [[]], []
+        for op in fn.operations:
+            if op.op_type == "ktdp.inter_tile_reduce":
+                collectives.append(op)
+                segments.append([])
+            else:
+                segments[-1].append(op)
+        for si, seg in enumerate(segments):
+            for core in cores:
+                self.run_ops(core, seg)
+            if si < len(collectives):
+                self._ring(collectives[si], cores)
         out = {}
         for name, v in kwargs.items():
             if isinstance(v, np.ndarray):
@@ -373,6 +397,73 @@ class OracleInterpreter:
 
     def run_region(self, core: Core, region: Region):
         return self.run_ops(core, region.ops)
+
+    # -- inter-tile produce / ring reduce ----------------------------------------------
+    def op_ktdp_inter_tile_produce(self, core, op):
+        """ktir_cpu/dialects/ktdp_ops.py:947-995 with the group lookup of :913-940."""
+        a = op.attributes
+        n = self.n_cores
+        keys = [g for g in range(n) if a["groups"].contains([g])
+                and a["producer_tiles_per_group"].contains([core.core_id], [g])]
+        if len(keys) != 1:
+            raise RuntimeError(f"tile {core.core_id} matched groups {keys}")
+        gid = keys[0]
+        region = op.regions[0]
+        core.push()
+        if region.args:
+            core.set(region.args[0][0], gid)
+        r = self.run_ops(core, region.ops)
+        core.pop()
+        part = r.values[0] if isinstance(r, _Yield) else r
+        return _Future(part, a["producer_tiles_per_group"], gid)
+
+    def op_ktdp_yield_partial(self, core, op):
+        return _Yield([core.get(o) for o in op.operands])
+
+    op_ktdp_yield_reduced = op_ktdp_yield_partial
+
+    def _ring(self, op, cores):
+        """RingReduceBackend.run (ktir_cpu/ops/comm_ops.py:283-345) for every core:
+        the tile core c receives in round k comes from core (c - k) mod n and is
+        folded into c's accumulator when that core produces in c's group."""
+        n = self.n_cores
+        a = op.attributes
+        region = op.regions[0]
+        lhs, rhs = region.args[0][0], region.args[1][0]
+        info = []
+        for core in cores:
+            fut = core.get(op.operands[0])
+            part, pset, gid = fut.partial, fut.producer_set, fut.group
+            ident = core.get(op.operands[1]) if len(op.operands) > 1 else None
+            prod = [i for i in range(n) if pset.contains([i], [gid])]
+            cons = [i for i in range(n) if a["consumer_tiles_per_group"].contains([i], [gid])]
+            seed = part if core.core_id in prod else ident
+            info.append((prod, cons, seed))
+        for core in cores:
+            c = core.core_id
+            prod, cons, seed = info[c]
+            acc = Tile(seed.data.copy(), seed.dtype, seed.data.shape)
+            for k in range(1, n):
+                o = (c - k) % n
+                if o not in prod:
+                    continue
+                core.push()
+                core.set(lhs, acc)
+                core.set(rhs, info[o][2])
+                r = self.run_ops(core, region.ops)
+                core.pop()
+                acc = r.values[0] if isinstance(r, _Yield) else r
+            if c not in cons:
+                # RingReduceBackend returns None off the consumer set and
+                # reshape_tile_to_target rejects it (ktdp_helpers.py:186-189)
+                raise TypeError("reshape_tile_to_target: expected Tile, got NoneType")
+            if not op.results:
+                continue
+            shape = a.get("result_shape")
+            if shape is not None and tuple(shape) != acc.data.shape:
+                acc = Tile(acc.data.reshape(shape), acc.dtype, tuple(shape))
+            core.set(op.results[0], acc)
+            core.track(op.results[0], acc.nbytes())
 
     # -- grid ------------------------------------------------------------------
     def op_ktdp_get_compute_tile_id(self, core, op):

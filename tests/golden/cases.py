@@ -62,11 +62,13 @@ def _tile(name, view, idx, vshape, dtype, tshape, cset=None, order=None):
             f"{_mref(vshape, dtype)} -> {_at(tshape)}")
 
 
-def _fn(name, args, body, grid=(1,)):
+def _fn(name, args, body, grid=(1,), aliases=()):
     g = ", ".join(str(v) for v in grid)
     a = ", ".join(f"%{n}: index" for n in args)
     lines = "\n    ".join(body)
-    return f"module {{\n  func.func @{name}({a}) attributes {{grid = [{g}]}} {{\n    {lines}\n    return\n  }}\n}}\n"
+    head = "".join(f"{k} = {v}\n" for k, v in aliases)
+    return (f"{head}module {{\n  func.func @{name}({a}) attributes {{grid = [{g}]}} {{\n"
+            f"    {lines}\n    return\n  }}\n}}\n")
 
 
 CASES: List[Dict[str, Any]] = []
@@ -321,3 +323,168 @@ case("matmul_f16_tiles", _fn("mm", ["a", "b", "c"], [
 ]), "mm", {"a": rng.uniform(-1, 1, (64, 128)).astype(np.float16),
            "b": rng.uniform(-1, 1, (128, 64)).astype(np.float16),
            "c": np.zeros((64, 64), np.float16)}, tol=1e-2)
+
+
+# --- inter-tile produce / ring reduce (the reference's only collective) ------------------
+def _ring_case(name, grid, rows, cols, group_size, consumer_cond, combiner, store_all,
+               expect_error=None):
+    """Each core loads row `pid` of x, produces it into its group (cores
+    [group_size*g, group_size*g + group_size)), and the ring reduce leaves the
+    group's fold on the consumer cores, which store it to row `pid` (every
+    consumer) or row `g` (one consumer per group) of o."""
+    n = grid
+    ng = n // group_size
+    t = _tt((1, cols), "f16")
+    fam = f"affine_set<(i)[g] : (i - {group_size}*g >= 0, -i + {group_size}*g + {group_size - 1} >= 0)>"
+    grp = f"affine_set<(g) : (g >= 0, -g + {ng - 1} >= 0)>"
+    cons = f"affine_set<(i)[g] : ({consumer_cond})>"
+    if combiner == "add":
+        comb = [f"      %i0 = tensor.empty() : {t}",
+                f"      %s = linalg.add ins(%l, %r : {t}, {t}) outs(%i0 : {t}) -> {t}",
+                f"      ktdp.yield_reduced %s : {t}"]
+        ident = "0.0"
+    else:
+        comb = [f"      %s = arith.maxnumf %l, %r : {t}",
+                f"      ktdp.yield_reduced %s : {t}"]
+        ident = "0xFC00"
+    out_row = "%pid" if store_all else "%g"
+    body = [
+        "%c0 = arith.constant 0 : index",
+        f"%cg = arith.constant {group_size} : index",
+        "%pid = ktdp.get_compute_tile_id : index",
+        "%g = arith.divui %pid, %cg : index",
+        "%lead = arith.remui %pid, %cg : index",
+        _view("%xv", "%x", (rows, cols), "f16"),
+        _view("%ov", "%o", (rows, cols), "f16"),
+        _tile("%xt", "%xv", ["%pid", "%c0"], (rows, cols), "f16", (1, cols)),
+        f"%part = ktdp.load %xt : {_at((1, cols))} -> {t}",
+        f"%fut = ktdp.inter_tile_produce\n"
+        f"        producer_tiles_per_group = #fam,\n"
+        f"        groups = #grp\n"
+        f"        : {t} -> !ktdp.tile_future<{t}>\n"
+        f"    {{\n"
+        f"      ^bb0(%gid: index):\n"
+        f"        ktdp.yield_partial %part : {t}\n"
+        f"    }}",
+        f"%zero = arith.constant {ident} : f16",
+        f"%e = tensor.empty() : {t}",
+        f"%id = linalg.fill ins(%zero : f16) outs(%e : {t}) -> {t}",
+        f"%red = ktdp.inter_tile_reduce(%fut)\n"
+        f"        consumer_tiles_per_group = #cons,\n"
+        f"        groups = #grp,\n"
+        f"        identity(%id : {t})\n"
+        f"        : !ktdp.tile_future<{t}> -> {_tt((cols,), 'f16')}\n"
+        f"    {{\n"
+        f"      ^bb0(%l: {t}, %r: {t}):\n" + "\n".join(comb) + "\n"
+        f"    }}",
+        "%is_c = arith.cmpi eq, %lead, %c0 : index" if not store_all else
+        "%is_c = arith.cmpi sge, %pid, %c0 : index",
+        f"scf.if %is_c {{\n"
+        f"      %r2 = tensor.expand_shape %red [[0, 1]] output_shape [1, {cols}] : "
+        f"{_tt((cols,), 'f16')} into {t}\n"
+        f"      {_tile('%ot', '%ov', [out_row, '%c0'], (rows, cols), 'f16', (1, cols))}\n"
+        f"      ktdp.store %r2, %ot : {t}, {_at((1, cols))}\n"
+        f"    }}",
+    ]
+    x = (rng.standard_normal((rows, cols)) * 60).astype(np.float16)
+    aliases = [("#fam", fam), ("#grp", grp), ("#cons", cons)]
+    case(name, _fn("ring", ["x", "o"], body, grid=(grid,), aliases=aliases), "ring",
+         {"x": x, "o": np.zeros((rows, cols), np.float16)}, expect_error=expect_error)
+
+
+# all 8 cores produce and consume; each stores its own fold (the fold order
+# differs per core, so the f16 sums differ in their last bits)
+_ring_case("ring_reduce_all_f16", 8, 8, 64, 8, "i - 8*g >= 0, -i + 8*g + 7 >= 0", "add", True)
+# two groups of four, every core consumes its group's fold: the other group's
+# tiles travel the ring but are not folded in
+_ring_case("ring_reduce_groups", 8, 8, 128, 4, "i - 4*g >= 0, -i + 4*g + 3 >= 0", "add", True)
+# a consumer set smaller than the grid: the reference raises TypeError on the
+# cores outside it (their result is None when it is reshaped to the result type)
+_ring_case("ring_reduce_groups_leader", 8, 8, 128, 4, "i - 4*g == 0", "add", False,
+           expect_error="TypeError")
+# max combiner over groups of two
+_ring_case("ring_reduce_pairs_max", 6, 6, 64, 2, "i - 2*g >= 0, -i + 2*g + 1 >= 0", "max", True)
+
+
+# --- distributed memory views (partitions in HBM and in a core's LX) -----------------------
+def _dist_case(name, gshape, parts, acc_shape, acc_idx, store=False):
+    """A [gshape] f16 tensor split into rectangular partitions `parts` =
+    [(row0, row1, col0, col1, space, strides, addr)] (inclusive bounds; addr is
+    a stick for HBM, a byte address for LX core 0), seeded with arange.  Load:
+    the access tile at acc_idx is copied to a dense HBM output.  Store: a dense
+    HBM input is stored through the access tile into the partitions."""
+    out_stick = 0x400
+    body = ["%c0 = arith.constant 0 : index"]
+    names = []
+    for i, (r0, r1, c0, c1, space, strides, addr) in enumerate(parts):
+        nr, nc = r1 - r0 + 1, c1 - c0 + 1
+        body.append(f"%p{i}_addr = arith.constant {addr} : index")
+        body.append(
+            f"%P{i} = ktdp.construct_memory_view %p{i}_addr, sizes: [{nr}, {nc}], "
+            f"strides: [{strides[0]}, {strides[1]}] {{coordinate_set = #P{i}, "
+            f"memory_space = #ktdp.spyre_memory_space<{space}>}} : memref<{nr}x{nc}xf16>")
+        names.append((f"%P{i}", f"memref<{nr}x{nc}xf16>"))
+    g = f"memref<{gshape[0]}x{gshape[1]}xf16>"
+    body.append(f"%A = ktdp.construct_distributed_memory_view ({', '.join(n for n, _ in names)} : "
+                f"{', '.join(t for _, t in names)}) : {g}")
+    body.append(f"%b_addr = arith.constant {out_stick} : index")
+    body.append(f"%B = ktdp.construct_memory_view %b_addr, sizes: [{acc_shape[0]}, {acc_shape[1]}], "
+                f"strides: [{acc_shape[1]}, 1] {{coordinate_set = #AC, memory_space = "
+                f"#ktdp.spyre_memory_space<HBM>}} : memref<{acc_shape[0]}x{acc_shape[1]}xf16>")
+    body.append(f"%i0 = arith.constant {acc_idx[0]} : index")
+    body.append(f"%i1 = arith.constant {acc_idx[1]} : index")
+    at = _at(acc_shape)
+    body.append(f"%A_at = ktdp.construct_access_tile %A[%i0, %i1] {{access_tile_set = #AC, "
+                f"access_tile_order = #ID}} : {g} -> {at}")
+    body.append(f"%B_at = ktdp.construct_access_tile %B[%c0, %c0] {{access_tile_set = #AC, "
+                f"access_tile_order = #ID}} : memref<{acc_shape[0]}x{acc_shape[1]}xf16> -> {at}")
+    tt = _tt(acc_shape, "f16")
+    if store:
+        body.append(f"%d = ktdp.load %B_at : {at} -> {tt}")
+        body.append(f"ktdp.store %d, %A_at : {tt}, {at}")
+    else:
+        body.append(f"%d = ktdp.load %A_at : {at} -> {tt}")
+        body.append(f"ktdp.store %d, %B_at : {tt}, {at}")
+    aliases = [(f"#P{i}", _box_incl(p[0], p[1], p[2], p[3])) for i, p in enumerate(parts)]
+    aliases += [("#AC", _box_incl(0, acc_shape[0] - 1, 0, acc_shape[1] - 1)),
+                ("#ID", "affine_map<(d0, d1) -> (d0, d1)>")]
+    src = (f"{''.join(f'{k} = {v}' + chr(10) for k, v in aliases)}module {{\n"
+           f"  func.func @dist() {{\n    " + "\n    ".join(body) + "\n    return\n  }\n}\n")
+    full = np.arange(gshape[0] * gshape[1], dtype=np.float16).reshape(gshape)
+    seed, reads = [], []
+    for i, (r0, r1, c0, c1, space, strides, addr) in enumerate(parts):
+        block = full[r0:r1 + 1, c0:c1 + 1]
+        if store:
+            block = np.zeros_like(block) - 1
+        offs = (np.arange(block.shape[0])[:, None] * strides[0] +
+                np.arange(block.shape[1])[None, :] * strides[1]).reshape(-1)
+        flat = np.zeros(int(offs.max()) + 1, np.float16)
+        flat[offs] = block.reshape(-1)
+        seed.append((space, 0, addr, flat))
+        reads.append((f"part{i}", space, 0, addr, flat.size, "f16"))
+    n_acc = acc_shape[0] * acc_shape[1]
+    bfill = (np.arange(n_acc, dtype=np.float16) + 100) if store else np.zeros(n_acc, np.float16)
+    seed.append(("HBM", 0, out_stick, bfill))
+    reads.append(("out", "HBM", 0, out_stick, n_acc, "f16"))
+    CASES.append(dict(name=name, src=src, func="dist", inputs={}, tol=None, expect_error=None,
+                      seed=seed, reads=reads))
+
+
+def _box_incl(r0, r1, c0, c1):
+    return (f"affine_set<(d0, d1) : (d0 - {r0} >= 0, -d0 + {r1} >= 0, "
+            f"d1 - {c0} >= 0, -d1 + {c1} >= 0)>")
+
+
+# two HBM row bands; the access tile spans both
+_dist_case("dist_load_hbm_rows", (4, 8), [(0, 1, 0, 7, "HBM", [8, 1], 0x100),
+                                          (2, 3, 0, 7, "HBM", [8, 1], 0x200)], (2, 4), (1, 2))
+# HBM left band (row-major) and an LX right band stored column-packed
+_dist_case("dist_load_hbm_lx_cols", (4, 8), [(0, 3, 0, 3, "HBM", [4, 1], 0x100),
+                                             (0, 3, 4, 7, "LX", [1, 4], 0x800)], (4, 6), (0, 1))
+# only part of the access tile is covered: uncovered elements load as zero
+_dist_case("dist_load_partial_cover", (4, 8), [(0, 3, 0, 3, "HBM", [4, 1], 0x100),
+                                               (2, 3, 4, 7, "HBM", [4, 1], 0x200)], (4, 8), (0, 0))
+# store through a distributed view into HBM and LX partitions
+_dist_case("dist_store_hbm_lx", (4, 8), [(0, 1, 0, 7, "LX", [8, 1], 0x400),
+                                         (2, 3, 0, 7, "HBM", [1, 2], 0x200)], (3, 5), (1, 2),
+           store=True)

@@ -3,7 +3,9 @@
 Usage (in a checkout that has the reference at REFERENCE_ROOT, default
 /root/reference):
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_golden.py [REFERENCE_ROOT] [CASE_NAME ...]
+
+With case names, only those fixtures are regenerated.
 
 For every case in ``cases.py`` it stores the KTIR source, function name,
 inputs, and either the reference outputs or the name and message of the
@@ -13,6 +15,7 @@ the tests read the committed fixtures.
 
 from __future__ import annotations
 
+import json
 import os
 import sys
 import time
@@ -25,6 +28,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 
 def main() -> None:
     ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    only = set(sys.argv[2:])
     sys.dont_write_bytecode = True
     sys.path.insert(0, ref_root)
     sys.path.insert(0, REPO)
@@ -35,6 +39,8 @@ def main() -> None:
     from cases import CASES
 
     for c in CASES:
+        if only and c["name"] not in only:
+            continue
         interp = KTIRInterpreter()
         interp.load(c["src"])
         kw = {k: v.copy() for k, v in c["inputs"].items()}
@@ -42,9 +48,29 @@ def main() -> None:
                "tol": np.array(-1.0 if c["tol"] is None else c["tol"])}
         for k, v in c["inputs"].items():
             rec["in__" + k] = v
+        seeded = "seed" in c
+        if seeded:
+            # memory seeded at fixed addresses before the call (HBM sticks, LX
+            # bytes) through the _prepare_execution hook, read back after it
+            rec["seed_meta"] = np.array(json.dumps([[sp, core, addr] for sp, core, addr, _ in c["seed"]]))
+            rec["reads_meta"] = np.array(json.dumps(c["reads"]))
+            for i, (_, _, _, arr) in enumerate(c["seed"]):
+                rec[f"seed__{i}"] = arr
+            orig = interp._prepare_execution
+
+            def prep(grid, _orig=orig, _c=c, _interp=interp):
+                _orig(grid)
+                for sp, core, addr, arr in _c["seed"]:
+                    mem = _interp.memory.hbm if sp == "HBM" else _interp.memory.get_lx(core)
+                    mem.write(addr, arr.copy())
+            interp._prepare_execution = prep
         t0 = time.time()
         try:
             out = interp.execute_function(c["func"], **kw)
+            if seeded:
+                for name, sp, core, addr, n, dt in c["reads"]:
+                    mem = interp.memory.hbm if sp == "HBM" else interp.memory.get_lx(core)
+                    rec["out__" + name] = mem.read(addr, n, dt)
             for k, v in out.items():
                 # unchanged buffers are not stored twice
                 if not np.array_equal(v, c["inputs"][k], equal_nan=True):

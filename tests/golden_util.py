@@ -19,11 +19,38 @@ def load_golden(name):
     for k, v in inputs.items():
         outputs.setdefault(k, v)
     tol = float(z["tol"])
+    seed, reads = None, None
+    if "seed_meta" in z.files:
+        import json
+        seed = [(sp, core, addr, z[f"seed__{i}"])
+                for i, (sp, core, addr) in enumerate(json.loads(str(z["seed_meta"])))]
+        reads = [tuple(r) for r in json.loads(str(z["reads_meta"]))]
     return {
         "src": str(z["src"]), "func": str(z["func"]), "inputs": inputs, "outputs": outputs,
         "tol": None if tol < 0 else tol, "error": str(z["error"]),
         "error_msg": str(z["error_msg"]) if "error_msg" in z.files else "",
+        "seed": seed, "reads": reads,
     }
+
+
+def run_seeded(interp, g):
+    """Run a golden case whose memory is seeded at fixed addresses (HBM sticks,
+    LX bytes) through the `_prepare_execution` hook, as the reference's own
+    tests do; returns the regions named by the case, read back after the call."""
+    orig = interp._prepare_execution
+
+    def prep(grid):
+        orig(grid)
+        for sp, core, addr, arr in g["seed"]:
+            mem = interp.memory.hbm if sp == "HBM" else interp.memory.get_lx(core)
+            mem.write(addr, arr.copy())
+    interp._prepare_execution = prep
+    interp.execute_function(g["func"], **{k: v.copy() for k, v in g["inputs"].items()})
+    out = {}
+    for name, sp, core, addr, n, dt in g["reads"]:
+        mem = interp.memory.hbm if sp == "HBM" else interp.memory.get_lx(core)
+        out[name] = mem.read(addr, n, dt)
+    return out
 
 
 def max_rel_err(got, want, floor=1e-3):

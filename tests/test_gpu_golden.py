@@ -3,7 +3,7 @@
 import numpy as np
 import pytest
 
-from golden_util import assert_matches, golden_names, load_golden
+from golden_util import assert_matches, golden_names, load_golden, run_seeded
 
 pytestmark = pytest.mark.gpu
 
@@ -14,6 +14,11 @@ def test_b200_matches_reference(name):
     g = load_golden(name)
     interp = KTIRInterpreter()
     interp.load(g["src"])
+    if g["seed"] is not None:
+        out = run_seeded(interp, g)
+        for k, want in g["outputs"].items():
+            assert_matches(f"{name}:{k}", out[k], want, g["tol"])
+        return
     kw = {k: v.copy() for k, v in g["inputs"].items()}
     if g["error"]:
         with pytest.raises(Exception) as ei:

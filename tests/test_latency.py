@@ -117,3 +117,24 @@ def test_indirect_sticks_follow_index_values():
     inputs[idx_name][:] = 0
     same = interp.estimate_latency(c["func"], **inputs).counters[0].total_bytes
     assert same <= spread
+
+
+def test_seeded_distributed_cases_trace_on_the_host():
+    """Distributed / LX view programs trace (and get a latency report) without a GPU."""
+    from golden_util import golden_names, load_golden
+    for name in golden_names():
+        g = load_golden(name)
+        if g["seed"] is None:
+            continue
+        interp = KTIRInterpreter(latency_config=HardwareConfig())
+        interp.load(g["src"])
+        orig = interp._prepare_execution
+
+        def prep(grid, _o=orig, _g=g, _i=interp):
+            _o(grid)
+            for sp, core, addr, arr in _g["seed"]:
+                mem = _i.memory.hbm if sp == "HBM" else _i.memory.get_lx(core)
+                mem.write(addr, arr.copy())
+        interp._prepare_execution = prep
+        rep = interp.estimate_latency(g["func"])
+        assert rep.kernel_cycles >= 0

@@ -10,6 +10,9 @@ from oracle.interp import OracleInterpreter
 @pytest.mark.parametrize("name", golden_names())
 def test_oracle_matches_reference(name):
     g = load_golden(name)
+    if g["seed"] is not None:
+        pytest.skip("distributed / LX views are checked on the GPU against the recorded "
+                    "reference outputs; the oracle does not restate them")
     o = OracleInterpreter()
     o.load(g["src"])
     kw = {k: v.copy() for k, v in g["inputs"].items()}
