@@ -173,12 +173,6 @@ typedef struct {
   int32_t add_zero;            /* epilogue adds +0.0 (normalises -0) as outs-init does */
   int32_t pad;
   int32_t* status;             /* device status word (KTIR_STATUS_TIMEOUT) */
-  /* Optional scratch of ktir_gemm_workspace_bytes(m, n, k) bytes, 256-byte
-   * aligned, zero on first use and left zero after each call: with it the
-   * tiles of a last, partly filled wave are split in K across two SMs.  NULL
-   * (or too small) = no split, same result within f32 rounding. */
-  void* workspace;
-  int64_t workspace_bytes;
 } KtirGemmDesc;
 
 /* Causal flash attention over [bh, seq, d] f16 tensors laid out as
@@ -255,9 +249,6 @@ int ktir_wait_selftest(int32_t* status, uint32_t spin_limit, void* stream);
 /* tcgen05 GEMM (replaces the linalg.matmul K loop, ktir_cpu/dialects/linalg_ops.py:273-297
  * with ops/arith_ops.py:403-419, for whole-matrix tilings). */
 int ktir_gemm_f16(const KtirGemmDesc* desc, void* stream);
-/* Workspace bytes ktir_gemm_f16 can use for an m x n x k product on the
- * current device (0 = it would not split any tile; -1 = no device). */
-int64_t ktir_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k);
 
 /* Causal attention (replaces the online-softmax scf.for of matmul / reduce /
  * exp ops the attention rewrite recognises). */

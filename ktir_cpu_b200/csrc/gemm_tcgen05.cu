@@ -4,13 +4,8 @@
 // pass over B).
 //
 // Persistent: one CTA per SM walks 128x256 output tiles (tile t, t + grid,
-// ...).  When the tiles leave a last, partly filled wave of at most half the
-// SMs, those tiles are split in K across two CTAs each (given a workspace):
-// both halves write f32 row partials, and per row the half that arrives
-// second adds half 0 + half 1 and stores f16, so every SM ends within half a
-// tile of the others.  The accumulator is double-buffered in TMEM
-// (2 x 256 columns), so the epilogue of one tile overlaps the main loop of
-// the next:
+// ...).  The accumulator is double-buffered in TMEM (2 x 256 columns), so the
+// epilogue of one tile overlaps the main loop of the next:
 //   warp 0      one thread issues TMA loads: A box 64(k) x 128(m), four B
 //               boxes 64(n) x 64(k), 128-byte swizzle, into a 4-stage ring
 //               that runs continuously across tiles
@@ -49,38 +44,7 @@ struct GemmParams {
   int m, n, k;
   int add_zero;
   int* status;
-  int split_base;     // first tile split in K (n_tiles = no split)
-  int* counters;      // per split tile and row: halves finished (0 on entry and exit)
-  float* partials;    // per split tile and half: 128 x 256 f32 row partials
 };
-
-// The work units of CTA b: full tiles b, b + G, ... below split_base, then
-// (if b < 2 * (n_tiles - split_base)) half h = b of split tile split_base + h/2.
-struct Unit {
-  int tile, kt0, kt1, half;   // half -1 = whole K
-};
-
-__device__ __forceinline__ int unit_count(int b, int G, int split_base, int n_tiles) {
-  const int full = split_base > b ? (split_base - b + G - 1) / G : 0;
-  return full + (b < 2 * (n_tiles - split_base) ? 1 : 0);
-}
-
-__device__ __forceinline__ Unit unit_at(int i, int b, int G, int split_base, int KT) {
-  const int full = split_base > b ? (split_base - b + G - 1) / G : 0;
-  Unit u;
-  if (i < full) {
-    u.tile = b + i * G;
-    u.kt0 = 0;
-    u.kt1 = KT;
-    u.half = -1;
-  } else {
-    u.tile = split_base + b / 2;
-    u.half = b & 1;
-    u.kt0 = u.half * (KT / 2);
-    u.kt1 = u.kt0 + KT / 2;
-  }
-  return u;
-}
 
 __global__ void __launch_bounds__(192, 1)
     k_gemm_tcgen05(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
@@ -99,7 +63,6 @@ __global__ void __launch_bounds__(192, 1)
   const int lane = threadIdx.x & 31;
   const int MT = p.m / BM;
   const int n_tiles = MT * (p.n / BN);
-  const int n_units = unit_count(blockIdx.x, gridDim.x, p.split_base, n_tiles);
   const int KT = p.k / BK;
   volatile int* abort = &abort_flag;
 
@@ -129,11 +92,10 @@ __global__ void __launch_bounds__(192, 1)
       tma_prefetch_desc(&ta);
       tma_prefetch_desc(&tb);
       uint32_t g = 0;   // k steps issued so far, across tiles
-      for (int i = 0; i < n_units && !*abort; ++i) {
-        const Unit u = unit_at(i, blockIdx.x, gridDim.x, p.split_base, KT);
-        const int m0 = (u.tile % MT) * BM;
-        const int n0 = (u.tile / MT) * BN;
-        for (int kt = u.kt0; kt < u.kt1; ++kt, ++g) {
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+        const int m0 = (t % MT) * BM;
+        const int n0 = (t / MT) * BN;
+        for (int kt = 0; kt < KT; ++kt, ++g) {
           const int s = g % STAGES;
           if (!mbar_wait(smem_u32(&empty_bar[s]), ((g / STAGES) & 1) ^ 1, abort)) break;
           const uint32_t fb = smem_u32(&full_bar[s]);
@@ -151,15 +113,15 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(BM, BN, 0, 1);
       uint32_t g = 0;
-      for (int i = 0; i < n_units && !*abort; ++i) {
-        const Unit u = unit_at(i, blockIdx.x, gridDim.x, p.split_base, KT);
+      int i = 0;   // local tile count
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++i) {
         const int b = i & 1;
         // accumulator b was last drained by the epilogue of local tile i - 2
         if (i >= 2 && !mbar_wait(smem_u32(&acc_empty[b]), ((i - 2) >> 1) & 1, abort)) break;
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(b * BN);
         bool ok = true;
-        for (int kt = u.kt0; kt < u.kt1; ++kt, ++g) {
+        for (int kt = 0; kt < KT; ++kt, ++g) {
           const int s = g % STAGES;
           if (!mbar_wait(smem_u32(&full_bar[s]), (g / STAGES) & 1, abort)) {
             ok = false;
@@ -175,7 +137,7 @@ __global__ void __launch_bounds__(192, 1)
             // B: MN-major, 16 k = 16 rows of 128 bytes further; 64-column
             // groups 8 KiB apart (LBO), 8-row groups 1 KiB apart (SBO)
             const uint64_t bd = sdesc_sw128(b_addr + kk * 16 * 128, B_BOX_BYTES, 1024);
-            mma_f16(acc, ad, bd, idesc, (kt != u.kt0) || kk != 0);
+            mma_f16(acc, ad, bd, idesc, (kt | kk) != 0);
           }
           mma_commit(smem_u32(&empty_bar[s]));
         }
@@ -188,77 +150,34 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;
     const int row = 32 * q + lane;
     const float z = p.add_zero ? 0.0f : -0.0f;
-    for (int i = 0; i < n_units; ++i) {
-      const Unit u = unit_at(i, blockIdx.x, gridDim.x, p.split_base, KT);
+    int i = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
       const int b = i & 1;
       const bool ok = mbar_wait(smem_u32(&acc_full[b]), (i >> 1) & 1, abort);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const int m0 = (u.tile % MT) * BM;
-      const int n0 = (u.tile / MT) * BN;
+      const int m0 = (t % MT) * BM;
+      const int n0 = (t / MT) * BN;
       __half* crow = p.c + (long long)(m0 + row) * p.ldc + n0;
       const uint32_t acc = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * BN);
-      if (u.half < 0) {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(acc + c, r);
-          tmem_ld_wait();
-          if (c + 32 == BN) {
-            // every column of this accumulator is in registers: hand it back
-            tc_fence_before();
-            mbar_arrive(smem_u32(&acc_empty[b]));
-          }
-          __half2 h[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            h[j] = __floats2half2_rn(__uint_as_float(r[2 * j]) + z, __uint_as_float(r[2 * j + 1]) + z);
-          uint4* dst = reinterpret_cast<uint4*>(crow + c);
-          const uint4* src = reinterpret_cast<const uint4*>(h);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dst[j] = src[j];
-        }
-        continue;
-      }
-      // half of a split tile: publish this row's f32 partial, then the
-      // second half to arrive for this row adds half 0 + half 1
-      const int st = u.tile - p.split_base;
-      float* mine = p.partials + ((size_t)(2 * st + u.half) * BM + row) * BN;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
         tmem_ld32(acc + c, r);
         tmem_ld_wait();
         if (c + 32 == BN) {
+          // every column of this accumulator is in registers: hand it back
           tc_fence_before();
           mbar_arrive(smem_u32(&acc_empty[b]));
         }
-        float4* dst = reinterpret_cast<float4*>(mine + c);
+        __half2 h[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-      }
-      __threadfence();
-      int* cnt = p.counters + st * BM + row;
-      if (atomicAdd(cnt, 1) == 1) {
-        __threadfence();
-        const float* h0 = p.partials + ((size_t)(2 * st) * BM + row) * BN;
-        const float* h1 = h0 + (size_t)BM * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 8) {
-          const float4 a0 = __ldcg(reinterpret_cast<const float4*>(h0 + c));
-          const float4 a1 = __ldcg(reinterpret_cast<const float4*>(h0 + c + 4));
-          const float4 b0 = __ldcg(reinterpret_cast<const float4*>(h1 + c));
-          const float4 b1 = __ldcg(reinterpret_cast<const float4*>(h1 + c + 4));
-          __half2 h[4];
-          h[0] = __floats2half2_rn(a0.x + b0.x + z, a0.y + b0.y + z);
-          h[1] = __floats2half2_rn(a0.z + b0.z + z, a0.w + b0.w + z);
-          h[2] = __floats2half2_rn(a1.x + b1.x + z, a1.y + b1.y + z);
-          h[3] = __floats2half2_rn(a1.z + b1.z + z, a1.w + b1.w + z);
-          *reinterpret_cast<uint4*>(crow + c) = *reinterpret_cast<const uint4*>(h);
-        }
-        *cnt = 0;
+        for (int j = 0; j < 16; ++j)
+          h[j] = __floats2half2_rn(__uint_as_float(r[2 * j]) + z, __uint_as_float(r[2 * j + 1]) + z);
+        uint4* dst = reinterpret_cast<uint4*>(crow + c);
+        const uint4* src = reinterpret_cast<const uint4*>(h);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dst[j] = src[j];
       }
     }
   }
@@ -306,38 +225,7 @@ bool make_map(CUtensorMap* m, const void* base, long long rows, long long cols, 
 
 thread_local char g_msg[256];
 
-int sm_count() {
-  static int n_sm = 0;
-  if (!n_sm) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      n_sm = 0;
-  }
-  return n_sm;
-}
-
-// tiles of the last, partial wave that are split in K: only when that wave
-// fills at most half the SMs (two halves each still fit) and K splits evenly
-long long split_tiles(long long m, long long n, long long k, int n_sm) {
-  if (m % BM || n % BN || k % (2 * BK) || n_sm < 2) return 0;
-  const long long tiles = (m / BM) * (n / BN);
-  const long long rem = tiles % n_sm;
-  if (tiles < n_sm || rem == 0 || 2 * rem > n_sm) return 0;
-  return rem;
-}
-
-size_t counter_bytes(long long split) { return ((size_t)split * BM * 4 + 255) & ~(size_t)255; }
-size_t workspace_bytes(long long split) {
-  return split > 0 ? counter_bytes(split) + (size_t)split * 2 * BM * BN * 4 : 0;
-}
-
 }  // namespace
-
-extern "C" int64_t ktir_gemm_workspace_bytes(int64_t m, int64_t n, int64_t k) {
-  const int n_sm = sm_count();
-  return n_sm < 1 ? -1 : (int64_t)workspace_bytes(split_tiles(m, n, k, n_sm));
-}
 
 extern "C" const char* ktir_gemm_error(void) { return g_msg; }
 
@@ -367,21 +255,16 @@ extern "C" int ktir_gemm_f16(const KtirGemmDesc* d, void* stream) {
   p.k = (int)d->k;
   p.add_zero = d->add_zero;
   p.status = static_cast<int*>(d->status);
-  const int n_sm = sm_count();
-  if (n_sm < 1) return KTIR_ERR_CUDA;
+  static int n_sm = 0;
+  if (!n_sm) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm < 1)
+      return KTIR_ERR_CUDA;
+  }
   const long long tiles = (d->m / BM) * (d->n / BN);
   if (tiles > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
   const unsigned grid = (unsigned)(tiles < n_sm ? tiles : n_sm);
-  const long long split = split_tiles(d->m, d->n, d->k, n_sm);
-  p.split_base = (int)tiles;
-  p.counters = nullptr;
-  p.partials = nullptr;
-  if (split > 0 && d->workspace != nullptr &&
-      d->workspace_bytes >= workspace_bytes(split) && !(reinterpret_cast<uintptr_t>(d->workspace) & 255)) {
-    p.split_base = (int)(tiles - split);
-    p.counters = static_cast<int*>(d->workspace);
-    p.partials = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + counter_bytes(split));
-  }
   k_gemm_tcgen05<<<grid, 192, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   return cudaGetLastError() == cudaSuccess ? KTIR_OK : KTIR_ERR_CUDA;
 }

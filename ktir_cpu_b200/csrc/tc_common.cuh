@@ -63,7 +63,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (i > 64) __nanosleep(32);
+    // mbarrier.try_wait already suspends the thread for a while; back off
+    // further only after a long wait, so a wake-up is not delayed by a sleep
+    if (i > 4096) __nanosleep(32);
   }
   *abort = 1;
   return false;

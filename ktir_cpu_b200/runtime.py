@@ -104,8 +104,7 @@ class KtirGemmDesc(C.Structure):
     _fields_ = [("a", C.c_void_p), ("b", C.c_void_p), ("c", C.c_void_p),
                 ("lda", C.c_int64), ("ldb", C.c_int64), ("ldc", C.c_int64),
                 ("m", C.c_int64), ("n", C.c_int64), ("k", C.c_int64),
-                ("add_zero", C.c_int32), ("pad", C.c_int32), ("status", C.c_void_p),
-                ("workspace", C.c_void_p), ("workspace_bytes", C.c_int64)]
+                ("add_zero", C.c_int32), ("pad", C.c_int32), ("status", C.c_void_p)]
 
 
 class KtirFmhaDesc(C.Structure):
@@ -117,7 +116,7 @@ class KtirFmhaDesc(C.Structure):
 EXPORTS = ["ktir_version", "ktir_last_error", "ktir_device_count", "ktir_ew",
            "ktir_softmax_rows", "ktir_gather_rmw", "ktir_reduce", "ktir_matmul",
            "ktir_offsets", "ktir_indirect", "ktir_gemm_f16", "ktir_fmha_f16",
-           "ktir_wait_selftest", "ktir_gemm_workspace_bytes"]
+           "ktir_wait_selftest"]
 
 _LIB: Optional[C.CDLL] = None
 
@@ -157,8 +156,6 @@ def load_library(build_if_missing: bool = False) -> C.CDLL:
     lib.ktir_wait_selftest.argtypes = [vp, C.c_uint32, vp]
     for name in EXPORTS:
         getattr(lib, name).restype = C.c_int if name != "ktir_last_error" else C.c_char_p
-    lib.ktir_gemm_workspace_bytes.argtypes = [C.c_int64, C.c_int64, C.c_int64]
-    lib.ktir_gemm_workspace_bytes.restype = C.c_int64
     _LIB = lib
     return lib
 

@@ -134,10 +134,6 @@ def match_gemm(low, stores: List[Store]):
     lib = R.load_library()
     sa, sb, sc = low.slots[abuf.index], low.slots[bbuf.index], low.slots[cbuf.index]
     a_off, b_off, c_off = i_lo * lda * 2, j_lo * 2, (i_lo * ldc + j_lo) * 2
-    # scratch for splitting the last partial wave's tiles in K (zero-filled)
-    ws_bytes = int(lib.ktir_gemm_workspace_bytes(M, N, K))
-    ws = low.dev.bytes(ws_bytes) if ws_bytes > 0 else None
-    ws_ptr = ws.data_ptr() if ws is not None else None
 
     def run(bufs, stream, status):
         d = R.KtirGemmDesc()
@@ -146,8 +142,6 @@ def match_gemm(low, stores: List[Store]):
         d.m, d.n, d.k = M, N, K
         d.add_zero = 1
         d.status = status
-        if ws_ptr is not None:
-            d.workspace, d.workspace_bytes = ws_ptr, ws_bytes
         R.check(lib.ktir_gemm_f16(C.byref(d), stream), "ktir_gemm_f16")
 
     from .lower import Launch, Plan
