@@ -488,3 +488,296 @@ _dist_case("dist_load_partial_cover", (4, 8), [(0, 3, 0, 3, "HBM", [4, 1], 0x100
 _dist_case("dist_store_hbm_lx", (4, 8), [(0, 1, 0, 7, "LX", [8, 1], 0x400),
                                          (2, 3, 0, 7, "HBM", [1, 2], 0x200)], (3, 5), (1, 2),
            store=True)
+
+
+# --- model-style kernels through the generic executor ----------------------------------
+def _layernorm(rows=64, cols=256, grid=4, chunk=8, eps=1e-5):
+    """y = (x - mean) / sqrt(var + eps) * w + b per row, statistics in f32."""
+    per = rows // grid
+    t32, t16 = _tt((chunk, cols), "f32"), _tt((chunk, cols), "f16")
+    r32 = _tt((chunk,), "f32")
+    bm = ("[affine_map<(d0, d1) -> (d0, d1)>, affine_map<(d0, d1) -> (d0)>, "
+          "affine_map<(d0, d1) -> (d0, d1)>]")
+    wm = ("[affine_map<(d0, d1) -> (d0, d1)>, affine_map<(d0, d1) -> (d1)>, "
+          "affine_map<(d0, d1) -> (d0, d1)>]")
+    body = [
+        "%c0 = arith.constant 0 : index",
+        f"%per = arith.constant {per} : index",
+        f"%step = arith.constant {chunk} : index",
+        "%core = ktdp.get_compute_tile_id : index",
+        "%row0 = arith.muli %core, %per : index",
+        "%row1 = arith.addi %row0, %per : index",
+        _view("%xv", "%x", (rows, cols), "f16"),
+        _view("%yv", "%y", (rows, cols), "f16"),
+        _view("%wv", "%w", (cols,), "f16"),
+        _view("%bv", "%b", (cols,), "f16"),
+        _tile("%wt", "%wv", ["%c0"], (cols,), "f16", (cols,)),
+        _tile("%bt", "%bv", ["%c0"], (cols,), "f16", (cols,)),
+        f"%w16 = ktdp.load %wt : {_at((cols,))} -> {_tt((cols,), 'f16')}",
+        f"%b16 = ktdp.load %bt : {_at((cols,))} -> {_tt((cols,), 'f16')}",
+        f"%w = arith.extf %w16 : {_tt((cols,), 'f16')} to {_tt((cols,), 'f32')}",
+        f"%bb = arith.extf %b16 : {_tt((cols,), 'f16')} to {_tt((cols,), 'f32')}",
+        f"%n = arith.constant {float(cols)} : f32",
+        f"%eps = arith.constant {eps} : f32",
+        "%zero = arith.constant 0.0 : f32",
+        f"scf.for %r = %row0 to %row1 step %step {{\n"
+        f"      {_tile('%xt', '%xv', ['%r', '%c0'], (rows, cols), 'f16', (chunk, cols))}\n"
+        f"      %x16 = ktdp.load %xt : {_at((chunk, cols))} -> {t16}\n"
+        f"      %xf = arith.extf %x16 : {t16} to {t32}\n"
+        f"      %s0 = tensor.splat %zero : {r32}\n"
+        f"      %s = linalg.reduce {{ arith.addf }} ins(%xf : {t32}) outs(%s0 : {r32}) dimensions = [1]\n"
+        f"      %nn = tensor.splat %n : {r32}\n"
+        f"      %mean = arith.divf %s, %nn : {r32}\n"
+        f"      %e0 = tensor.empty() : {t32}\n"
+        f"      %dx = linalg.generic {{indexing_maps = {bm}, iterator_types = [\"parallel\", \"parallel\"]}} ins(%xf, %mean : {t32}, {r32}) outs(%e0 : {t32}) {{\n"
+        f"      ^bb0(%a: f32, %m: f32, %o: f32):\n"
+        f"        %d = arith.subf %a, %m : f32\n"
+        f"        linalg.yield %d : f32\n"
+        f"      }} -> {t32}\n"
+        f"      %sq = arith.mulf %dx, %dx : {t32}\n"
+        f"      %v0 = tensor.splat %zero : {r32}\n"
+        f"      %vs = linalg.reduce {{ arith.addf }} ins(%sq : {t32}) outs(%v0 : {r32}) dimensions = [1]\n"
+        f"      %var = arith.divf %vs, %nn : {r32}\n"
+        f"      %ee = tensor.splat %eps : {r32}\n"
+        f"      %ve = arith.addf %var, %ee : {r32}\n"
+        f"      %rstd = math.rsqrt %ve : {r32}\n"
+        f"      %e1 = tensor.empty() : {t32}\n"
+        f"      %nrm = linalg.generic {{indexing_maps = {bm}, iterator_types = [\"parallel\", \"parallel\"]}} ins(%dx, %rstd : {t32}, {r32}) outs(%e1 : {t32}) {{\n"
+        f"      ^bb0(%a: f32, %q: f32, %o: f32):\n"
+        f"        %p = arith.mulf %a, %q : f32\n"
+        f"        linalg.yield %p : f32\n"
+        f"      }} -> {t32}\n"
+        f"      %e2 = tensor.empty() : {t32}\n"
+        f"      %sc = linalg.generic {{indexing_maps = {wm}, iterator_types = [\"parallel\", \"parallel\"]}} ins(%nrm, %w : {t32}, {_tt((cols,), 'f32')}) outs(%e2 : {t32}) {{\n"
+        f"      ^bb0(%a: f32, %g: f32, %o: f32):\n"
+        f"        %p = arith.mulf %a, %g : f32\n"
+        f"        linalg.yield %p : f32\n"
+        f"      }} -> {t32}\n"
+        f"      %e3 = tensor.empty() : {t32}\n"
+        f"      %sh = linalg.generic {{indexing_maps = {wm}, iterator_types = [\"parallel\", \"parallel\"]}} ins(%sc, %bb : {t32}, {_tt((cols,), 'f32')}) outs(%e3 : {t32}) {{\n"
+        f"      ^bb0(%a: f32, %g: f32, %o: f32):\n"
+        f"        %p = arith.addf %a, %g : f32\n"
+        f"        linalg.yield %p : f32\n"
+        f"      }} -> {t32}\n"
+        f"      %y16 = arith.truncf %sh : {t32} to {t16}\n"
+        f"      {_tile('%yt', '%yv', ['%r', '%c0'], (rows, cols), 'f16', (chunk, cols))}\n"
+        f"      ktdp.store %y16, %yt : {t16}, {_at((chunk, cols))}\n"
+        f"    }}",
+    ]
+    return _fn("layernorm", ["x", "w", "b", "y"], body, grid=(grid,))
+
+
+case("layernorm_rows64_cols256", _layernorm(), "layernorm",
+     {"x": (rng.standard_normal((64, 256)) * 3 + 1).astype(np.float16),
+      "w": rng.uniform(0.5, 1.5, 256).astype(np.float16),
+      "b": rng.uniform(-0.5, 0.5, 256).astype(np.float16),
+      "y": np.zeros((64, 256), np.float16)}, tol=1e-2)
+
+
+def _sdpa2d(s=32, d=64, scale=0.125):
+    """O = softmax(Q K^T * scale) V for one [s, d] head on one core, f32 math."""
+    tq16, tq32 = _tt((s, d), "f16"), _tt((s, d), "f32")
+    tk32t = _tt((d, s), "f32")
+    ts = _tt((s, s), "f32")
+    rs = _tt((s,), "f32")
+    bm = ("[affine_map<(d0, d1) -> (d0, d1)>, affine_map<(d0, d1) -> (d0)>, "
+          "affine_map<(d0, d1) -> (d0, d1)>]")
+    body = [
+        "%c0 = arith.constant 0 : index",
+        _view("%qv", "%q", (s, d), "f16"), _view("%kv", "%k", (s, d), "f16"),
+        _view("%vv", "%v", (s, d), "f16"), _view("%ov", "%o", (s, d), "f16"),
+        _tile("%qt", "%qv", ["%c0", "%c0"], (s, d), "f16", (s, d)),
+        _tile("%kt", "%kv", ["%c0", "%c0"], (s, d), "f16", (s, d)),
+        _tile("%vt", "%vv", ["%c0", "%c0"], (s, d), "f16", (s, d)),
+        _tile("%ot", "%ov", ["%c0", "%c0"], (s, d), "f16", (s, d)),
+        f"%q16 = ktdp.load %qt : {_at((s, d))} -> {tq16}",
+        f"%k16 = ktdp.load %kt : {_at((s, d))} -> {tq16}",
+        f"%v16 = ktdp.load %vt : {_at((s, d))} -> {tq16}",
+        f"%qf = arith.extf %q16 : {tq16} to {tq32}",
+        f"%kf = arith.extf %k16 : {tq16} to {tq32}",
+        f"%vf = arith.extf %v16 : {tq16} to {tq32}",
+        f"%kt0 = tensor.empty() : {tk32t}",
+        f"%ktr = linalg.transpose ins(%kf : {tq32}) outs(%kt0 : {tk32t}) permutation = [1, 0]",
+        f"%z = arith.constant 0.0 : f32",
+        f"%s0 = tensor.splat %z : {ts}",
+        f"%sc = linalg.matmul ins(%qf, %ktr : {tq32}, {tk32t}) outs(%s0 : {ts}) -> {ts}",
+        f"%scale = arith.constant {scale} : f32",
+        f"%sp = tensor.splat %scale : {ts}",
+        f"%x = arith.mulf %sc, %sp : {ts}",
+        "%ninf = arith.constant 0xFF800000 : f32",
+        f"%m0 = tensor.splat %ninf : {rs}",
+        f"%m = linalg.reduce {{ arith.maxnumf }} ins(%x : {ts}) outs(%m0 : {rs}) dimensions = [1]",
+        f"%e0 = tensor.empty() : {ts}",
+        f"%e = linalg.generic {{indexing_maps = {bm}, iterator_types = [\"parallel\", \"parallel\"]}} ins(%x, %m : {ts}, {rs}) outs(%e0 : {ts}) {{\n"
+        f"    ^bb0(%a: f32, %b: f32, %o: f32):\n"
+        f"      %dd = arith.subf %a, %b : f32\n"
+        f"      %ex = math.exp %dd : f32\n"
+        f"      linalg.yield %ex : f32\n"
+        f"    }} -> {ts}",
+        f"%l0 = tensor.splat %z : {rs}",
+        f"%l = linalg.reduce {{ arith.addf }} ins(%e : {ts}) outs(%l0 : {rs}) dimensions = [1]",
+        f"%p0 = tensor.empty() : {ts}",
+        f"%p = linalg.generic {{indexing_maps = {bm}, iterator_types = [\"parallel\", \"parallel\"]}} ins(%e, %l : {ts}, {rs}) outs(%p0 : {ts}) {{\n"
+        f"    ^bb0(%a: f32, %b: f32, %o: f32):\n"
+        f"      %dv = arith.divf %a, %b : f32\n"
+        f"      linalg.yield %dv : f32\n"
+        f"    }} -> {ts}",
+        f"%o0 = tensor.splat %z : {tq32}",
+        f"%of = linalg.matmul ins(%p, %vf : {ts}, {tq32}) outs(%o0 : {tq32}) -> {tq32}",
+        f"%o16 = arith.truncf %of : {tq32} to {tq16}",
+        f"ktdp.store %o16, %ot : {tq16}, {_at((s, d))}",
+    ]
+    return _fn("sdpa", ["q", "k", "v", "o"], body)
+
+
+case("sdpa_2d_s32_d64", _sdpa2d(), "sdpa",
+     {"q": rng.standard_normal((32, 64)).astype(np.float16),
+      "k": rng.standard_normal((32, 64)).astype(np.float16),
+      "v": rng.standard_normal((32, 64)).astype(np.float16),
+      "o": np.zeros((32, 64), np.float16)}, tol=1e-2)
+
+
+def _indexed_add(rows=64, cols=32, n_idx=128, grid=2):
+    """out[idx[i], :] += src[i, :] over index chunks, one chunk per core:
+    within a chunk colliding indices do not accumulate (last writer wins),
+    across cores they do."""
+    per = n_idx // grid
+    t = f"{per}x{cols}"
+    body = [
+        "%c0 = arith.constant 0 : index",
+        "%core = ktdp.get_compute_tile_id : index",
+        f"%per = arith.constant {per} : index",
+        "%s = arith.muli %core, %per : index",
+        _view("%ov", "%out", (rows, cols), "f16"),
+        _view("%xv", "%idx", (n_idx,), "i32"),
+        _view("%sv", "%src", (n_idx, cols), "f16"),
+        f"%g = ktdp.construct_indirect_access_tile\n"
+        f"        intermediate_variables(%gi, %gj)\n"
+        f"        %ov[ind(%xv[%s + %gi]), (%gj)] {{\n"
+        f"          variables_space_set = {_box((per, cols))},\n"
+        f"          variables_space_order = {W._ident(2)}\n"
+        f"        }} : memref<{rows}x{cols}xf16>, memref<{n_idx}xi32> -> !ktdp.access_tile<{t}xindex>",
+        _tile("%st", "%sv", ["%s", "%c0"], (n_idx, cols), "f16", (per, cols)),
+        f"%cur = ktdp.load %g : !ktdp.access_tile<{t}xindex> -> tensor<{t}xf16>",
+        f"%add = ktdp.load %st : {_at((per, cols))} -> tensor<{t}xf16>",
+        f"%new = arith.addf %cur, %add : tensor<{t}xf16>",
+        f"ktdp.store %new, %g : tensor<{t}xf16>, !ktdp.access_tile<{t}xindex>",
+    ]
+    return _fn("indexed_add", ["out", "idx", "src"], body, grid=(grid,))
+
+
+case("indexed_add_dups", _indexed_add(), "indexed_add",
+     {"out": rng.standard_normal((64, 32)).astype(np.float16),
+      "idx": rng.integers(0, 48, 128).astype(np.int32),
+      "src": rng.standard_normal((128, 32)).astype(np.float16)})
+
+
+def _paged_attention(n_tok=8, d=128, tile=16, n_tiles=8, n_pages=12, context_len=120,
+                     scale=0.08838834764831843):
+    """One sequence's queries attend over a paged KV cache: logical tile t of
+    the context lives in physical page block_table[t] of k_cache/v_cache
+    [n_pages, tile, d]; an online softmax runs over the tiles (f32 state),
+    keys at positions >= context_len are masked."""
+    tq = _tt((n_tok, d), "f32")
+    tkv16, tkv = _tt((tile, d), "f16"), _tt((tile, d), "f32")
+    tkt = _tt((d, tile), "f32")
+    ts = _tt((n_tok, tile), "f32")
+    rs = _tt((n_tok,), "f32")
+    bm = ("[affine_map<(d0, d1) -> (d0, d1)>, affine_map<(d0, d1) -> (d0)>, "
+          "affine_map<(d0, d1) -> (d0, d1)>]")
+    mm = ("[affine_map<(d0, d1) -> (d0, d1)>, affine_map<(d0, d1) -> (d0, d1)>]")
+    iat_k = (f"%gk = ktdp.construct_indirect_access_tile\n"
+             f"          intermediate_variables(%ki, %kj, %kd)\n"
+             f"          %kcv[ind(%btv[%t]), (%kj), (%kd)] {{\n"
+             f"            variables_space_set = {_box((1, tile, d))},\n"
+             f"            variables_space_order = {W._ident(3)}\n"
+             f"          }} : memref<{n_pages}x{tile}x{d}xf16>, memref<{n_tiles}xi32> -> "
+             f"!ktdp.access_tile<1x{tile}x{d}xindex>")
+    iat_v = iat_k.replace("%gk", "%gv").replace("%kcv", "%vcv").replace("%ki", "%vi") \
+        .replace("%kj", "%vj").replace("%kd", "%vd")
+    body = [
+        "%c0 = arith.constant 0 : index",
+        "%c1 = arith.constant 1 : index",
+        f"%ntl = arith.constant {n_tiles} : index",
+        _view("%qv", "%q", (n_tok, d), "f16"), _view("%ov", "%o", (n_tok, d), "f16"),
+        _view("%kcv", "%k_cache", (n_pages, tile, d), "f16"),
+        _view("%vcv", "%v_cache", (n_pages, tile, d), "f16"),
+        _view("%btv", "%block_table", (n_tiles,), "i32"),
+        _tile("%qt", "%qv", ["%c0", "%c0"], (n_tok, d), "f16", (n_tok, d)),
+        f"%q16 = ktdp.load %qt : {_at((n_tok, d))} -> {_tt((n_tok, d), 'f16')}",
+        f"%qf = arith.extf %q16 : {_tt((n_tok, d), 'f16')} to {tq}",
+        f"%scale = arith.constant {scale} : f32",
+        f"%clen = arith.constant {context_len} : index",
+        f"%ctile = arith.constant {tile} : index",
+        "%ninf = arith.constant 0xFF800000 : f32",
+        "%z = arith.constant 0.0 : f32",
+        f"%m0 = tensor.splat %ninf : {rs}",
+        f"%l0 = tensor.splat %z : {rs}",
+        f"%a0 = tensor.splat %z : {tq}",
+        f"%mf, %lf, %accf = scf.for %t = %c0 to %ntl step %c1 iter_args(%m = %m0, %l = %l0, %acc = %a0) -> ({rs}, {rs}, {tq}) {{\n"
+        f"      {iat_k}\n"
+        f"      {iat_v}\n"
+        f"      %k3 = ktdp.load %gk : !ktdp.access_tile<1x{tile}x{d}xindex> -> {tkv16}\n"
+        f"      %v3 = ktdp.load %gv : !ktdp.access_tile<1x{tile}x{d}xindex> -> {tkv16}\n"
+        f"      %kf = arith.extf %k3 : {tkv16} to {tkv}\n"
+        f"      %vf = arith.extf %v3 : {tkv16} to {tkv}\n"
+        f"      %kt0 = tensor.empty() : {tkt}\n"
+        f"      %ktr = linalg.transpose ins(%kf : {tkv}) outs(%kt0 : {tkt}) permutation = [1, 0]\n"
+        f"      %s0 = tensor.splat %z : {ts}\n"
+        f"      %sc = linalg.matmul ins(%qf, %ktr : {tq}, {tkt}) outs(%s0 : {ts}) -> {ts}\n"
+        f"      %ssp = tensor.splat %scale : {ts}\n"
+        f"      %ss = arith.mulf %sc, %ssp : {ts}\n"
+        f"      %tb = arith.muli %t, %ctile : index\n"
+        f"      %mk0 = tensor.empty() : {ts}\n"
+        f"      %sm = linalg.generic {{indexing_maps = {mm}, iterator_types = [\"parallel\", \"parallel\"]}} ins(%ss : {ts}) outs(%mk0 : {ts}) {{\n"
+        f"      ^bb0(%a: f32, %o: f32):\n"
+        f"        %j = linalg.index 1 : index\n"
+        f"        %pos = arith.addi %tb, %j : index\n"
+        f"        %oob = arith.cmpi sge, %pos, %clen : index\n"
+        f"        %sel = arith.select %oob, %ninf, %a : f32\n"
+        f"        linalg.yield %sel : f32\n"
+        f"      }} -> {ts}\n"
+        f"      %bmx0 = tensor.splat %ninf : {rs}\n"
+        f"      %bmx = linalg.reduce {{ arith.maxnumf }} ins(%sm : {ts}) outs(%bmx0 : {rs}) dimensions = [1]\n"
+        f"      %mn = arith.maximumf %m, %bmx : {rs}\n"
+        f"      %dm = arith.subf %m, %mn : {rs}\n"
+        f"      %al = math.exp %dm : {rs}\n"
+        f"      %pe0 = tensor.empty() : {ts}\n"
+        f"      %p = linalg.generic {{indexing_maps = {bm}, iterator_types = [\"parallel\", \"parallel\"]}} ins(%sm, %mn : {ts}, {rs}) outs(%pe0 : {ts}) {{\n"
+        f"      ^bb0(%a: f32, %b: f32, %o: f32):\n"
+        f"        %dd = arith.subf %a, %b : f32\n"
+        f"        %ex = math.exp %dd : f32\n"
+        f"        linalg.yield %ex : f32\n"
+        f"      }} -> {ts}\n"
+        f"      %ps0 = tensor.splat %z : {rs}\n"
+        f"      %ps = linalg.reduce {{ arith.addf }} ins(%p : {ts}) outs(%ps0 : {rs}) dimensions = [1]\n"
+        f"      %la = arith.mulf %l, %al : {rs}\n"
+        f"      %ln = arith.addf %la, %ps : {rs}\n"
+        f"      %ac0 = tensor.empty() : {tq}\n"
+        f"      %acs = linalg.generic {{indexing_maps = {bm}, iterator_types = [\"parallel\", \"parallel\"]}} ins(%acc, %al : {tq}, {rs}) outs(%ac0 : {tq}) {{\n"
+        f"      ^bb0(%a: f32, %b: f32, %o: f32):\n"
+        f"        %mu = arith.mulf %a, %b : f32\n"
+        f"        linalg.yield %mu : f32\n"
+        f"      }} -> {tq}\n"
+        f"      %pv = linalg.matmul ins(%p, %vf : {ts}, {tkv}) outs(%acs : {tq}) -> {tq}\n"
+        f"      scf.yield %mn, %ln, %pv : {rs}, {rs}, {tq}\n"
+        f"    }}",
+        f"%on0 = tensor.empty() : {tq}",
+        f"%on = linalg.generic {{indexing_maps = {bm}, iterator_types = [\"parallel\", \"parallel\"]}} ins(%accf, %lf : {tq}, {rs}) outs(%on0 : {tq}) {{\n"
+        f"    ^bb0(%a: f32, %b: f32, %o: f32):\n"
+        f"      %dv = arith.divf %a, %b : f32\n"
+        f"      linalg.yield %dv : f32\n"
+        f"    }} -> {tq}",
+        f"%o16 = arith.truncf %on : {tq} to {_tt((n_tok, d), 'f16')}",
+        _tile("%ot", "%ov", ["%c0", "%c0"], (n_tok, d), "f16", (n_tok, d)),
+        f"ktdp.store %o16, %ot : {_tt((n_tok, d), 'f16')}, {_at((n_tok, d))}",
+    ]
+    return _fn("paged_attention", ["q", "k_cache", "v_cache", "block_table", "o"], body)
+
+
+case("paged_attention_8tok_8tiles", _paged_attention(), "paged_attention",
+     {"q": rng.standard_normal((8, 128)).astype(np.float16),
+      "k_cache": rng.standard_normal((12, 16, 128)).astype(np.float16),
+      "v_cache": rng.standard_normal((12, 16, 128)).astype(np.float16),
+      "block_table": rng.permutation(12)[:8].astype(np.int32),
+      "o": np.zeros((8, 128), np.float16)}, tol=1e-2)
