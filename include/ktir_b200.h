@@ -254,6 +254,41 @@ int ktir_gemm_f16(const KtirGemmDesc* desc, void* stream);
  * exp ops the attention rewrite recognises). */
 int ktir_fmha_f16(const KtirFmhaDesc* desc, void* stream);
 
+/* Host staging for calls made with host buffers (the reference keeps a
+ * call's arrays in host memory, ktir_cpu/interpreter.py:137-177 and
+ * ktir_cpu/memory.py:201-288; here they travel to the device and back).
+ * `pinned` is page-locked host memory of at least `bytes`, `device` device
+ * memory of at least `bytes`. */
+typedef struct {
+  const void* host;            /* upload: source; download: destination (void* cast) */
+  void* pinned;
+  void* device;
+  int64_t bytes;
+} KtirHostXfer;
+
+typedef struct {
+  void* dst;
+  const void* src;
+  int64_t bytes;
+} KtirHostCopy;
+
+/* Number of host worker threads the staging copies run on
+ * (KTIR_HOST_THREADS, default min(16, hardware threads)). */
+int ktir_host_threads(void);
+
+/* host -> pinned copies in chunks on the worker threads; each chunk's
+ * host-to-device copy is enqueued on `stream` as soon as it is staged.
+ * Returns once every copy is enqueued (the pinned buffers must then stay
+ * untouched until the stream has passed them). */
+int ktir_host_upload(const KtirHostXfer* x, int n, int device, void* stream);
+
+/* Enqueues the device-to-pinned copies of `x` on `stream` (after whatever the
+ * stream already holds), copies each chunk on to its host destination as soon
+ * as it lands, runs the `extra` host-to-host copies meanwhile, and returns
+ * after all of them and the stream have completed. */
+int ktir_host_download(const KtirHostXfer* x, int n, const KtirHostCopy* extra, int m,
+                       int device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,272 @@
+// Host side of a call made with host (NumPy) buffers: the copies between the
+// caller's pageable arrays and the pinned staging buffers run in page-aligned
+// chunks on a persistent pool of worker threads, and the DMA of each chunk is
+// issued the moment it is staged (upload) or copied out the moment it lands
+// (download), so the PCIe transfer and the host copies overlap.  The
+// reference keeps its simulated HBM in host NumPy arrays and copies whole
+// allocations per access (ktir_cpu/memory.py:131-198); this is the cost of
+// moving a call's arrays to the device and back instead.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <condition_variable>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <deque>
+#include <functional>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "../../include/ktir_b200.h"
+
+int ktir_set_error(int code, const char* msg);
+
+namespace {
+
+constexpr int64_t kMinChunk = 1 << 20;      // below this a copy stays on the calling thread
+constexpr int64_t kChunkAlign = 1 << 16;
+
+int n_workers() {
+  const char* env = getenv("KTIR_HOST_THREADS");
+  int n = env ? atoi(env) : 0;
+  if (n <= 0) {
+    n = (int)std::thread::hardware_concurrency();
+    if (n > 16) n = 16;
+  }
+  return n < 1 ? 1 : n;
+}
+
+// Worker threads live for the whole process (the pool is never destroyed, so
+// no thread is joined or torn down while a static destructor runs).
+class Pool {
+ public:
+  explicit Pool(int n) : n_(n) {
+    for (int i = 0; i < n; ++i) std::thread([this] { loop(); }).detach();
+  }
+  int size() const { return n_; }
+  void submit(std::function<void()> f) {
+    {
+      std::lock_guard<std::mutex> l(mu_);
+      q_.push_back(std::move(f));
+    }
+    cv_.notify_one();
+  }
+
+ private:
+  void loop() {
+    for (;;) {
+      std::function<void()> f;
+      {
+        std::unique_lock<std::mutex> l(mu_);
+        cv_.wait(l, [this] { return !q_.empty(); });
+        f = std::move(q_.front());
+        q_.pop_front();
+      }
+      f();
+    }
+  }
+  int n_;
+  std::mutex mu_;
+  std::condition_variable cv_;
+  std::deque<std::function<void()>> q_;
+};
+
+Pool& pool() {
+  static Pool* p = new Pool(n_workers());
+  return *p;
+}
+
+// completion tracking for one batch of chunk tasks
+struct Batch {
+  std::mutex mu;
+  std::condition_variable cv;
+  std::vector<char> done;
+  int remaining = 0;
+  int error = 0;
+  explicit Batch(size_t n) : done(n, 0), remaining((int)n) {}
+  void finish(size_t i, int err) {
+    {
+      std::lock_guard<std::mutex> l(mu);
+      done[i] = 1;
+      --remaining;
+      if (err) error = err;
+    }
+    cv.notify_all();
+  }
+  void wait_one(size_t i) {
+    std::unique_lock<std::mutex> l(mu);
+    cv.wait(l, [&] { return done[i] != 0; });
+  }
+  void wait_all() {
+    std::unique_lock<std::mutex> l(mu);
+    cv.wait(l, [&] { return remaining == 0; });
+  }
+};
+
+struct Chunk {
+  int xfer;
+  int64_t off, len;
+};
+
+std::vector<Chunk> split(const int64_t* sizes, int n, int workers) {
+  std::vector<Chunk> out;
+  for (int i = 0; i < n; ++i) {
+    const int64_t b = sizes[i];
+    if (b <= 0) continue;
+    int64_t parts = b / kMinChunk;
+    if (parts > workers) parts = workers;
+    if (parts < 1) parts = 1;
+    int64_t step = (b + parts - 1) / parts;
+    step = (step + kChunkAlign - 1) / kChunkAlign * kChunkAlign;
+    for (int64_t off = 0; off < b; off += step) out.push_back({i, off, b - off < step ? b - off : step});
+  }
+  return out;
+}
+
+int cuda_err(cudaError_t e, const char* what) {
+  char buf[256];
+  snprintf(buf, sizeof(buf), "%s: %s", what, cudaGetErrorString(e));
+  return ktir_set_error(KTIR_ERR_CUDA, buf);
+}
+
+// events recorded after each download chunk, reused across calls (per device)
+std::mutex g_ev_mu;
+std::vector<std::vector<cudaEvent_t>> g_events;
+
+int events(int dev, size_t n, std::vector<cudaEvent_t>& out) {
+  std::lock_guard<std::mutex> l(g_ev_mu);
+  if ((int)g_events.size() <= dev) g_events.resize(dev + 1);
+  auto& v = g_events[dev];
+  while (v.size() < n) {
+    cudaEvent_t e;
+    cudaError_t rc = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    if (rc != cudaSuccess) return cuda_err(rc, "ktir_host_download: event");
+    v.push_back(e);
+  }
+  out.assign(v.begin(), v.begin() + n);
+  return KTIR_OK;
+}
+
+}  // namespace
+
+extern "C" int ktir_host_threads(void) { return pool().size(); }
+
+extern "C" int ktir_host_upload(const KtirHostXfer* x, int n, int device, void* stream) {
+  if (n < 0 || (n > 0 && !x)) return ktir_set_error(KTIR_ERR_ARG, "ktir_host_upload: bad transfer list");
+  cudaError_t rc = cudaSetDevice(device);
+  if (rc != cudaSuccess) return cuda_err(rc, "ktir_host_upload: device");
+  std::vector<int64_t> sizes(n);
+  for (int i = 0; i < n; ++i) {
+    if (x[i].bytes > 0 && (!x[i].host || !x[i].pinned || !x[i].device))
+      return ktir_set_error(KTIR_ERR_ARG, "ktir_host_upload: null buffer");
+    sizes[i] = x[i].bytes;
+  }
+  Pool& P = pool();
+  const std::vector<Chunk> chunks = split(sizes.data(), n, P.size());
+  auto st = static_cast<cudaStream_t>(stream);
+  auto dma = [&](const Chunk& c) {
+    return cudaMemcpyAsync(static_cast<char*>(x[c.xfer].device) + c.off,
+                           static_cast<const char*>(x[c.xfer].pinned) + c.off, (size_t)c.len,
+                           cudaMemcpyHostToDevice, st);
+  };
+  if (chunks.size() == 1 && chunks[0].len < kMinChunk) {
+    const Chunk& c = chunks[0];
+    memcpy(static_cast<char*>(x[c.xfer].pinned) + c.off,
+           static_cast<const char*>(x[c.xfer].host) + c.off, (size_t)c.len);
+    rc = dma(c);
+    return rc == cudaSuccess ? KTIR_OK : cuda_err(rc, "ktir_host_upload: copy");
+  }
+  auto batch = std::make_shared<Batch>(chunks.size());
+  for (size_t i = 0; i < chunks.size(); ++i) {
+    const Chunk c = chunks[i];
+    void* dst = static_cast<char*>(x[c.xfer].pinned) + c.off;
+    const void* src = static_cast<const char*>(x[c.xfer].host) + c.off;
+    P.submit([batch, i, dst, src, c] {
+      memcpy(dst, src, (size_t)c.len);
+      batch->finish(i, 0);
+    });
+  }
+  int ret = KTIR_OK;
+  for (size_t i = 0; i < chunks.size(); ++i) {
+    batch->wait_one(i);
+    if (ret == KTIR_OK) {
+      rc = dma(chunks[i]);
+      if (rc != cudaSuccess) ret = cuda_err(rc, "ktir_host_upload: copy");
+    }
+  }
+  return ret;
+}
+
+extern "C" int ktir_host_download(const KtirHostXfer* x, int n, const KtirHostCopy* extra, int m,
+                                  int device, void* stream) {
+  if (n < 0 || m < 0 || (n > 0 && !x) || (m > 0 && !extra))
+    return ktir_set_error(KTIR_ERR_ARG, "ktir_host_download: bad transfer list");
+  cudaError_t rc = cudaSetDevice(device);
+  if (rc != cudaSuccess) return cuda_err(rc, "ktir_host_download: device");
+  std::vector<int64_t> sizes(n), esizes(m);
+  for (int i = 0; i < n; ++i) {
+    if (x[i].bytes > 0 && (!x[i].host || !x[i].pinned || !x[i].device))
+      return ktir_set_error(KTIR_ERR_ARG, "ktir_host_download: null buffer");
+    sizes[i] = x[i].bytes;
+  }
+  for (int i = 0; i < m; ++i) {
+    if (extra[i].bytes > 0 && (!extra[i].dst || !extra[i].src))
+      return ktir_set_error(KTIR_ERR_ARG, "ktir_host_download: null host copy");
+    esizes[i] = extra[i].bytes;
+  }
+  Pool& P = pool();
+  auto st = static_cast<cudaStream_t>(stream);
+  const std::vector<Chunk> chunks = split(sizes.data(), n, P.size());
+  const std::vector<Chunk> hchunks = split(esizes.data(), m, P.size());
+  std::vector<cudaEvent_t> ev;
+  int ret = events(device, chunks.size(), ev);
+  if (ret != KTIR_OK) return ret;
+  // the device-to-host chunks, in order, each followed by its event
+  for (size_t i = 0; i < chunks.size() && ret == KTIR_OK; ++i) {
+    const Chunk& c = chunks[i];
+    rc = cudaMemcpyAsync(static_cast<char*>(x[c.xfer].pinned) + c.off,
+                         static_cast<const char*>(x[c.xfer].device) + c.off, (size_t)c.len,
+                         cudaMemcpyDeviceToHost, st);
+    if (rc == cudaSuccess) rc = cudaEventRecord(ev[i], st);
+    if (rc != cudaSuccess) ret = cuda_err(rc, "ktir_host_download: copy");
+  }
+  auto batch = std::make_shared<Batch>(chunks.size() + hchunks.size());
+  size_t k = 0;
+  // host-to-host copies first: they need nothing from the device
+  for (const Chunk& c : hchunks) {
+    void* dst = static_cast<char*>(extra[c.xfer].dst) + c.off;
+    const void* src = static_cast<const char*>(extra[c.xfer].src) + c.off;
+    P.submit([batch, k, dst, src, c] {
+      memcpy(dst, src, (size_t)c.len);
+      batch->finish(k, 0);
+    });
+    ++k;
+  }
+  for (size_t i = 0; i < chunks.size(); ++i) {
+    const Chunk c = chunks[i];
+    void* dst = const_cast<char*>(static_cast<const char*>(x[c.xfer].host)) + c.off;
+    const void* src = static_cast<const char*>(x[c.xfer].pinned) + c.off;
+    const cudaEvent_t e = ev[i];
+    const bool issued = ret == KTIR_OK;
+    P.submit([batch, k, dst, src, c, e, issued, device] {
+      int err = 0;
+      if (issued) {
+        cudaSetDevice(device);
+        if (cudaEventSynchronize(e) == cudaSuccess)
+          memcpy(dst, src, (size_t)c.len);
+        else
+          err = KTIR_ERR_CUDA;
+      }
+      batch->finish(k, err);
+    });
+    ++k;
+  }
+  batch->wait_all();
+  // the call's kernels and copies have all completed once the stream has
+  rc = cudaStreamSynchronize(st);
+  if (ret == KTIR_OK && rc != cudaSuccess) ret = cuda_err(rc, "ktir_host_download: synchronize");
+  if (ret == KTIR_OK && batch->error) ret = ktir_set_error(KTIR_ERR_CUDA, "ktir_host_download: event wait failed");
+  return ret;
+}

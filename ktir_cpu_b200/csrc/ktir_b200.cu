@@ -41,6 +41,9 @@ static int check_launch(const char* what) {
   return KTIR_OK;
 }
 
+// shared with the other translation units of the library
+int ktir_set_error(int code, const char* msg) { return set_err(code, msg); }
+
 extern "C" int ktir_version(void) { return 100; }
 extern "C" const char* ktir_last_error(void) { return g_err; }
 extern "C" int ktir_device_count(int* count) {

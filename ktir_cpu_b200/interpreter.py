@@ -18,8 +18,6 @@ schedule depends on tile data.
 from __future__ import annotations
 
 import ctypes as C
-import math
-import os
 from typing import Any, Dict, List, Optional, Tuple
 
 import numpy as np
@@ -151,7 +149,7 @@ class Executable:
         self.dev_tensors = None
         self.latency_tape = None
         self.pinned = None
-        self.pinned_np = None
+        self.status_pinned = None
         self.last_h2d_bytes = self.last_d2h_bytes = 0
         self.bufs = None
         self.arena = None
@@ -199,10 +197,12 @@ class Executable:
                 self.launch(ts, s, b)
         return g
 
-    def check_status(self) -> None:
+    def check_status(self, value: Optional[int] = None) -> None:
+        """Raise for the device status word (read here unless the caller has
+        already downloaded it)."""
         if not self.plan.status_check:
             return
-        v = int(self.status.item())
+        v = int(self.status.item()) if value is None else value
         if v & R.STATUS_NEGATIVE_INDEX:
             self.status.zero_()
             raise IndexError("indirect index from an index view is negative")
@@ -395,84 +395,64 @@ class KTIRInterpreter:
 
         Every allocation of the façade is replaced by a new array holding its
         contents after the call (the caller's input arrays are never written).
-        Host copies run in parallel chunks on a thread pool: into the pinned
-        staging buffers (each chunk's DMA issued as soon as it is staged),
-        out of them after the call, and — overlapped with the device work —
-        the copies of buffers the plan does not write.  Buffers the plan
-        overwrites entirely without reading are not uploaded.  Device and
-        pinned buffers belong to the Executable and are reused by every call
-        with the same signature.
+        The host side runs in the library (ktir_host_upload / ktir_host_download):
+        page-aligned chunks are copied into the pinned staging buffers by its
+        worker threads, each chunk's DMA issued as soon as it is staged; after
+        the plan, each downloaded chunk is copied out as soon as it lands while
+        the copies of buffers the plan does not write run alongside.  Buffers
+        the plan overwrites entirely without reading are not uploaded.  Device
+        and pinned buffers belong to the Executable and are reused by every
+        call with the same signature.
         """
         torch = exe.torch
+        lib = exe.lib
         where = {a: (fac, k) for a, fac, k in self.memory.allocations()}
         arrays = [where[a][0].allocs[where[a][1]] for a in order]
-        pool = _pool()
         if exe.dev_tensors is None:
-            exe.dev_tensors, exe.pinned, exe.pinned_np = [], [], []
+            exe.dev_tensors, exe.pinned = [], []
             for arr in arrays:
                 nb = arr.nbytes
                 exe.dev_tensors.append(torch.empty(nb + 16, dtype=torch.uint8, device=exe.device))
-                pin = torch.empty(max(nb, 1), dtype=torch.uint8, pin_memory=True)
-                exe.pinned.append(pin)
-                exe.pinned_np.append(pin.numpy()[:nb])
+                exe.pinned.append(torch.empty(max(nb, 1), dtype=torch.uint8, pin_memory=True))
             exe.bufs = exe.buffers(exe.dev_tensors)
+            exe.status_pinned = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         stream = torch.cuda.current_stream(exe.device)
+        sp = C.c_void_p(stream.cuda_stream)
+        dev = exe.device.index if exe.device.index is not None else torch.cuda.current_device()
         written = exe.plan.info.get("written")
         skip = exe.plan.info.get("overwritten", set())
-        src = [arr.view(np.uint8).reshape(-1) for arr in arrays]
-        staged = []
-        for i in range(len(order)):
-            if i in skip:
-                continue
-            for a, b in _chunks(src[i].size, _WORKERS):
-                staged.append((i, a, b, pool.submit(np.copyto, exe.pinned_np[i][a:b], src[i][a:b])))
-        h2d = 0
-        for i, a, b, f in staged:
-            f.result()
-            exe.dev_tensors[i][a:b].copy_(exe.pinned[i][a:b], non_blocking=True)
-            h2d += b - a
-        exe.status.zero_()
+        src = [np.ascontiguousarray(arr).view(np.uint8).reshape(-1) for arr in arrays]
+        up = [i for i in range(len(order)) if i not in skip and src[i].size]
+        xs = (R.KtirHostXfer * max(1, len(up)))()
+        for k, i in enumerate(up):
+            xs[k].host, xs[k].pinned = src[i].ctypes.data, exe.pinned[i].data_ptr()
+            xs[k].device, xs[k].bytes = exe.dev_tensors[i].data_ptr(), src[i].size
+        R.check(lib.ktir_host_upload(xs, len(up), dev, sp), "ktir_host_upload")
+        if exe.plan.status_check:
+            exe.status.zero_()
         exe.launch(exe.dev_tensors, stream, exe.bufs)
-        back = [i for i in range(len(order)) if written is None or i in written]
-        d2h = 0
-        for i in back:
-            nb = src[i].size
-            exe.pinned[i][:nb].copy_(exe.dev_tensors[i][:nb], non_blocking=True)
-            d2h += nb
+        back = [i for i in range(len(order)) if (written is None or i in written) and src[i].size]
         results = [np.empty(s_.size, np.uint8) for s_ in src]
-        copies = [pool.submit(np.copyto, results[i][a:b], src[i][a:b])
-                  for i in range(len(order)) if i not in back
-                  for a, b in _chunks(src[i].size, _WORKERS)]
-        stream.synchronize()
-        for f in copies:
-            f.result()
-        exe.check_status()
-        copies = [pool.submit(np.copyto, results[i][a:b], exe.pinned_np[i][a:b])
-                  for i in back for a, b in _chunks(src[i].size, _WORKERS)]
-        for f in copies:
-            f.result()
+        status = np.zeros(1, np.int32)
+        ys = (R.KtirHostXfer * (len(back) + 1))()
+        for k, i in enumerate(back):
+            ys[k].host, ys[k].pinned = results[i].ctypes.data, exe.pinned[i].data_ptr()
+            ys[k].device, ys[k].bytes = exe.dev_tensors[i].data_ptr(), src[i].size
+        n_y = len(back)
+        if exe.plan.status_check:
+            ys[n_y].host, ys[n_y].pinned = status.ctypes.data, exe.status_pinned.data_ptr()
+            ys[n_y].device, ys[n_y].bytes = exe.status.data_ptr(), 4
+            n_y += 1
+        rest = [i for i in range(len(order)) if i not in back and src[i].size]
+        cs = (R.KtirHostCopy * max(1, len(rest)))()
+        for k, i in enumerate(rest):
+            cs[k].dst, cs[k].src, cs[k].bytes = results[i].ctypes.data, src[i].ctypes.data, src[i].size
+        R.check(lib.ktir_host_download(ys, n_y, cs, len(rest), dev, sp), "ktir_host_download")
+        exe.check_status(int(status[0]))
         for i, addr in enumerate(order):
             fac, k = where[addr]
             fac.allocs[k] = results[i].view(arrays[i].dtype)
             fac.borrowed.add(k)
-        exe.last_h2d_bytes, exe.last_d2h_bytes = h2d, d2h
+        exe.last_h2d_bytes = sum(src[i].size for i in up)
+        exe.last_d2h_bytes = sum(src[i].size for i in back)
 
-
-_WORKERS = max(1, min(16, os.cpu_count() or 1))
-_POOL = None
-
-
-def _pool():
-    """Shared thread pool for host staging copies (NumPy copies release the GIL)."""
-    global _POOL
-    if _POOL is None:
-        from concurrent.futures import ThreadPoolExecutor
-        _POOL = ThreadPoolExecutor(max_workers=_WORKERS, thread_name_prefix="ktir-copy")
-    return _POOL
-
-
-def _chunks(n: int, parts: int, min_chunk: int = 1 << 20) -> List[Tuple[int, int]]:
-    """Split [0, n) into at most `parts` page-aligned chunks of at least min_chunk bytes."""
-    k = max(1, min(parts, n // min_chunk))
-    step = ((-(-n // k)) + 4095) & ~4095
-    return [(a, min(n, a + step)) for a in range(0, n, step)] or [(0, 0)]

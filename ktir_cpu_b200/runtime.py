@@ -113,10 +113,19 @@ class KtirFmhaDesc(C.Structure):
                 ("causal", C.c_int32), ("row_stride", C.c_int64), ("status", C.c_void_p)]
 
 
+class KtirHostXfer(C.Structure):
+    _fields_ = [("host", C.c_void_p), ("pinned", C.c_void_p), ("device", C.c_void_p),
+                ("bytes", C.c_int64)]
+
+
+class KtirHostCopy(C.Structure):
+    _fields_ = [("dst", C.c_void_p), ("src", C.c_void_p), ("bytes", C.c_int64)]
+
+
 EXPORTS = ["ktir_version", "ktir_last_error", "ktir_device_count", "ktir_ew",
            "ktir_softmax_rows", "ktir_gather_rmw", "ktir_reduce", "ktir_matmul",
            "ktir_offsets", "ktir_indirect", "ktir_gemm_f16", "ktir_fmha_f16",
-           "ktir_wait_selftest"]
+           "ktir_wait_selftest", "ktir_host_threads", "ktir_host_upload", "ktir_host_download"]
 
 _LIB: Optional[C.CDLL] = None
 
@@ -154,6 +163,10 @@ def load_library(build_if_missing: bool = False) -> C.CDLL:
     lib.ktir_gemm_f16.argtypes = [C.POINTER(KtirGemmDesc), vp]
     lib.ktir_fmha_f16.argtypes = [C.POINTER(KtirFmhaDesc), vp]
     lib.ktir_wait_selftest.argtypes = [vp, C.c_uint32, vp]
+    lib.ktir_host_threads.argtypes = []
+    lib.ktir_host_upload.argtypes = [C.POINTER(KtirHostXfer), C.c_int, C.c_int, vp]
+    lib.ktir_host_download.argtypes = [C.POINTER(KtirHostXfer), C.c_int, C.POINTER(KtirHostCopy),
+                                       C.c_int, C.c_int, vp]
     for name in EXPORTS:
         getattr(lib, name).restype = C.c_int if name != "ktir_last_error" else C.c_char_p
     _LIB = lib

@@ -14,7 +14,7 @@ HEADER = os.path.join(ROOT, "include", "ktir_b200.h")
 
 STRUCTS = ["KtirBuffers", "KtirView", "KtirInstr", "KtirEwProgram", "KtirSoftmaxDesc",
            "KtirGatherRmwDesc", "KtirReduceDesc", "KtirMatmulDesc", "KtirOffsetsDesc",
-           "KtirIndirectDesc", "KtirGemmDesc", "KtirFmhaDesc"]
+           "KtirIndirectDesc", "KtirGemmDesc", "KtirFmhaDesc", "KtirHostXfer", "KtirHostCopy"]
 
 
 def declared_functions():
@@ -52,3 +52,24 @@ def test_struct_layouts_match_the_header(tmp_path):
     c_sizes = dict(zip(out[0::2], map(int, out[1::2])))
     for s in STRUCTS:
         assert C.sizeof(getattr(R, s)) == c_sizes[s], s
+
+
+def test_host_staging_pool_and_loud_failure_without_a_gpu():
+    """The staging worker pool starts without a GPU; a transfer then fails
+    with an error code and a message instead of touching memory."""
+    import numpy as np
+    from ktir_cpu_b200 import runtime as R
+    lib = R.load_library()
+    assert lib.ktir_host_threads() >= 1
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("checks the behaviour without a GPU")
+    except ImportError:
+        pass
+    a = np.arange(16, dtype=np.uint8)
+    x = R.KtirHostXfer()
+    x.host, x.pinned, x.device, x.bytes = a.ctypes.data, a.ctypes.data, a.ctypes.data, 16
+    assert lib.ktir_host_upload(C.byref(x), 1, 0, None) < 0
+    assert lib.ktir_last_error()
+    assert lib.ktir_host_upload(None, -1, 0, None) < 0
