@@ -10,16 +10,18 @@
 //   warp 10 (MMA)     S_t = Q_t K_j^T (M=128 N=128 K=128) into tile t's S
 //                     buffer; once the softmax warps of tile t hand over P_t
 //                     it issues O_t += P_t V_j (M=128 N=128 K=128) with P read
-//                     straight from TMEM, then S_t for block j+1 into the same
-//                     buffer (the tensor pipe runs a CTA's MMAs in issue
-//                     order, so that write follows the PV product's reads).
-//                     While tile 0's softmax works, the tensor cores run tile
-//                     1's products and the other way round
+//                     straight from TMEM, and S_t for block j+1 into the same
+//                     buffer once that PV product has completed (a later MMA
+//                     may write TMEM while an earlier one still reads it).
+//                     An event loop issues whichever tile's product is ready,
+//                     so while tile 0's softmax works the tensor cores run
+//                     tile 1's products and the other way round
 //   warps 0-3, 4-7    softmax of tile 0 / tile 1: thread r owns query row r
 //                     of its tile = TMEM lane r: tcgen05.ld of the 128 scores,
 //                     masked max of x = s * scale * log2(e), P = 2^(x - m)
-//                     evaluated in f16 pairs (P is f16 in the PV product
-//                     anyway), tcgen05.st of P over the first 64 columns of
+//                     (five pairs in eight by ex2.approx.f16x2 on MUFU, three
+//                     by a cubic on the FMA pipe: MUFU alone cannot keep up
+//                     with the tensor cores), tcgen05.st of P over the first 64 columns of
 //                     the S buffer, row sum l from f16 pair partials
 // TMEM (512 columns): S_0 / P_0 0..127, S_1 / P_1 128..255, O_0 256..383,
 // O_1 384..511.  The running max m only moves when a row's max exceeds it by
@@ -57,7 +59,7 @@ struct Bars {
   uint64_t q_full[2];
   uint64_t k_full[KST], k_empty[KST];
   uint64_t v_full[VST], v_empty[VST];
-  uint64_t s_full[2], p_full[2];
+  uint64_t s_full[2], p_full[2], pv_done[2];
   uint64_t o_full;
   uint32_t tmem_base;
   int abort_flag;
@@ -92,6 +94,26 @@ __device__ __forceinline__ uint32_t ex2_pair(float a, float b) {
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
   asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(h));
   return y;
+}
+
+// 2^x on the FMA and integer pipes, for the share of P the MUFU unit (16
+// exponentials per clock per SM) does not take: x = n + t with n = round(x)
+// by the 1.5 * 2^23 shift, 2^t on [-0.5, 0.5] by a cubic fitted to the
+// relative error (max 7.5e-5, below the f16 rounding P gets), and n added to
+// the exponent field.  x is clamped at -125 so the exponent cannot wrap;
+// 2^-125 rounds to 0 in f16 like any P below the f16 range.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.f);
+  const float r = x + 12582912.f;
+  const float t = x - (r - 12582912.f);
+  const float q = fmaf(fmaf(fmaf(0.0551716536f, t, 0.242611125f), t, 0.693260968f), t, 0.999928057f);
+  return __uint_as_float(__float_as_uint(q) + (__float_as_uint(r) << 23));
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+  return h;
 }
 
 // three-input max (NaN inputs ignored, like fmaxf)
@@ -139,6 +161,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(smem_u32(&B.q_full[t]), 1);
       mbar_init(smem_u32(&B.s_full[t]), 1);
       mbar_init(smem_u32(&B.p_full[t]), BQ);
+      mbar_init(smem_u32(&B.pv_done[t]), 1);
     }
     for (int s = 0; s < KST; ++s) {
       mbar_init(smem_u32(&B.k_full[s]), 1);
@@ -224,39 +247,71 @@ __global__ void __launch_bounds__(THREADS, 1)
                      idesc_pv, (acc || kk != 0) ? 1u : 0u);
         }
       };
-      bool ok = n_kv > 0 && mbar_wait(smem_u32(&B.k_full[0]), 0, abort);
-      for (int t = 0; ok && t < 2; ++t) {
-        if ((t ? n_1 : n_0) == 0) continue;
-        ok = mbar_wait(smem_u32(&B.q_full[t]), 0, abort);
-        if (ok) {
-          tc_fence_after();
-          issue_s(t, 0);
-        }
-      }
-      if (ok) mma_commit(smem_u32(&B.k_empty[0]));
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int vs = j % VST;
-        const int ks = (j + 1) % KST;
-        bool k_ready = false;
-        if (!mbar_wait(smem_u32(&B.v_full[vs]), (j / VST) & 1, abort)) break;
-        for (int t = 0; ok && t < 2; ++t) {
-          if (j >= (t ? n_1 : n_0)) continue;
-          // softmax of tile t has read S_t and written P_t
-          if (!mbar_wait(smem_u32(&B.p_full[t]), j & 1, abort)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(t, vs, j != 0);
-          if (j + 1 < (t ? n_1 : n_0)) {
-            if (!k_ready) {
-              if (!mbar_wait(smem_u32(&B.k_full[ks]), ((j + 1) / KST) & 1, abort)) { ok = false; break; }
-              tc_fence_after();
-              k_ready = true;
-            }
+      // Event loop over the two tiles: for tile t the next step is either
+      // PV(t, jp) (its softmax has handed over P, value block jp loaded) or
+      // S(t, js) (key block js loaded and PV(t, js - 1), which reads P where
+      // S lands, completed).  Whatever is ready is issued, so one tile's
+      // wait never holds back the other tile's products.
+      const int nt[2] = {n_0, n_1};
+      int jp[2] = {0, 0}, js[2] = {0, 0};
+      bool pv_pending[2] = {false, false};   // PV(t, jp - 1) issued, not yet seen complete
+      int kf = 0, vf = 0;                    // key / value blocks seen loaded
+      int k_users[KST], v_users[VST];
+      for (int i = 0; i < KST; ++i) k_users[i] = 0;
+      for (int i = 0; i < VST; ++i) v_users[i] = 0;
+      bool q_ok[2] = {n_0 == 0, n_1 == 0};
+      uint32_t idle = 0;
+      bool ok = n_kv > 0;
+      while (ok) {
+        bool progress = false;
+        while (kf < n_kv && mbar_test_wait(smem_u32(&B.k_full[kf % KST]), (kf / KST) & 1)) ++kf;
+        while (vf < n_kv && mbar_test_wait(smem_u32(&B.v_full[vf % VST]), (vf / VST) & 1)) ++vf;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (!q_ok[t] && mbar_test_wait(smem_u32(&B.q_full[t]), 0)) q_ok[t] = true;
+          if (pv_pending[t] && mbar_test_wait(smem_u32(&B.pv_done[t]), (jp[t] - 1) & 1))
+            pv_pending[t] = false;
+          // S(t, js): block js of the keys (every block a tile reads comes
+          // from both tiles' S products; the slot is released after the last)
+          if (js[t] < nt[t] && js[t] == jp[t] && !pv_pending[t] && kf > js[t] && q_ok[t]) {
+            tc_fence_after();
+            const int ks = js[t] % KST;
             issue_s(t, ks);
+            const int users = (js[t] < n_0) + (js[t] < n_1);
+            if (++k_users[ks] == users) {
+              mma_commit(smem_u32(&B.k_empty[ks]));
+              k_users[ks] = 0;
+            }
+            ++js[t];
+            progress = true;
+          }
+          // PV(t, jp): the softmax of tile t has read S and written P
+          if (jp[t] < js[t] && vf > jp[t] && mbar_test_wait(smem_u32(&B.p_full[t]), jp[t] & 1)) {
+            tc_fence_after();
+            const int vs = jp[t] % VST;
+            issue_pv(t, vs, jp[t] != 0);
+            mma_commit(smem_u32(&B.pv_done[t]));
+            const int users = (jp[t] < n_0) + (jp[t] < n_1);
+            if (++v_users[vs] == users) {
+              mma_commit(smem_u32(&B.v_empty[vs]));
+              v_users[vs] = 0;
+            }
+            ++jp[t];
+            pv_pending[t] = true;
+            progress = true;
           }
         }
-        if (!ok) break;
-        mma_commit(smem_u32(&B.v_empty[vs]));
-        if (k_ready) mma_commit(smem_u32(&B.k_empty[ks]));
+        if (jp[0] == n_0 && jp[1] == n_1) break;
+        if (progress) {
+          idle = 0;
+        } else {
+          if (*abort) ok = false;
+          if (++idle > kSpinLimit) {
+            *abort = 1;
+            ok = false;
+          }
+          if (idle > 4096) __nanosleep(32);
+        }
       }
       if (ok) mma_commit(smem_u32(&B.o_full));
     }
@@ -333,7 +388,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const int c = 32 * qtr + i;
-          ph[i / 2] = ex2_pair(fmaf(sv[c], p.scale_log2, -msub), fmaf(sv[c + 1], p.scale_log2, -msub));
+          const float xa = fmaf(sv[c], p.scale_log2, -msub);
+          const float xb = fmaf(sv[c + 1], p.scale_log2, -msub);
+          // three pairs in eight on the FMA pipe, the rest on MUFU
+          ph[i / 2] = ((i / 2) % 8 == 1 || (i / 2) % 8 == 4 || (i / 2) % 8 == 6)
+                          ? pack_f16x2(exp2_fma(xa), exp2_fma(xb))
+                          : ex2_pair(xa, xb);
           const __half2 v2 = *reinterpret_cast<const __half2*>(&ph[i / 2]);
           const int slot = (c / 2) & 15;
           h16[slot] = (c < 32) ? v2 : __hadd2(h16[slot], v2);
