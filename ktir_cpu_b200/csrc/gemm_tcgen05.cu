@@ -163,8 +163,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
-        tmem_ld32(acc + c, r);
-        tmem_ld_wait();
+        tmem_ld32_wait(acc + c, r);
         if (c + 32 == BN) {
           // every column of this accumulator is in registers: hand it back
           tc_fence_before();
