@@ -74,3 +74,24 @@ def test_fmha_running_max_moves(causal):
     ref = _reference(q, k, v, bh, seq, scale, causal)
     err = ((o.float() - ref).abs() / ref.abs().clamp_min(1.0)).max().item()
     assert err <= TOL, err
+
+
+def test_fmha_no_corrupted_rows_across_shapes_and_seeds():
+    """Repeated launches over several shapes and seeds: every output row is
+    finite and within tolerance (a TMEM hazard between the softmax warps and
+    the tensor pipe shows up as whole warps of NaN rows on some launches
+    only)."""
+    import torch
+    worst = 0.0
+    for seed in range(3):
+        for bh, seq, causal in [(3, 384, False), (1, 512, False), (2, 256, True), (2, 512, True),
+                                (4, 1024, True), (2, 1024, False)]:
+            g = torch.Generator(device="cpu").manual_seed(seed * 100 + bh * 10 + seq)
+            q, k, v = (torch.randn(bh * seq, 128, generator=g).half().cuda() for _ in range(3))
+            o = torch.full((bh * seq, 128), float("nan"), dtype=torch.float16, device="cuda")
+            scale = float(1.0 / math.sqrt(128))
+            _fmha(q, k, v, o, bh, seq, scale, causal)
+            assert not torch.isnan(o).any().item(), (seed, bh, seq, causal)
+            ref = _reference(q, k, v, bh, seq, scale, causal)
+            worst = max(worst, ((o.float() - ref).abs() / ref.abs().clamp_min(1.0)).max().item())
+    assert worst <= TOL, worst
