@@ -284,8 +284,9 @@ int ktir_host_upload(const KtirHostXfer* x, int n, int device, void* stream);
 
 /* Enqueues the device-to-pinned copies of `x` on `stream` (after whatever the
  * stream already holds), copies each chunk on to its host destination as soon
- * as it lands, runs the `extra` host-to-host copies meanwhile, and returns
- * after all of them and the stream have completed. */
+ * as it lands (no copy where `host` is the pinned buffer itself), runs the
+ * `extra` host-to-host copies meanwhile, and returns after all of them and
+ * the stream have completed. */
 int ktir_host_download(const KtirHostXfer* x, int n, const KtirHostCopy* extra, int m,
                        int device, void* stream);
 

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstdio>
 #include <cstdlib>
@@ -39,7 +40,11 @@ int n_workers() {
 }
 
 // Worker threads live for the whole process (the pool is never destroyed, so
-// no thread is joined or torn down while a static destructor runs).
+// no thread is joined or torn down while a static destructor runs).  An idle
+// worker polls the queue for a short while before it sleeps: calls come back
+// to back, and waking a sleeping thread costs tens of microseconds, which is
+// as long as copying a chunk.  The calling thread runs queued chunks itself
+// while it waits for one.
 class Pool {
  public:
   explicit Pool(int n) : n_(n) {
@@ -50,27 +55,55 @@ class Pool {
     {
       std::lock_guard<std::mutex> l(mu_);
       q_.push_back(std::move(f));
+      pending_.fetch_add(1, std::memory_order_release);
     }
     cv_.notify_one();
   }
+  // run one queued task on the calling thread; false if the queue is empty
+  bool try_run_one() {
+    std::function<void()> f;
+    if (!pop(f)) return false;
+    f();
+    return true;
+  }
 
  private:
+  bool pop(std::function<void()>& f) {
+    if (pending_.load(std::memory_order_acquire) == 0) return false;
+    std::lock_guard<std::mutex> l(mu_);
+    if (q_.empty()) return false;
+    f = std::move(q_.front());
+    q_.pop_front();
+    pending_.fetch_sub(1, std::memory_order_relaxed);
+    return true;
+  }
   void loop() {
     for (;;) {
       std::function<void()> f;
-      {
+      const auto t0 = std::chrono::steady_clock::now();
+      bool got = false;
+      for (int i = 0; !got; ++i) {
+        got = pop(f);
+        if (!got && (i & 63) == 63 &&
+            std::chrono::steady_clock::now() - t0 > std::chrono::microseconds(kSpinMicros))
+          break;
+      }
+      if (!got) {
         std::unique_lock<std::mutex> l(mu_);
         cv_.wait(l, [this] { return !q_.empty(); });
         f = std::move(q_.front());
         q_.pop_front();
+        pending_.fetch_sub(1, std::memory_order_relaxed);
       }
       f();
     }
   }
+  static constexpr int kSpinMicros = 300;
   int n_;
   std::mutex mu_;
   std::condition_variable cv_;
   std::deque<std::function<void()>> q_;
+  std::atomic<int> pending_{0};
 };
 
 Pool& pool() {
@@ -95,11 +128,24 @@ struct Batch {
     }
     cv.notify_all();
   }
-  void wait_one(size_t i) {
+  bool is_done(size_t i) {
+    std::lock_guard<std::mutex> l(mu);
+    return done[i] != 0;
+  }
+  bool all_done() {
+    std::lock_guard<std::mutex> l(mu);
+    return remaining == 0;
+  }
+  // wait for task i, running queued tasks on this thread meanwhile
+  void wait_one(size_t i, Pool& P) {
+    while (!is_done(i))
+      if (!P.try_run_one()) break;
     std::unique_lock<std::mutex> l(mu);
     cv.wait(l, [&] { return done[i] != 0; });
   }
-  void wait_all() {
+  void wait_all(Pool& P) {
+    while (!all_done())
+      if (!P.try_run_one()) break;
     std::unique_lock<std::mutex> l(mu);
     cv.wait(l, [&] { return remaining == 0; });
   }
@@ -190,7 +236,7 @@ extern "C" int ktir_host_upload(const KtirHostXfer* x, int n, int device, void* 
   }
   int ret = KTIR_OK;
   for (size_t i = 0; i < chunks.size(); ++i) {
-    batch->wait_one(i);
+    batch->wait_one(i, P);
     if (ret == KTIR_OK) {
       rc = dma(chunks[i]);
       if (rc != cudaSuccess) ret = cuda_err(rc, "ktir_host_upload: copy");
@@ -246,6 +292,11 @@ extern "C" int ktir_host_download(const KtirHostXfer* x, int n, const KtirHostCo
   }
   for (size_t i = 0; i < chunks.size(); ++i) {
     const Chunk c = chunks[i];
+    if (x[c.xfer].host == x[c.xfer].pinned) {
+      // the pinned buffer is the destination itself: nothing to copy on
+      batch->finish(k++, 0);
+      continue;
+    }
     void* dst = const_cast<char*>(static_cast<const char*>(x[c.xfer].host)) + c.off;
     const void* src = static_cast<const char*>(x[c.xfer].pinned) + c.off;
     const cudaEvent_t e = ev[i];
@@ -263,7 +314,7 @@ extern "C" int ktir_host_download(const KtirHostXfer* x, int n, const KtirHostCo
     });
     ++k;
   }
-  batch->wait_all();
+  batch->wait_all(P);
   // the call's kernels and copies have all completed once the stream has
   rc = cudaStreamSynchronize(st);
   if (ret == KTIR_OK && rc != cudaSuccess) ret = cuda_err(rc, "ktir_host_download: synchronize");

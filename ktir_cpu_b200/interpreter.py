@@ -18,6 +18,8 @@ schedule depends on tile data.
 from __future__ import annotations
 
 import ctypes as C
+import os
+import sys
 from typing import Any, Dict, List, Optional, Tuple
 
 import numpy as np
@@ -395,25 +397,24 @@ class KTIRInterpreter:
 
         Every allocation of the façade is replaced by a new array holding its
         contents after the call (the caller's input arrays are never written).
-        The host side runs in the library (ktir_host_upload / ktir_host_download):
-        page-aligned chunks are copied into the pinned staging buffers by its
-        worker threads, each chunk's DMA issued as soon as it is staged; after
-        the plan, each downloaded chunk is copied out as soon as it lands while
-        the copies of buffers the plan does not write run alongside.  Buffers
-        the plan overwrites entirely without reading are not uploaded.  Device
-        and pinned buffers belong to the Executable and are reused by every
-        call with the same signature.
+        Each allocation gets a page-locked buffer from a pool for the call: the
+        library copies the caller's array into it in chunks on its worker
+        threads, DMAs each chunk to the device as soon as it is staged, and
+        after the plan DMAs what the plan wrote back into the same buffer,
+        which is then the returned array (an allocation the plan does not
+        write comes back as its staged copy).  A buffer returns to the pool
+        once no array refers to it any more.  Buffers the plan overwrites
+        entirely without reading are not uploaded.  When the pool is at its
+        size limit, the call stages through the Executable's own pinned
+        buffers and copies the results into new arrays instead.
         """
         torch = exe.torch
         lib = exe.lib
         where = {a: (fac, k) for a, fac, k in self.memory.allocations()}
         arrays = [where[a][0].allocs[where[a][1]] for a in order]
         if exe.dev_tensors is None:
-            exe.dev_tensors, exe.pinned = [], []
-            for arr in arrays:
-                nb = arr.nbytes
-                exe.dev_tensors.append(torch.empty(nb + 16, dtype=torch.uint8, device=exe.device))
-                exe.pinned.append(torch.empty(max(nb, 1), dtype=torch.uint8, pin_memory=True))
+            exe.dev_tensors = [torch.empty(arr.nbytes + 16, dtype=torch.uint8, device=exe.device)
+                               for arr in arrays]
             exe.bufs = exe.buffers(exe.dev_tensors)
             exe.status_pinned = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         stream = torch.cuda.current_stream(exe.device)
@@ -422,28 +423,40 @@ class KTIRInterpreter:
         written = exe.plan.info.get("written")
         skip = exe.plan.info.get("overwritten", set())
         src = [np.ascontiguousarray(arr).view(np.uint8).reshape(-1) for arr in arrays]
-        up = [i for i in range(len(order)) if i not in skip and src[i].size]
+        n = len(order)
+        staged = _PINNED.take([s_.size for s_ in src], torch)
+        if staged is None:
+            if exe.pinned is None:
+                exe.pinned = [torch.empty(max(s_.size, 1), dtype=torch.uint8, pin_memory=True)
+                              for s_ in src]
+            pinned = [t.data_ptr() for t in exe.pinned]
+            results = [np.empty(s_.size, np.uint8) for s_ in src]
+        else:
+            pinned = [a.ctypes.data for _, a in staged]
+            results = [a[:s_.size] for (_, a), s_ in zip(staged, src)]
+        up = [i for i in range(n) if i not in skip and src[i].size]
         xs = (R.KtirHostXfer * max(1, len(up)))()
         for k, i in enumerate(up):
-            xs[k].host, xs[k].pinned = src[i].ctypes.data, exe.pinned[i].data_ptr()
+            xs[k].host, xs[k].pinned = src[i].ctypes.data, pinned[i]
             xs[k].device, xs[k].bytes = exe.dev_tensors[i].data_ptr(), src[i].size
         R.check(lib.ktir_host_upload(xs, len(up), dev, sp), "ktir_host_upload")
         if exe.plan.status_check:
             exe.status.zero_()
         exe.launch(exe.dev_tensors, stream, exe.bufs)
-        back = [i for i in range(len(order)) if (written is None or i in written) and src[i].size]
-        results = [np.empty(s_.size, np.uint8) for s_ in src]
+        back = [i for i in range(n) if (written is None or i in written) and src[i].size]
         status = np.zeros(1, np.int32)
         ys = (R.KtirHostXfer * (len(back) + 1))()
         for k, i in enumerate(back):
-            ys[k].host, ys[k].pinned = results[i].ctypes.data, exe.pinned[i].data_ptr()
+            ys[k].host, ys[k].pinned = results[i].ctypes.data, pinned[i]
             ys[k].device, ys[k].bytes = exe.dev_tensors[i].data_ptr(), src[i].size
         n_y = len(back)
         if exe.plan.status_check:
             ys[n_y].host, ys[n_y].pinned = status.ctypes.data, exe.status_pinned.data_ptr()
             ys[n_y].device, ys[n_y].bytes = exe.status.data_ptr(), 4
             n_y += 1
-        rest = [i for i in range(len(order)) if i not in back and src[i].size]
+        # allocations neither written back nor already staged into their result
+        rest = [i for i in range(n) if i not in back and src[i].size
+                and (staged is None or i not in up)]
         cs = (R.KtirHostCopy * max(1, len(rest)))()
         for k, i in enumerate(rest):
             cs[k].dst, cs[k].src, cs[k].bytes = results[i].ctypes.data, src[i].ctypes.data, src[i].size
@@ -455,4 +468,52 @@ class KTIRInterpreter:
             fac.borrowed.add(k)
         exe.last_h2d_bytes = sum(src[i].size for i in up)
         exe.last_d2h_bytes = sum(src[i].size for i in back)
+
+
+class _PinnedPool:
+    """Page-locked host buffers handed out as call results and reused once
+    nothing refers to them (every view of a buffer holds a reference to it,
+    so an idle buffer is one only the pool holds).  Buffers are kept per
+    size; the pool stops growing at KTIR_PINNED_POOL_BYTES (default 8 GiB)."""
+
+    def __init__(self) -> None:
+        self.free: Dict[int, List[List[Any]]] = {}
+        self.bytes = 0
+        self.limit = int(os.environ.get("KTIR_PINNED_POOL_BYTES", str(8 << 30)))
+
+    def take(self, sizes: List[int], torch) -> Optional[List[Tuple[Any, np.ndarray]]]:
+        """One idle buffer per size (all or none)."""
+        picked: List[List[Any]] = []
+        new_bytes = 0
+        for nb in sizes:
+            nb = max(int(nb), 1)
+            entry = None
+            for e in self.free.get(nb, []):
+                # held by the pool's list and by getrefcount's argument only
+                if not e[2] and sys.getrefcount(e[1]) == 2:
+                    entry = e
+                    break
+            if entry is None:
+                new_bytes += nb
+                entry = [None, None, False, nb]
+            entry[2] = True
+            picked.append(entry)
+        if self.bytes + new_bytes > self.limit:
+            for e in picked:
+                e[2] = False
+            return None
+        out = []
+        for e in picked:
+            if e[0] is None:
+                t = torch.empty(e[3], dtype=torch.uint8, pin_memory=True)
+                e[0], e[1] = t, t.numpy()
+                self.free.setdefault(e[3], []).append(e)
+                self.bytes += e[3]
+            e[2] = False
+            out.append((e[0], e[1]))
+        return out
+
+
+_PINNED = _PinnedPool()
+
 

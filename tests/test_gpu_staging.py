@@ -63,3 +63,34 @@ def test_execute_function_returns_fresh_arrays():
         assert a[k] is not kw[k] and b[k] is not a[k]
         assert np.array_equal(a[k], b[k])
     assert np.array_equal(a["in_ptr"].view(np.uint16), kw["in_ptr"].view(np.uint16))
+
+
+def test_results_held_or_viewed_are_never_reused():
+    """Results come back in pooled page-locked buffers: a buffer is reused only
+    once nothing refers to it, so a kept result, or a view that outlives its
+    result, keeps its contents across later calls."""
+    import gc
+    from ktir_cpu_b200 import KTIRInterpreter
+    import ktir_cpu_b200.workloads as W
+    src = W.source("vector_add")
+    interp = KTIRInterpreter()
+    interp.load(src)
+    fn = W.FUNC["vector_add"]
+    kws = [W.inputs("vector_add", seed=s) for s in range(4)]
+    first = interp.execute_function(fn, **kws[0])
+    keep = {k: v.copy() for k, v in first.items()}
+    name = [k for k in first if not np.array_equal(first[k], kws[0][k])][0]   # the output
+    view = first[name][3:]
+    view_copy = view.copy()
+    other = interp.execute_function(fn, **kws[1])
+    del other
+    gc.collect()
+    for s in range(2, 4):
+        interp.execute_function(fn, **kws[s])
+    for k in first:
+        assert np.array_equal(first[k].view(np.uint16), keep[k].view(np.uint16))
+    del first
+    gc.collect()
+    for s in range(4):
+        interp.execute_function(fn, **kws[s])
+    assert np.array_equal(view.view(np.uint16), view_copy.view(np.uint16))
