@@ -71,13 +71,20 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait: returns false (and raises *abort) when the limit runs out or
-// another role already aborted.
+// another role already aborted.  It polls with the non-blocking test first:
+// mbarrier.try_wait may suspend the thread for a fixed window and then
+// reacts hundreds of cycles after the phase completed, which on a pipeline's
+// critical path (the MMA thread waiting for P, the softmax waiting for S)
+// costs more than the polling does.  After a long wait it falls back to
+// try_wait with a back-off.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  for (uint32_t i = 0; i < 8192; ++i) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((i & 255) == 255 && *abort) return false;
+  }
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    // mbarrier.try_wait already suspends the thread for a while; back off
-    // further only after a long wait, so a wake-up is not delayed by a sleep
     if (i > 4096) __nanosleep(32);
   }
   *abort = 1;
@@ -285,6 +292,30 @@ __device__ __forceinline__ void tmem_st64_wait(uint32_t taddr, const uint32_t (&
         "r"(r[50]), "r"(r[51]), "r"(r[52]), "r"(r[53]), "r"(r[54]), "r"(r[55]), "r"(r[56]),
         "r"(r[57]), "r"(r[58]), "r"(r[59]), "r"(r[60]), "r"(r[61]), "r"(r[62]), "r"(r[63])
       : "memory");
+}
+
+// one 32-bit column of this thread's TMEM lane, stored / loaded and waited for
+__device__ __forceinline__ void tmem_st1_wait(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};\n"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr), "r"(v)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t tmem_ld1_wait(uint32_t taddr) {
+  uint32_t v;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(v)
+      : "r"(taddr)
+      : "memory");
+  return v;
+}
+
+// named barrier over `count` threads (whole warps)
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // shared-memory descriptor, 128-byte swizzle
