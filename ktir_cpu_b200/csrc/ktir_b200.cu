@@ -315,6 +315,147 @@ __global__ void __launch_bounds__(128) k_softmax_rows(const __grid_constant__ Kt
   }
 }
 
+// The same row softmax for rows of 256 or more elements with 16-byte moves:
+// lane l owns elements 256m + 8l + k (k < 8) of the row, so a warp load or
+// store covers 512 contiguous bytes.  The sum is still the reference's
+// pairwise-halving fold pair for pair: in-lane rounds over m (distances
+// n/2 .. 256), five shuffle rounds (128 .. 8), then in-lane rounds over k
+// (4, 2, 1).
+template <int M, bool F16>
+__device__ __forceinline__ float sum_fold8(float (&v)[M][8]) {
+  const unsigned full = 0xffffffffu;
+#pragma unroll
+  for (int hm = M / 2; hm >= 1; hm >>= 1)
+#pragma unroll
+    for (int m = 0; m < hm; ++m)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float r = v[m][k] + v[m + hm][k];
+        v[m][k] = F16 ? __half2float(__float2half_rn(r)) : r;
+      }
+#pragma unroll
+  for (int dl = 16; dl >= 1; dl >>= 1)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float c = __shfl_down_sync(full, v[0][k], dl);
+      const float r = v[0][k] + c;
+      v[0][k] = F16 ? __half2float(__float2half_rn(r)) : r;
+    }
+#pragma unroll
+  for (int hk = 4; hk >= 1; hk >>= 1)
+#pragma unroll
+    for (int k = 0; k < hk; ++k) {
+      const float r = v[0][k] + v[0][k + hk];
+      v[0][k] = F16 ? __half2float(__float2half_rn(r)) : r;
+    }
+  return __shfl_sync(full, v[0][0], 0);
+}
+
+template <int M>
+__device__ __forceinline__ void load_row8(const __half* in, int64_t numel, int64_t ib, int lane,
+                                          uint4 (&raw)[M]) {
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const int64_t e = ib + 256 * m + 8 * lane;
+    if (e >= 0 && e + 8 <= numel) {
+      raw[m] = __ldg(reinterpret_cast<const uint4*>(in + e));
+    } else {
+      __align__(16) __half h[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        h[k] = (e + k >= 0 && e + k < numel) ? in[e + k] : __float2half(0.f);
+      raw[m] = *reinterpret_cast<const uint4*>(h);
+    }
+  }
+}
+
+template <int M, bool F16>
+__global__ void __launch_bounds__(128) k_softmax_rows8(const __grid_constant__ KtirSoftmaxDesc d,
+                                                       const __grid_constant__ KtirBuffers b,
+                                                       const int64_t* __restrict__ ut) {
+  pdl_prologue();
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t total_rows = (int64_t)d.n_units * d.rows;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const __half* in = (const __half*)b.base[d.in.slot];
+  __half* out = (__half*)b.base[d.out.slot];
+  const int64_t in_numel = b.numel[d.in.slot];
+  const int64_t out_numel = b.numel[d.out.slot];
+  auto base_of = [&](const KtirView& vw, int64_t row) -> int64_t {
+    if (vw.unit_col < 0) return vw.off + row * vw.stride[0];
+    const int unit = (int)row / d.rows;
+    const int r = (int)row - unit * d.rows;
+    return vw.off + ut[(int64_t)unit * d.unit_cols + vw.unit_col] + (int64_t)r * vw.stride[0];
+  };
+  uint4 cur[M];
+  if (warp < total_rows) load_row8<M>(in, in_numel, base_of(d.in, warp), lane, cur);
+  for (int64_t row = warp; row < total_rows; row += nwarps) {
+    uint4 nxt[M];
+    const int64_t nrow = row + nwarps;
+    if (nrow < total_rows) load_row8<M>(in, in_numel, base_of(d.in, nrow), lane, nxt);
+    const int64_t ob = base_of(d.out, row);
+    float v[M][8];
+    float pm[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const __half2* h2 = reinterpret_cast<const __half2*>(&cur[m]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __half22float2(h2[q]);
+        v[m][2 * q] = f.x;
+        v[m][2 * q + 1] = f.y;
+      }
+      pm[m] = fmaxf(fmaxf(fmaxf(v[m][0], v[m][1]), fmaxf(v[m][2], v[m][3])),
+                    fmaxf(fmaxf(v[m][4], v[m][5]), fmaxf(v[m][6], v[m][7])));
+    }
+#pragma unroll
+    for (int h = M / 2; h >= 1; h >>= 1)
+#pragma unroll
+      for (int m = 0; m < h; ++m) pm[m] = fmaxf(pm[m], pm[m + h]);
+    const float mx = warp_max(pm[0]);
+    // exp(x - max) as in k_softmax_rows
+    const float l2e = 1.4426950408889634f;
+    const float mx2 = mx * l2e;
+    float t[M][8];
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float x;
+        if (F16) {
+          x = __half2float(__float2half_rn(v[m][k] - mx));
+          x = __half2float(__float2half_rn(expf(x)));
+        } else {
+          x = fast_exp2(fmaf(v[m][k], l2e, -mx2));
+        }
+        v[m][k] = x;
+        t[m][k] = x;
+      }
+    const float sum = sum_fold8<M, F16>(t);
+    const float rs = 1.0f / sum;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int64_t e = ob + 256 * m + 8 * lane;
+      __align__(16) __half2 o2[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        o2[q] = F16 ? __floats2half2_rn(v[m][2 * q] / sum, v[m][2 * q + 1] / sum)
+                    : __floats2half2_rn(v[m][2 * q] * rs, v[m][2 * q + 1] * rs);
+      if (e >= 0 && e + 8 <= out_numel) {
+        *reinterpret_cast<uint4*>(out + e) = *reinterpret_cast<const uint4*>(o2);
+      } else {
+        const __half* oh = reinterpret_cast<const __half*>(o2);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (e + k >= 0 && e + k < out_numel) out[e + k] = oh[k];
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) cur[m] = nxt[m];
+  }
+}
+
 extern "C" int ktir_softmax_rows(const KtirSoftmaxDesc* d, const KtirBuffers* bufs,
                                  const int64_t* unit_table, void* stream) {
   if (!d || !bufs) return set_err(KTIR_ERR_ARG, "ktir_softmax_rows: null descriptor");
@@ -341,16 +482,33 @@ extern "C" int ktir_softmax_rows(const KtirSoftmaxDesc* d, const KtirBuffers* bu
       launch_pdl(k_softmax_rows<V, false>, dim3(blocks), dim3(threads), 0, s, *d, *bufs, \
                  unit_table);                                                        \
     break;
-  switch (n / 64) {
-    KTIR_SOFTMAX_CASE(1)
-    KTIR_SOFTMAX_CASE(2)
-    KTIR_SOFTMAX_CASE(4)
-    KTIR_SOFTMAX_CASE(8)
-    KTIR_SOFTMAX_CASE(16)
-    KTIR_SOFTMAX_CASE(32)
-    KTIR_SOFTMAX_CASE(64)
-    default: return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: row length");
+#define KTIR_SOFTMAX8_CASE(V)                                                         \
+  case V:                                                                             \
+    if (d->compute_f16)                                                               \
+      launch_pdl(k_softmax_rows8<V, true>, dim3(blocks), dim3(threads), 0, s, *d, *bufs, \
+                 unit_table);                                                         \
+    else                                                                              \
+      launch_pdl(k_softmax_rows8<V, false>, dim3(blocks), dim3(threads), 0, s, *d, *bufs, \
+                 unit_table);                                                         \
+    break;
+  if (n >= 256) {
+    // 16-byte moves (rows are 16-byte aligned, checked above)
+    switch (n / 256) {
+      KTIR_SOFTMAX8_CASE(1)
+      KTIR_SOFTMAX8_CASE(2)
+      KTIR_SOFTMAX8_CASE(4)
+      KTIR_SOFTMAX8_CASE(8)
+      KTIR_SOFTMAX8_CASE(16)
+      default: return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: row length");
+    }
+  } else {
+    switch (n / 64) {
+      KTIR_SOFTMAX_CASE(1)
+      KTIR_SOFTMAX_CASE(2)
+      default: return set_err(KTIR_ERR_UNSUPPORTED, "ktir_softmax_rows: row length");
+    }
   }
+#undef KTIR_SOFTMAX8_CASE
 #undef KTIR_SOFTMAX_CASE
   return check_launch("ktir_softmax_rows");
 }
