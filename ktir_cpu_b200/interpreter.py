@@ -477,12 +477,18 @@ class _PinnedPool:
     size; the pool stops growing at KTIR_PINNED_POOL_BYTES (default 8 GiB)."""
 
     def __init__(self) -> None:
+        import threading
         self.free: Dict[int, List[List[Any]]] = {}
         self.bytes = 0
         self.limit = int(os.environ.get("KTIR_PINNED_POOL_BYTES", str(8 << 30)))
+        self.lock = threading.Lock()
 
     def take(self, sizes: List[int], torch) -> Optional[List[Tuple[Any, np.ndarray]]]:
-        """One idle buffer per size (all or none)."""
+        """One idle buffer per size (all or none); safe to call from several threads."""
+        with self.lock:
+            return self._take(sizes, torch)
+
+    def _take(self, sizes: List[int], torch) -> Optional[List[Tuple[Any, np.ndarray]]]:
         picked: List[List[Any]] = []
         new_bytes = 0
         for nb in sizes:
