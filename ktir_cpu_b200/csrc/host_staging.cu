@@ -171,6 +171,24 @@ std::vector<Chunk> split(const int64_t* sizes, int n, int workers) {
   return out;
 }
 
+// Chunks for an upload: many more than there are workers, so that the DMA of
+// the first chunks runs while the workers still copy the later ones (with one
+// chunk per worker every chunk is staged at about the same time and the DMA
+// only starts after the whole copy).
+std::vector<Chunk> split_pipelined(const int64_t* sizes, int n) {
+  int64_t total = 0;
+  for (int i = 0; i < n; ++i) total += sizes[i] > 0 ? sizes[i] : 0;
+  int64_t step = total / 64;
+  if (step < kMinChunk) step = kMinChunk;
+  if (step > (4 << 20)) step = 4 << 20;
+  step = (step + kChunkAlign - 1) / kChunkAlign * kChunkAlign;
+  std::vector<Chunk> out;
+  for (int i = 0; i < n; ++i)
+    for (int64_t off = 0; off < sizes[i]; off += step)
+      out.push_back({i, off, sizes[i] - off < step ? sizes[i] - off : step});
+  return out;
+}
+
 int cuda_err(cudaError_t e, const char* what) {
   char buf[256];
   snprintf(buf, sizeof(buf), "%s: %s", what, cudaGetErrorString(e));
@@ -210,7 +228,7 @@ extern "C" int ktir_host_upload(const KtirHostXfer* x, int n, int device, void* 
     sizes[i] = x[i].bytes;
   }
   Pool& P = pool();
-  const std::vector<Chunk> chunks = split(sizes.data(), n, P.size());
+  const std::vector<Chunk> chunks = split_pipelined(sizes.data(), n);
   auto st = static_cast<cudaStream_t>(stream);
   auto dma = [&](const Chunk& c) {
     return cudaMemcpyAsync(static_cast<char*>(x[c.xfer].device) + c.off,
