@@ -273,7 +273,7 @@ typedef struct {
 } KtirHostCopy;
 
 /* Number of host worker threads the staging copies run on
- * (KTIR_HOST_THREADS, default min(16, hardware threads)). */
+ * (KTIR_HOST_THREADS, default min(16, hardware threads / LOCAL_WORLD_SIZE)). */
 int ktir_host_threads(void);
 
 /* host -> pinned copies in chunks on the worker threads; each chunk's

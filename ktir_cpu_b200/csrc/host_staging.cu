@@ -29,11 +29,16 @@ namespace {
 constexpr int64_t kMinChunk = 1 << 20;      // below this a copy stays on the calling thread
 constexpr int64_t kChunkAlign = 1 << 16;
 
+// KTIR_HOST_THREADS, else the host's hardware threads shared among the
+// processes of this node (LOCAL_WORLD_SIZE, set by torchrun), at most 16
 int n_workers() {
   const char* env = getenv("KTIR_HOST_THREADS");
   int n = env ? atoi(env) : 0;
   if (n <= 0) {
     n = (int)std::thread::hardware_concurrency();
+    const char* lws = getenv("LOCAL_WORLD_SIZE");
+    const int procs = lws ? atoi(lws) : 1;
+    if (procs > 1) n /= procs;
     if (n > 16) n = 16;
   }
   return n < 1 ? 1 : n;
