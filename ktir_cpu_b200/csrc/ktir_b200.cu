@@ -618,6 +618,22 @@ __global__ void __launch_bounds__(256) k_rmw_apply(const __grid_constant__ KtirG
     for (int c = sub * 8; c < d.row_len; c += 128) {
       const int64_t e = rb + c;
       const bool vec = (c + 8 <= d.row_len) && ((e & 7) == 0) && (e + 8 <= tnumel) && e >= 0;
+      if (SOP != 0 && vec) {
+        // y = x op imm on f16 pairs: one f16 rounding of the exact result is
+        // what the f32 operation rounded to f16 gives (f32 carries more than
+        // 2 x 11 + 2 bits, so the double rounding cannot differ)
+        uint4 raw = *reinterpret_cast<const uint4*>(table + e);
+        __half2* h2 = reinterpret_cast<__half2*>(&raw);
+        const __half2 imm2 = __float2half2_rn(simple_imm);
+        for (int rep = 0; rep < m; ++rep) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            h2[q] = SOP == OP_FADD ? __hadd2(h2[q], imm2)
+                                   : (SOP == OP_FSUB ? __hsub2(h2[q], imm2) : __hmul2(h2[q], imm2));
+        }
+        *reinterpret_cast<uint4*>(table + e) = raw;
+        continue;
+      }
       float x[8];
       if (vec) {
         uint4 raw = *reinterpret_cast<const uint4*>(table + e);
