@@ -10,7 +10,7 @@ list, parsed attributes and nested regions with their block arguments.
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import Any, Dict, Iterator, List, Optional, Tuple
+from typing import Any, Dict, Iterator, List, Tuple
 
 
 @dataclass

@@ -27,7 +27,6 @@ elementwise bytecode, tree reductions, CUDA-core matmuls and stores.
 from __future__ import annotations
 
 import ctypes as C
-import operator
 import os
 from dataclasses import dataclass, field
 from typing import Any, Callable, Dict, List, Optional, Sequence, Tuple
@@ -36,8 +35,7 @@ import numpy as np
 
 from . import runtime as R
 from .affine import BoxSet, linearize
-from .trace import (Const, CoordTarget, IATV, IndirectTarget, Node, RectTarget, Store, Trace,
-                    np_dtype)
+from .trace import Const, CoordTarget, IATV, IndirectTarget, Node, RectTarget, Store, Trace
 
 # ---------------------------------------------------------------------------
 # elementwise bytecode compiler

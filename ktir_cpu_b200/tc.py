@@ -16,7 +16,7 @@ Attention: see :mod:`ktir_cpu_b200.rewrite`.
 from __future__ import annotations
 
 import ctypes as C
-from typing import List, Optional, Tuple
+from typing import List
 
 import numpy as np
 

@@ -33,13 +33,13 @@ from __future__ import annotations
 
 import bisect
 import operator
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import Any, Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
 
-from .affine import AffineMap, AffineSet, BoxSet
-from .ir import IRFunction, Operation, Region, iter_ops
+from .affine import AffineMap, BoxSet
+from .ir import IRFunction, Operation, iter_ops
 
 STICK = 128
 LX_CAPACITY = 2 * 1024 * 1024

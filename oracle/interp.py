@@ -44,12 +44,12 @@ import bisect
 import math
 import operator
 from dataclasses import dataclass
-from typing import Any, Dict, List, Optional, Sequence, Tuple
+from typing import Any, Dict, List, Optional, Tuple
 
 import numpy as np
 
-from ktir_cpu_b200.affine import AffineSet, BoxSet, eval_expr
-from ktir_cpu_b200.ir import IRFunction, IRModule, Operation, Region
+from ktir_cpu_b200.affine import BoxSet, eval_expr
+from ktir_cpu_b200.ir import IRModule, Operation, Region
 from ktir_cpu_b200.parser import KTIRParser
 
 STICK = 128

@@ -2,7 +2,6 @@
 
 import ctypes as C
 
-import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu

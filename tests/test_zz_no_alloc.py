@@ -19,7 +19,7 @@ pytestmark = pytest.mark.gpu
 
 def _descriptor(n_units, unit_len, row_len, n_rows):
     from ktir_cpu_b200 import runtime as R
-    from ktir_cpu_b200.lower import EwBuilder, mkview, program, OP
+    from ktir_cpu_b200.lower import EwBuilder, mkview, program
     b = EwBuilder()
     b.view("g")
     b.view("s")
