@@ -181,7 +181,7 @@ def config_dict(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="softmax", choices=sorted(W.FULL))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -274,6 +274,10 @@ def main():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
+        # a short device-side wait ahead of the start event, so the host has
+        # queued the K steps before the clock starts (the host's launch
+        # latency is not device time)
+        torch.cuda._sleep(200000)
         ev0.record(stream)
         if graph is not None:
             graph.replay()
