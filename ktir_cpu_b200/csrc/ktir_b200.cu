@@ -354,6 +354,13 @@ __device__ __forceinline__ float sum_fold8(float (&v)[M][8]) {
 template <int M>
 __device__ __forceinline__ void load_row8(const __half* in, int64_t numel, int64_t ib, int lane,
                                           uint4 (&raw)[M]) {
+  if (ib >= 0 && ib + 256 * M <= numel) {
+    // the whole row lies inside the buffer: no per-chunk bounds
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+      raw[m] = __ldg(reinterpret_cast<const uint4*>(in + ib + 256 * m + 8 * lane));
+    return;
+  }
 #pragma unroll
   for (int m = 0; m < M; ++m) {
     const int64_t e = ib + 256 * m + 8 * lane;
@@ -434,6 +441,7 @@ __global__ void __launch_bounds__(128) k_softmax_rows8(const __grid_constant__ K
       }
     const float sum = sum_fold8<M, F16>(t);
     const float rs = 1.0f / sum;
+    const bool whole = ob >= 0 && ob + 256 * M <= out_numel;
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       const int64_t e = ob + 256 * m + 8 * lane;
@@ -442,7 +450,7 @@ __global__ void __launch_bounds__(128) k_softmax_rows8(const __grid_constant__ K
       for (int q = 0; q < 4; ++q)
         o2[q] = F16 ? __floats2half2_rn(v[m][2 * q] / sum, v[m][2 * q + 1] / sum)
                     : __floats2half2_rn(v[m][2 * q] * rs, v[m][2 * q + 1] * rs);
-      if (e >= 0 && e + 8 <= out_numel) {
+      if (whole || (e >= 0 && e + 8 <= out_numel)) {
         *reinterpret_cast<uint4*>(out + e) = *reinterpret_cast<const uint4*>(o2);
       } else {
         const __half* oh = reinterpret_cast<const __half*>(o2);
