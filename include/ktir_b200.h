@@ -276,7 +276,8 @@ typedef struct {
  * (KTIR_HOST_THREADS, default min(16, hardware threads / LOCAL_WORLD_SIZE)). */
 int ktir_host_threads(void);
 
-/* host -> pinned copies in chunks on the worker threads; each chunk's
+/* host -> pinned copies in chunks on the worker threads, at most
+ * KTIR_UPLOAD_INFLIGHT (default 8, 0 = all) queued at a time; each chunk's
  * host-to-device copy is enqueued on `stream` as soon as it is staged.
  * Returns once every copy is enqueued (the pinned buffers must then stay
  * untouched until the stream has passed them). */

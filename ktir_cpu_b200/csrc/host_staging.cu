@@ -194,6 +194,15 @@ std::vector<Chunk> split_pipelined(const int64_t* sizes, int n) {
   return out;
 }
 
+// Upload chunk copies queued at once: KTIR_UPLOAD_INFLIGHT, default 8 (0 = all).
+size_t upload_inflight(size_t n_chunks) {
+  static const long v = [] {
+    const char* env = getenv("KTIR_UPLOAD_INFLIGHT");
+    return env ? atol(env) : 8L;
+  }();
+  return v > 0 && (size_t)v < n_chunks ? (size_t)v : n_chunks;
+}
+
 int cuda_err(cudaError_t e, const char* what) {
   char buf[256];
   snprintf(buf, sizeof(buf), "%s: %s", what, cudaGetErrorString(e));
@@ -248,7 +257,7 @@ extern "C" int ktir_host_upload(const KtirHostXfer* x, int n, int device, void* 
     return rc == cudaSuccess ? KTIR_OK : cuda_err(rc, "ktir_host_upload: copy");
   }
   auto batch = std::make_shared<Batch>(chunks.size());
-  for (size_t i = 0; i < chunks.size(); ++i) {
+  auto submit = [&](size_t i) {
     const Chunk c = chunks[i];
     void* dst = static_cast<char*>(x[c.xfer].pinned) + c.off;
     const void* src = static_cast<const char*>(x[c.xfer].host) + c.off;
@@ -256,10 +265,16 @@ extern "C" int ktir_host_upload(const KtirHostXfer* x, int n, int device, void* 
       memcpy(dst, src, (size_t)c.len);
       batch->finish(i, 0);
     });
-  }
+  };
+  // Only a few chunks are queued at a time: they finish nearly in order, and
+  // the caller, which helps with queued copies while it waits, does not pick
+  // up a late chunk before it has issued the DMA of an early one.
+  const size_t inflight = upload_inflight(chunks.size());
+  for (size_t i = 0; i < inflight; ++i) submit(i);
   int ret = KTIR_OK;
   for (size_t i = 0; i < chunks.size(); ++i) {
     batch->wait_one(i, P);
+    if (i + inflight < chunks.size()) submit(i + inflight);
     if (ret == KTIR_OK) {
       rc = dma(chunks[i]);
       if (rc != cudaSuccess) ret = cuda_err(rc, "ktir_host_upload: copy");
