@@ -380,10 +380,23 @@ template <int M, bool F16>
 __global__ void __launch_bounds__(128) k_softmax_rows8(const __grid_constant__ KtirSoftmaxDesc d,
                                                        const __grid_constant__ KtirBuffers b,
                                                        const int64_t* __restrict__ ut) {
-  pdl_prologue();
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t total_rows = (int64_t)d.n_units * d.rows;
+  // Before waiting for the previous kernel on the stream, ask L2 for this
+  // warp's first input row (from the parameters alone, so only for affine
+  // rows).  A prefetch changes no value that a later load returns, even if
+  // the previous kernel writes that row, and it lets this kernel's HBM reads
+  // overlap the previous kernel's last CTAs.
+  if (d.in.unit_col < 0 && lane == 0 && warp < total_rows) {
+    const int64_t ib = d.in.off + warp * d.in.stride[0];
+    if (ib >= 0 && ib + 256 * M <= b.numel[d.in.slot])
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                       (const __half*)b.base[d.in.slot] + ib),
+                   "r"(512 * M)
+                   : "memory");
+  }
+  pdl_prologue();
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const __half* in = (const __half*)b.base[d.in.slot];
   __half* out = (__half*)b.base[d.out.slot];
