@@ -46,6 +46,7 @@ constexpr int BKV = 64;         // key rows per block
 constexpr int KST = 2;          // K ring stages
 constexpr int VST = 2;          // V ring stages
 constexpr int THREADS = 224;
+constexpr int HEAD_GROUP = 16;   // heads per group of the CTA order (16 MiB of K/V at S=2048)
 constexpr int Q_HALF = BQ * 64 * 2;             // 16 KiB: 128 rows x 64 columns
 constexpr int Q_BYTES = 2 * Q_HALF;             // 32 KiB
 constexpr int KV_HALF = BKV * 64 * 2;           // 8 KiB: 64 rows x 64 columns
@@ -77,6 +78,7 @@ struct FmhaParams {
   float scale_log2;   // scale * log2(e)
   int causal;
   int n_qtiles;
+  long long bh;
   int* status;
 };
 
@@ -126,8 +128,17 @@ __global__ void __launch_bounds__(THREADS, 2)
   Bars& B = *reinterpret_cast<Bars*>(smem_raw + (base - raw) + TILE_BYTES);
   volatile int* abort = &B.abort_flag;
 
-  const int qt = p.n_qtiles - 1 - (int)blockIdx.x;   // heaviest query tiles first
-  const long long head = blockIdx.y;
+  // CTA order (blocks are dispatched in index order): groups of HEAD_GROUP
+  // heads, and within a group every head's heaviest query tile, then every
+  // head's next one, ... so the grid ends on the lightest tiles while the
+  // CTAs in flight share the K/V of a few heads in L2
+  const long long lin = blockIdx.x;
+  const long long gsize = (long long)HEAD_GROUP * p.n_qtiles;
+  const long long grp = lin / gsize;
+  const long long heads = p.bh - grp * HEAD_GROUP < HEAD_GROUP ? p.bh - grp * HEAD_GROUP : HEAD_GROUP;
+  const long long w = lin - grp * gsize;
+  const int qt = p.n_qtiles - 1 - (int)(w / heads);
+  const long long head = grp * HEAD_GROUP + w % heads;
   const long long row0 = head * p.seq + (long long)qt * BQ;
   const int q0 = qt * BQ;
   const int n_kv = p.causal ? (q0 + BQ) / BKV : (int)(p.seq / BKV);
@@ -427,8 +438,9 @@ extern "C" int ktir_fmha_f16(const KtirFmhaDesc* d, void* stream) {
   p.scale_log2 = d->scale * 1.4426950408889634f;
   p.causal = d->causal;
   p.n_qtiles = (int)(d->seq / BQ);
+  p.bh = d->bh;
   p.status = d->status;
-  dim3 grid((unsigned)p.n_qtiles, (unsigned)d->bh);
+  dim3 grid((unsigned)(p.n_qtiles * d->bh));   // rows / 128 < 2^31
   k_fmha_tcgen05<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? KTIR_OK : KTIR_ERR_CUDA;
 }
