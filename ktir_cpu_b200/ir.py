@@ -15,8 +15,24 @@ from typing import Any, Dict, Iterator, List, Tuple
 
 @dataclass
 class Region:
-    args: List[Tuple[str, str]] = field(default_factory=list)  # ^bb0 block arguments
+    args: List[Tuple[str, str]] = field(default_factory=list)  # block arguments
     ops: List["Operation"] = field(default_factory=list)
+    label: bool = False   # the arguments come from a ``^bb0(...)`` label
+
+
+def linalg_block_args(region: Region) -> List[str]:
+    """Block-argument names of a ``linalg.reduce`` / ``linalg.generic``
+    region, found the way the reference finds them
+    (ktir_cpu/dialects/linalg_ops.py:30-58): the arguments of a ``^bb0(...)``
+    label, else the operands of the region's first op.  An inline
+    ``(%in: f32, %out: f32) {`` list is therefore read from the first op: a
+    region whose first op is ``arith.mulf %in, %in`` binds ``%in`` twice and
+    leaves ``%out`` unbound, as in the reference."""
+    if region.label and region.args:
+        return [n for n, _ in region.args]
+    if region.ops:
+        return list(region.ops[0].operands)
+    return [n for n, _ in region.args]
 
 
 @dataclass

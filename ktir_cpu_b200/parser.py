@@ -424,6 +424,7 @@ class KTIRParser(KTIRParserBase):
 
     def parse_region(self, pre: str, body: str) -> Region:
         args: List[Tuple[str, str]] = []
+        label = False
         if pre:
             args = self._parse_args(pre)
         stripped = body.strip()
@@ -431,8 +432,9 @@ class KTIRParser(KTIRParserBase):
         if m:
             if m.group(2):
                 args = self._parse_args(m.group(2))
+                label = True
             stripped = stripped[m.end():]
-        return Region(args=args, ops=self.parse_block(stripped))
+        return Region(args=args, ops=self.parse_block(stripped), label=label)
 
     def parse_statement(self, stmt: str) -> Optional[Operation]:
         text, raw_regions = extract_regions(stmt)

@@ -39,7 +39,7 @@ from typing import Any, Dict, List, Optional, Sequence, Tuple
 import numpy as np
 
 from .affine import AffineMap, BoxSet
-from .ir import IRFunction, Operation, iter_ops
+from .ir import IRFunction, Operation, iter_ops, linalg_block_args
 
 STICK = 128
 LX_CAPACITY = 2 * 1024 * 1024
@@ -1374,13 +1374,68 @@ def _bcast_to(tr, v: Node, shape):
     return tr.node("bcast", shape, v.dtype, (v,), {"map": tuple(range(off, nd))}, v.label)
 
 
+def _region_fold(tr, t: Node, dim, region, names) -> Node:
+    """linalg.reduce with a multi-op combiner region, folded the way the
+    reference folds it (ktir_cpu/dialects/linalg_ops.py:60-133, 196-207):
+    each round runs the region once on the two halves of the reduced axis
+    (first half bound to the first block argument, second half to the
+    second), an odd leftover slice is carried into the next round, and the
+    axis of extent 1 is squeezed at the end.  The region's ops become
+    ordinary graph nodes over slices of the running accumulator, so the
+    generic executor runs the fold; a name the region reads but the block
+    arguments do not bind fails here as it does in the reference."""
+    acc = t
+    if dim is None:
+        acc = tr.node("reshape", (t.numel,), t.dtype, (t,), {}, t.label)
+        dim = 0
+    n = acc.shape[dim]
+
+    def part(src, lo, hi):
+        shape = tuple(hi - lo if i == dim else s for i, s in enumerate(src.shape))
+        at = tuple(lo if i == dim else 0 for i in range(len(src.shape)))
+        return tr.node("slice", shape, src.dtype, (src,), {"at": at}, src.label)
+
+    lat, tr.lat = tr.lat, None   # the fold's latency is charged by _lat_fold
+    try:
+        return _region_rounds(tr, t, acc, dim, n, region, names, part)
+    finally:
+        tr.lat = lat
+
+
+def _region_rounds(tr, t, acc, dim, n, region, names, part) -> Node:
+    while n > 1:
+        h = n // 2
+        tr.core.push()
+        try:
+            if names:
+                tr.core.set(names[0], part(acc, 0, h))
+            if len(names) > 1:
+                tr.core.set(names[1], part(acc, h, 2 * h))
+            r = tr.run_ops(list(region.ops))
+        finally:
+            tr.core.pop()
+        c = r.values[0] if isinstance(r, _Yield) else r
+        if not _is_tile(c) or c.dtype != t.dtype:
+            raise NotImplementedError("linalg.reduce: a combiner region that changes the "
+                                      "element type or yields a scalar")
+        if n % 2:
+            shape = tuple(h + 1 if i == dim else s for i, s in enumerate(c.shape))
+            tail_at = tuple(h if i == dim else 0 for i in range(len(shape)))
+            c = tr.node("assemble", shape, t.dtype, (c, part(acc, 2 * h, n)),
+                        {"at": [(0,) * len(shape), tail_at]}, t.label)
+        acc = c
+        n = h + (n % 2)
+    shape = tuple(s for i, s in enumerate(acc.shape) if i != dim)
+    return tr.node("reshape", shape, t.dtype, (acc,), {}, t.label, pyscalar=not shape)
+
+
 def _op_linalg_reduce(self, op):
     t = self.core.get(op.operands[0])
     a = op.attributes
     if op.regions and op.regions[0].ops:
         region = op.regions[0]
         body = [o for o in region.ops if o.op_type != "linalg.yield"]
-        names = [n for n, _ in region.args] or list(body[0].operands)
+        names = linalg_block_args(region)
         if len(body) != 1 or list(body[0].operands[:2]) not in (names[:2], names[:2][::-1]):
             comb = ("region", region, names)
         else:
@@ -1392,6 +1447,8 @@ def _op_linalg_reduce(self, op):
     dims = a.get("dims")
     if not _is_tile(t):
         res = t
+    elif isinstance(comb, tuple) and comb[0] == "region":
+        res = _region_fold(self, t, dims[0] if dims else None, comb[1], comb[2])
     else:
         dim = dims[0] if dims else None
         if dim is None:
@@ -1418,7 +1475,7 @@ def _lat_fold(self, op, t: Node, dim):
     if op.regions and op.regions[0].ops:
         region = op.regions[0]
         body = list(region.ops)
-        names = [n for n, _ in region.args] or list(body[0].operands)
+        names = linalg_block_args(region)
     else:
         fn = op.attributes.get("combiner") or "arith.addf"
         body = [Operation(fn, ["__comb__"], ["__in__", "__acc__"], {}),
@@ -1514,7 +1571,7 @@ def _op_linalg_generic(self, op):
     ins = [self.core.get(o) for o in op.operands[:n_ins]]
     outs = self.core.get(op.operands[n_ins])
     region = op.regions[0]
-    names = [n for n, _ in region.args] or list(region.ops[0].operands)
+    names = linalg_block_args(region)
     shape = outs.shape
     self.core.push()
     self.core.set("__linalg_shape__", shape)

@@ -49,7 +49,7 @@ from typing import Any, Dict, List, Optional, Tuple
 import numpy as np
 
 from ktir_cpu_b200.affine import BoxSet, eval_expr
-from ktir_cpu_b200.ir import IRModule, Operation, Region
+from ktir_cpu_b200.ir import IRModule, Operation, Region, linalg_block_args
 from ktir_cpu_b200.parser import KTIRParser
 
 STICK = 128
@@ -915,10 +915,8 @@ class OracleInterpreter:
         a = op.attributes
         if op.regions and op.regions[0].ops:
             region = op.regions[0]
-            names = [n for n, _ in region.args]
+            names = linalg_block_args(region)
             body = region.ops
-            if not names:
-                names = list(body[0].operands)
         else:
             comb = a.get("combiner") or "arith.addf"
             names = ["%__in", "%__acc"]
@@ -1008,7 +1006,7 @@ class OracleInterpreter:
         ins = [core.get(o) for o in op.operands[:n_ins]]
         outs = core.get(op.operands[n_ins])
         region = op.regions[0]
-        names = [n for n, _ in region.args] or list(region.ops[0].operands)
+        names = linalg_block_args(region)
         shape = outs.shape
         core.push()
         core.set("__linalg_shape__", shape)

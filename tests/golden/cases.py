@@ -781,3 +781,57 @@ case("paged_attention_8tok_8tiles", _paged_attention(), "paged_attention",
       "v_cache": rng.standard_normal((12, 16, 128)).astype(np.float16),
       "block_table": rng.permutation(12)[:8].astype(np.int32),
       "o": np.zeros((8, 128), np.float16)}, tol=1e-2)
+
+
+# --- linalg.reduce with region combiners: a two-op max (cmpf + select) over f16
+# rows of odd length, and an f32 combiner that is not symmetric in its two
+# arguments ((in - out) + in), whose result depends on which half of each
+# round the fold binds to which argument ------------------------------------
+def _region_reduce_case(name, comb_f32):
+    return _fn(name, ["x", "y", "m", "q"], [
+        "%c0 = arith.constant 0 : index",
+        _view("%xv", "%x", (24, 300), "f16"),
+        _view("%yv", "%y", (24, 300), "f32"),
+        _view("%mv", "%m", (24,), "f16"),
+        _view("%qv", "%q", (24,), "f32"),
+        _tile("%xt", "%xv", ["%c0", "%c0"], (24, 300), "f16", (24, 300)),
+        _tile("%yt", "%yv", ["%c0", "%c0"], (24, 300), "f32", (24, 300)),
+        f"%x = ktdp.load %xt : {_at((24, 300))} -> {_tt((24, 300), 'f16')}",
+        f"%y = ktdp.load %yt : {_at((24, 300))} -> {_tt((24, 300), 'f32')}",
+        "%ninf = arith.constant 0xFC00 : f16",
+        "%z = arith.constant 0.0 : f32",
+        f"%m0 = tensor.splat %ninf : {_tt((24,), 'f16')}",
+        f"%q0 = tensor.splat %z : {_tt((24,), 'f32')}",
+        f"%mx = linalg.reduce ins(%x : {_tt((24, 300), 'f16')}) outs(%m0 : {_tt((24,), 'f16')}) dimensions = [1]\n"
+        "      (%in: f16, %out: f16) {\n"
+        "        %gt = arith.cmpf ogt, %in, %out : f16\n"
+        "        %mm = arith.select %gt, %in, %out : f16\n"
+        "        linalg.yield %mm : f16\n"
+        "      }",
+        f"%sq = linalg.reduce ins(%y : {_tt((24, 300), 'f32')}) outs(%q0 : {_tt((24,), 'f32')}) dimensions = [1]\n"
+        "      (%in: f32, %out: f32) {\n" + "".join(f"        {l}\n" for l in comb_f32) +
+        "      }",
+        _tile("%mt", "%mv", ["%c0"], (24,), "f16", (24,)),
+        _tile("%qt", "%qv", ["%c0"], (24,), "f32", (24,)),
+        f"ktdp.store %mx, %mt : {_tt((24,), 'f16')}, {_at((24,))}",
+        f"ktdp.store %sq, %qt : {_tt((24,), 'f32')}, {_at((24,))}",
+    ])
+
+
+_rx = rng.standard_normal((24, 300)).astype(np.float16)
+_ry = rng.standard_normal((24, 300)).astype(np.float32)
+case("reduce_region_combiners", _region_reduce_case("rred", [
+    "%d = arith.subf %in, %out : f32",
+    "%a = arith.addf %d, %in : f32",
+    "linalg.yield %a : f32",
+]), "rred", {"x": _rx, "y": _ry, "m": np.zeros(24, np.float16), "q": np.zeros(24, np.float32)})
+
+# the inline argument list is not where the reference reads the block
+# arguments from: they are the first op's operands, here (%in, %in), so %out
+# is never bound and the call fails
+case("reduce_region_inline_args", _region_reduce_case("rred2", [
+    "%p = arith.mulf %in, %in : f32",
+    "%a = arith.addf %out, %p : f32",
+    "linalg.yield %a : f32",
+]), "rred2", {"x": _rx, "y": _ry, "m": np.zeros(24, np.float16), "q": np.zeros(24, np.float32)},
+    expect_error="KeyError")
