@@ -905,6 +905,37 @@ class Tracer:
             return np.float32(v)
         return self._cast_to(v, np.dtype(np.float32), "f32", True, "extf")
 
+    def op_arith_convertf(self, op):
+        """ArithOps.convertf (ktir_cpu/ops/arith_ops.py:660-668): f16 becomes
+        f32, any other element type becomes f16."""
+        v = self.core.get(op.operands[0])
+        if isinstance(v, Node):
+            tgt = np.dtype(np.float32 if v.dtype == np.float16 else np.float16)
+            if _is_tile(v):
+                return self.node("ew", v.shape, tgt, (v,), {"op": "cast"}, "convertf")
+            return self.node("ew", (), tgt, (v,), {"op": "cast"}, "convertf")
+        return np.float32(v) if isinstance(v, np.float16) else np.float16(v)
+
+    def op_ktdp_coreid(self, op):
+        """GridOps.coreid (ktir_cpu/ops/grid_ops.py:43-62, ktir_cpu/grid.py:
+        402-470): the linear ids of the cores at grid coordinates padded with
+        0 to three axes, -1 matching every position on its axis."""
+        want = []
+        for o in op.operands:
+            v = self.core.get(o)
+            if isinstance(v, Node):
+                raise NotImplementedError("ktdp.coreid of a data-dependent coordinate")
+            want.append(int(v))
+        want = (want + [0, 0, 0])[:3]
+        nx, ny, nz = self.func.grid
+        out = []
+        for cid in range(nx * ny * nz):
+            z, r = divmod(cid, nx * ny)
+            y, x = divmod(r, nx)
+            if all(w == -1 or w == p for w, p in zip(want, (x, y, z))):
+                out.append(cid)
+        return out
+
     def op_arith_truncf(self, op):
         return self._cast_to(self.core.get(op.operands[0]), np.dtype(np.float16), "f16", True,
                              "truncf")

@@ -757,6 +757,27 @@ class OracleInterpreter:
             return np.float32(v)
         return self._cast(core, op, np.float32, True, "extf")
 
+    def op_arith_convertf(self, core, op):
+        # ktir_cpu/ops/arith_ops.py:660-668
+        v = core.get(op.operands[0])
+        if isinstance(v, Tile):
+            if v.data.dtype == np.float16:
+                return Tile(v.data.astype(np.float32), "f32", v.shape)
+            return Tile(v.data.astype(np.float16), "f16", v.shape)
+        return np.float32(v) if isinstance(v, np.float16) else np.float16(v)
+
+    def op_ktdp_coreid(self, core, op):
+        # ktir_cpu/ops/grid_ops.py:43-62 with ktir_cpu/grid.py:402-470
+        want = ([int(core.get(o)) for o in op.operands] + [0, 0, 0])[:3]
+        nx, ny, nz = self.grid
+        out = []
+        for cid in range(nx * ny * nz):
+            z, r = divmod(cid, nx * ny)
+            y, x = divmod(r, nx)
+            if all(w == -1 or w == p for w, p in zip(want, (x, y, z))):
+                out.append(cid)
+        return out
+
     def op_arith_truncf(self, core, op):
         return self._cast(core, op, np.float16, True, "truncf")
 

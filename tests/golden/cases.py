@@ -835,3 +835,29 @@ case("reduce_region_inline_args", _region_reduce_case("rred2", [
     "linalg.yield %a : f32",
 ]), "rred2", {"x": _rx, "y": _ry, "m": np.zeros(24, np.float16), "q": np.zeros(24, np.float32)},
     expect_error="KeyError")
+
+# --- arith.convertf (f16 -> f32, f32 -> f16) and ktdp.coreid on a 2 x 2 grid
+# (the core ids of a grid row; the reference returns them as a list that this
+# program does not read further) ----------------------------------------------
+case("convertf_coreid", _fn("cvt", ["x", "y", "a", "b"], [
+    "%c = ktdp.get_compute_tile_id : index",
+    "%c0 = arith.constant 0 : index",
+    "%m1 = arith.constant -1 : index",
+    "%row = ktdp.coreid %m1, %c0 : index, index",
+    "%c64 = arith.constant 64 : index",
+    "%off = arith.muli %c, %c64 : index",
+    _view("%xv", "%x", (128,), "f16"), _view("%yv", "%y", (128,), "f32"),
+    _view("%av", "%a", (128,), "f32"), _view("%bv", "%b", (128,), "f16"),
+    _tile("%xt", "%xv", ["%off"], (128,), "f16", (64,)),
+    _tile("%yt", "%yv", ["%off"], (128,), "f32", (64,)),
+    _tile("%at", "%av", ["%off"], (128,), "f32", (64,)),
+    _tile("%bt", "%bv", ["%off"], (128,), "f16", (64,)),
+    f"%x = ktdp.load %xt : {_at((64,))} -> {_tt((64,), 'f16')}",
+    f"%y = ktdp.load %yt : {_at((64,))} -> {_tt((64,), 'f32')}",
+    f"%xw = arith.convertf %x : {_tt((64,), 'f16')} to {_tt((64,), 'f32')}",
+    f"%yn = arith.convertf %y : {_tt((64,), 'f32')} to {_tt((64,), 'f16')}",
+    f"ktdp.store %xw, %at : {_tt((64,), 'f32')}, {_at((64,))}",
+    f"ktdp.store %yn, %bt : {_tt((64,), 'f16')}, {_at((64,))}",
+], grid=(2, 1)), "cvt", {"x": rng.standard_normal(128).astype(np.float16),
+                        "y": (rng.standard_normal(128) * 300).astype(np.float32),
+                        "a": np.zeros(128, np.float32), "b": np.zeros(128, np.float16)})
