@@ -12,6 +12,8 @@
 
 #include "../../include/ktir_b200.h"
 
+int ktir_set_error(int code, const char* msg);
+
 namespace {
 
 constexpr int64_t kMaxRows = KTIR_STATIC_RMW_MAX_ROWS;
@@ -22,7 +24,6 @@ static __device__ __align__(256) int32_t g_rmw_counts[kMaxRows];
 
 int32_t* g_counts_addr[kMaxDevices] = {nullptr};
 std::mutex g_lock;
-thread_local char g_msg[256];
 
 }  // namespace
 
@@ -31,10 +32,14 @@ extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* desc, const KtirBuffers*
 
 extern "C" int ktir_gather_rmw_static(const KtirGatherRmwDesc* desc, const KtirBuffers* bufs,
                                       int64_t n_rows, int32_t* status, void* stream) {
-  if (!desc || !bufs || !status) return KTIR_ERR_ARG;
-  if (n_rows < 0 || n_rows > kMaxRows) return KTIR_ERR_UNSUPPORTED;
+  if (!desc || !bufs || !status)
+    return ktir_set_error(KTIR_ERR_ARG, "ktir_gather_rmw_static: null argument");
+  if (n_rows < 0 || n_rows > kMaxRows)
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED,
+                          "ktir_gather_rmw_static: n_rows outside [0, KTIR_STATIC_RMW_MAX_ROWS]");
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return KTIR_ERR_CUDA;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return ktir_set_error(KTIR_ERR_CUDA, "ktir_gather_rmw_static: no usable current device");
   int32_t* counts;
   {
     // set-up, once per device, with that device current
@@ -42,14 +47,18 @@ extern "C" int ktir_gather_rmw_static(const KtirGatherRmwDesc* desc, const KtirB
     if (!g_counts_addr[dev]) {
       void* p = nullptr;
       cudaError_t e = cudaGetSymbolAddress(&p, g_rmw_counts);
-      if (e != cudaSuccess || p == nullptr) return KTIR_ERR_CUDA;
+      if (e != cudaSuccess || p == nullptr)
+        return ktir_set_error(KTIR_ERR_CUDA, "ktir_gather_rmw_static: cudaGetSymbolAddress failed");
       g_counts_addr[dev] = static_cast<int32_t*>(p);
     }
     counts = g_counts_addr[dev];
   }
-  // the array keeps the previous call's contents: the counts must start at zero
-  if (n_rows > 0 &&
+  // The array keeps the previous call's contents.  The count pass needs them
+  // at zero; an apply-only call (phases == 2) consumes the counts that its
+  // count-only call (phases == 1) left, so it must not clear them.
+  const bool do_count = desc->phases == 0 || (desc->phases & 1);
+  if (do_count && n_rows > 0 &&
       cudaMemsetAsync(counts, 0, (size_t)n_rows * sizeof(int32_t), (cudaStream_t)stream) != cudaSuccess)
-    return KTIR_ERR_CUDA;
+    return ktir_set_error(KTIR_ERR_CUDA, "ktir_gather_rmw_static: clearing the counts failed");
   return ktir_gather_rmw(desc, bufs, counts, n_rows, status, stream);
 }
