@@ -43,6 +43,7 @@ __device__ __forceinline__ float round_to(float x, int dt) {
 
 __device__ __forceinline__ long long wrap_to(long long v, int dt) {
   if (dt == KTIR_I32) return (long long)(int)v;
+  if (dt == KTIR_U32) return (long long)(unsigned)v;
   if (dt == KTIR_BOOL) return v != 0;
   return v;
 }
@@ -62,6 +63,7 @@ __device__ __forceinline__ Reg load_elem(const KtirBuffers& b, int slot, int dt,
     case KTIR_I32: r.i = ((const int*)p)[off]; break;
     case KTIR_I64: r.i = ((const long long*)p)[off]; break;
     case KTIR_BOOL: r.i = ((const uint8_t*)p)[off] != 0; break;
+    case KTIR_U32: r.i = ((const unsigned*)p)[off]; break;
   }
   return r;
 }
@@ -87,6 +89,9 @@ __device__ __forceinline__ void store_elem(const KtirBuffers& b, int slot, int d
       break;
     case KTIR_BOOL:
       ((uint8_t*)p)[off] = fsrc ? (v.f != 0.f) : (v.i != 0);
+      break;
+    case KTIR_U32:
+      ((unsigned*)p)[off] = fsrc ? (unsigned)(long long)v.f : (unsigned)v.i;
       break;
   }
 }
@@ -168,6 +173,18 @@ __device__ __forceinline__ Reg convert(Reg v, int from, int to) {
       r.f = round_to(v.f, to);
     } else if (to == KTIR_BOOL) {
       r.i = v.f != 0.f;
+    } else if (to == KTIR_I32) {
+      // NumPy's float -> int32 cast (x86): truncation toward zero, and the
+      // integer-indefinite value INT32_MIN for NaN and out-of-range inputs
+      r.i = (v.f > -2147483904.f && v.f < 2147483648.f) ? (long long)(int)v.f : (long long)INT32_MIN;
+    } else if (to == KTIR_U32) {
+      // NumPy's float -> uint32 cast (x86): values below 2^31 go through a
+      // signed int32 (negative inputs wrap), [2^31, 2^32) convert directly;
+      // other inputs are invalid casts (NumPy warns), given 2^31 here
+      r.i = (v.f > -2147483904.f && v.f < 2147483648.f)
+                ? (long long)(unsigned)(int)v.f
+                : ((v.f >= 2147483648.f && v.f < 4294967296.f) ? (long long)(unsigned)v.f
+                                                                 : 2147483648ll);
     } else {
       r.i = wrap_to((long long)v.f, to);
     }

@@ -24,12 +24,12 @@ MAX_INSTR = 64
 NREG = 12
 ARENA_SLOT = MAX_BUFFERS - 1
 
-F16, F32, I32, I64, BOOL = 0, 1, 2, 3, 4
+F16, F32, I32, I64, BOOL, U32 = 0, 1, 2, 3, 4, 5
 STATUS_NEGATIVE_INDEX = 1
 STATUS_TIMEOUT = 2
 
 _DT = {np.dtype(np.float16): F16, np.dtype(np.float32): F32, np.dtype(np.int32): I32,
-       np.dtype(np.int64): I64, np.dtype(np.bool_): BOOL}
+       np.dtype(np.int64): I64, np.dtype(np.bool_): BOOL, np.dtype(np.uint32): U32}
 
 
 def dtype_code(dt) -> int:

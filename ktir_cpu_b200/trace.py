@@ -59,7 +59,7 @@ NP = {
     "i64": np.int64, "si64": np.int64,
 }
 LABEL = {np.dtype(np.float16): "f16", np.dtype(np.float32): "f32", np.dtype(np.int32): "i32",
-         np.dtype(np.int64): "i64", np.dtype(np.bool_): "i1"}
+         np.dtype(np.int64): "i64", np.dtype(np.bool_): "i1", np.dtype(np.uint32): "ui32"}
 
 
 def np_dtype(name: str) -> np.dtype:
@@ -957,7 +957,9 @@ class Tracer:
     def op_arith_fptosi(self, op):
         return self._int_cast(op, np.dtype(np.int32), "i32")
 
-    op_arith_fptoui = op_arith_fptosi
+    def op_arith_fptoui(self, op):
+        # an unsigned tile, whatever the result type says (ops/arith_ops.py:504-508)
+        return self._int_cast(op, np.dtype(np.uint32), "ui32")
 
     def op_arith_sitofp(self, op):
         v = self.core.get(op.operands[0])

@@ -802,7 +802,12 @@ class OracleInterpreter:
             return Tile(v.data.astype(np.int32), "i32", v.shape)
         return int(v)
 
-    op_arith_fptoui = op_arith_fptosi
+    def op_arith_fptoui(self, core, op):
+        # ops/arith_ops.py:504-508: a uint32 tile labelled "ui32"
+        v = core.get(op.operands[0])
+        if isinstance(v, Tile):
+            return Tile(v.data.astype(np.uint32), "ui32", v.shape)
+        return int(v)
 
     def op_arith_extsi(self, core, op):
         v = core.get(op.operands[0])

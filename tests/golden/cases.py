@@ -861,3 +861,26 @@ case("convertf_coreid", _fn("cvt", ["x", "y", "a", "b"], [
 ], grid=(2, 1)), "cvt", {"x": rng.standard_normal(128).astype(np.float16),
                         "y": (rng.standard_normal(128) * 300).astype(np.float32),
                         "a": np.zeros(128, np.float32), "b": np.zeros(128, np.float16)})
+
+# --- arith.fptoui: an unsigned result (the reference's uint32 tile), stored into
+# an i32 buffer and widened back to f32; inputs span negative values (which wrap)
+# and values at and above 2^31 --------------------------------------------------
+_fu = np.concatenate([rng.uniform(-1000, 1000, 96), rng.uniform(2.0 ** 31, 4.0e9, 24),
+                      [2.0 ** 31, -0.5, -1.5, 0.75, 4294967040.0, 2.0 ** 31 - 128, -2.0 ** 30, 3.0]])
+case("fptoui_unsigned", _fn("fpu", ["x", "u", "w", "s"], [
+    "%c0 = arith.constant 0 : index",
+    _view("%xv", "%x", (128,), "f32"), _view("%uv", "%u", (128,), "i32"),
+    _view("%wv", "%w", (128,), "f32"), _view("%sv", "%s", (128,), "i32"),
+    _tile("%xt", "%xv", ["%c0"], (128,), "f32", (128,)),
+    _tile("%ut", "%uv", ["%c0"], (128,), "i32", (128,)),
+    _tile("%wt", "%wv", ["%c0"], (128,), "f32", (128,)),
+    _tile("%st", "%sv", ["%c0"], (128,), "i32", (128,)),
+    f"%x = ktdp.load %xt : {_at((128,))} -> {_tt((128,), 'f32')}",
+    f"%u = arith.fptoui %x : {_tt((128,), 'f32')} to {_tt((128,), 'i32')}",
+    f"%w = arith.uitofp %u : {_tt((128,), 'i32')} to {_tt((128,), 'f32')}",
+    f"%s = arith.fptosi %x : {_tt((128,), 'f32')} to {_tt((128,), 'i32')}",
+    f"ktdp.store %u, %ut : {_tt((128,), 'i32')}, {_at((128,))}",
+    f"ktdp.store %w, %wt : {_tt((128,), 'f32')}, {_at((128,))}",
+    f"ktdp.store %s, %st : {_tt((128,), 'i32')}, {_at((128,))}",
+]), "fpu", {"x": _fu.astype(np.float32), "u": np.zeros(128, np.int32),
+            "w": np.zeros(128, np.float32), "s": np.zeros(128, np.int32)})
