@@ -50,7 +50,8 @@ extern "C" {
 #define KTIR_STATUS_NEGATIVE_INDEX 1
 #define KTIR_STATUS_TIMEOUT 2
 
-enum KtirDtype { KTIR_F16 = 0, KTIR_F32 = 1, KTIR_I32 = 2, KTIR_I64 = 3, KTIR_BOOL = 4 };
+enum KtirDtype { KTIR_F16 = 0, KTIR_F32 = 1, KTIR_I32 = 2, KTIR_I64 = 3, KTIR_BOOL = 4,
+                 KTIR_U32 = 5 /* arith.fptoui results (NumPy uint32 tiles) */ };
 
 typedef struct {
   void* base[KTIR_MAX_BUFFERS];
@@ -231,10 +232,13 @@ int ktir_indirect(const KtirIndirectDesc* desc, const KtirBuffers* bufs,
  * KTIR_STATIC_RMW_MAX_ROWS int32 (4 MiB) that every GPU loading this library
  * holds until the process exits; tables with more rows are rejected with
  * KTIR_ERR_UNSUPPORTED.  The first call on a device looks up the array's
- * device address (make that first call before any stream capture); every
- * call clears the first n_rows counts on `stream`.  All calls share the one
- * array, so calls that overlap on the GPU (other streams, other threads)
- * race and give wrong results.  Allocates nothing: no cudaMalloc/cudaFree. */
+ * device address (make that first call before any stream capture).  A call
+ * that runs the count pass (phases 0 or 1) first clears the first n_rows
+ * counts on `stream`; an apply-only call (phases 2) uses the counts its
+ * count-only call left, so the two must go on one stream with no other call
+ * of this entry point between them.  All calls share the one array, so calls
+ * that overlap on the GPU (other streams, other threads) race and give wrong
+ * results.  Allocates nothing: no cudaMalloc/cudaFree. */
 #define KTIR_STATIC_RMW_MAX_ROWS (1 << 20)
 int ktir_gather_rmw_static(const KtirGatherRmwDesc* desc, const KtirBuffers* bufs,
                            int64_t n_rows, int32_t* status, void* stream);

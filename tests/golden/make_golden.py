@@ -1,9 +1,9 @@
 """Regenerate tests/golden/*.npz by running the ktir-cpu reference interpreter.
 
-Usage (in a checkout that has the reference at REFERENCE_ROOT, default
-/root/reference):
+Usage (REFERENCE_ROOT is a checkout of the ktir-cpu reference; the first
+argument, else the KTIR_REFERENCE_ROOT environment variable):
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT] [CASE_NAME ...]
+    python tests/golden/make_golden.py REFERENCE_ROOT [CASE_NAME ...]
 
 With case names, only those fixtures are regenerated.
 
@@ -27,7 +27,10 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 
 
 def main() -> None:
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KTIR_REFERENCE_ROOT")
+    if not ref_root or not os.path.isdir(os.path.join(ref_root, "ktir_cpu")):
+        raise SystemExit("give the reference checkout as the first argument "
+                         "(or set KTIR_REFERENCE_ROOT)")
     only = set(sys.argv[2:])
     sys.dont_write_bytecode = True
     sys.path.insert(0, ref_root)
