@@ -5,24 +5,28 @@
 // 64 rows with three warp roles that meet only at mbarriers; two CTAs share
 // an SM, so while one CTA's softmax warps work the other's keep the tensor
 // cores busy:
-//   warps 4, 6 (TMA)  warp 4 loads Q once and K_j, warp 6 loads V_j, each into
-//                     its own 2-stage ring, every slot refilled as soon as the
-//                     MMA that read it completes
+//   warps 4, 6 (TMA)  warp 4 loads Q once and K_j into a 2-stage ring, warp 6
+//                     loads V_j into a 1-stage ring, every slot refilled as soon
+//                     as the MMA that read it completes
 //   warp 5 (MMA)      S_j = Q K_j^T (M=128 N=64 K=128) into TMEM S buffer
 //                     j & 1; as soon as the softmax warps hand over P_j it
-//                     issues O += P_j V_j (M=128 N=128 K=64) and S_{j+2} into
-//                     the buffer S_j has just left, so the next two S blocks
-//                     are always computed ahead of the softmax
+//                     issues O += Phi_j V_j + Plo_j V_j (M=128 N=128 K=2x64)
+//                     and S_{j+2} into the buffer S_j has just left, so the
+//                     next two S blocks are always computed ahead of the softmax
 //   warps 0-3         thread t owns query row t = TMEM lane t: tcgen05.ld of
 //                     S_j, masked max of x = s * scale * log2(e), P = 2^(x - m)
-//                     evaluated in f16 pairs (P is f16 in the PV product
-//                     anyway), written as one 128-byte swizzled row of the P
-//                     tile in shared memory; row sum l from f16 pair partials
+//                     in f32, split into Phi = f16(P) and Plo = f16(P - Phi),
+//                     each written as one 128-byte swizzled row of its tile in
+//                     shared memory; row sum l in f32.  The two f16 halves
+//                     carry P to about 22 bits, so the PV product keeps the
+//                     f32 probabilities of the reference's online softmax
+//                     (an f16 P alone moves outputs that cancel by more than
+//                     1e-2 of their value)
 // TMEM (256 columns): S0 0..63, S1 64..127, O 128..255.  The running max m
 // only moves when a row's max exceeds it by more than 2^8; then the softmax
 // warp waits for the previous PV and rescales its O rows in TMEM
 // (warp-uniform), otherwise O and l keep sharing m.
-// Shared memory (Q, K and V rings, P, mbarriers) fills exactly half an SM, so
+// Shared memory (Q, K and V rings, Phi, Plo, mbarriers) fills exactly half an SM, so
 // the dynamic allocation keeps only 896 bytes for aligning the tiles to the
 // 1024 bytes the 128-byte swizzle needs; a CTA whose window cannot be aligned
 // within that reports KTIR_STATUS_TIMEOUT and does nothing.
@@ -44,7 +48,7 @@ constexpr int D = 128;          // head dim
 constexpr int BQ = 128;         // query rows per CTA
 constexpr int BKV = 64;         // key rows per block
 constexpr int KST = 2;          // K ring stages
-constexpr int VST = 2;          // V ring stages
+constexpr int VST = 1;          // V ring stages
 constexpr int THREADS = 224;
 constexpr int HEAD_GROUP = 16;   // heads per group of the CTA order (16 MiB of K/V at S=2048)
 constexpr int Q_HALF = BQ * 64 * 2;             // 16 KiB: 128 rows x 64 columns
@@ -52,7 +56,7 @@ constexpr int Q_BYTES = 2 * Q_HALF;             // 32 KiB
 constexpr int KV_HALF = BKV * 64 * 2;           // 8 KiB: 64 rows x 64 columns
 constexpr int KV_BYTES = 2 * KV_HALF;           // 16 KiB: 64 rows x 128 columns
 constexpr int P_BYTES = BQ * BKV * 2;           // 16 KiB: 128 rows x 64 keys
-constexpr int TILE_BYTES = Q_BYTES + (KST + VST) * KV_BYTES + P_BYTES;
+constexpr int TILE_BYTES = Q_BYTES + (KST + VST) * KV_BYTES + 2 * P_BYTES;   // Phi, Plo
 constexpr int ALIGN_SLACK = 896;
 
 struct Bars {
@@ -70,6 +74,10 @@ static_assert(2 * (SMEM_BYTES + 1024) <= 228 * 1024, "two CTAs per SM");
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t O_COL = 128;
 constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
+// P is evaluated as 2^(x - m + P_OFFSET): the row's largest P lies in
+// [2^7, 2^15] (below the f16 maximum), and P down to 2^-14 * 2^-7 of the row's
+// largest stays a normal f16 in both halves; O and l carry the same factor
+constexpr float P_OFFSET = 7.0f;
 
 struct FmhaParams {
   __half* o;
@@ -85,14 +93,6 @@ struct FmhaParams {
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// 2^x for a pair: x rounded to f16, one MUFU op for both lanes of the pair
-__device__ __forceinline__ uint32_t ex2_pair(float a, float b) {
-  uint32_t h, y;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(h));
   return y;
 }
 
@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   const uint32_t sK = base + Q_BYTES;
   const uint32_t sV = sK + KST * KV_BYTES;
   const uint32_t sP = sV + VST * KV_BYTES;
+  const uint32_t sPl = sP + P_BYTES;
   Bars& B = *reinterpret_cast<Bars*>(smem_raw + (base - raw) + TILE_BYTES);
   volatile int* abort = &B.abort_flag;
 
@@ -230,10 +231,12 @@ __global__ void __launch_bounds__(THREADS, 2)
         if (!mbar_wait(smem_u32(&B.v_full[vs]), (j / VST) & 1, abort)) break;
         tc_fence_after();
         const uint32_t vb = sV + vs * KV_BYTES;
+        // O += Phi V + Plo V: the K steps of both halves read the same V rows
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(sP + kk * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(vb + kk * 16 * 128, KV_HALF, 1024);
+        for (int kk = 0; kk < 2 * (BKV / 16); ++kk) {
+          const uint32_t pt = kk < BKV / 16 ? sP : sPl;
+          const uint64_t ad = sdesc_sw128(pt + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(vb + (kk & 3) * 16 * 128, KV_HALF, 1024);
           mma_f16(tmem + O_COL, ad, bd, idesc_pv, (j | kk) != 0);
         }
         mma_commit(smem_u32(&B.pv_done));
@@ -288,23 +291,19 @@ __global__ void __launch_bounds__(THREADS, 2)
         l_run *= factor;
         m_used = m_new;
       }
-      const float msub = (m_used == -INFINITY) ? 0.f : m_used;
-      uint32_t ph[BKV / 2];
-      // the row sum adds P in f16 pairs four at a time (each P <= 2^8, so a
-      // partial stays below 2^11 and keeps 2^-11 relative precision), then
-      // in f32
-      __half2 h8[8];
-#pragma unroll
-      for (int i = 0; i < BKV; i += 2) {
-        ph[i / 2] = ex2_pair(fmaf(sv[i], p.scale_log2, -msub), fmaf(sv[i + 1], p.scale_log2, -msub));
-        const __half2 v2 = *reinterpret_cast<const __half2*>(&ph[i / 2]);
-        h8[(i / 2) & 7] = (i < 16) ? v2 : __hadd2(h8[(i / 2) & 7], v2);
-      }
+      const float msub = (m_used == -INFINITY) ? 0.f : m_used - P_OFFSET;
+      uint32_t ph[BKV / 2], pl[BKV / 2];
+      // P in f32, its f16 head and the f16 rounding of the remainder; the row
+      // sum adds the f32 P in eight partial sums
       float s8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float2 f = __half22float2(h8[i]);
-        s8[i] = f.x + f.y;
+      for (int i = 0; i < BKV; i += 2) {
+        const float a = ex2(fmaf(sv[i], p.scale_log2, -msub));
+        const float b = ex2(fmaf(sv[i + 1], p.scale_log2, -msub));
+        ph[i / 2] = pack_h2(a, b);
+        const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&ph[i / 2]));
+        pl[i / 2] = pack_h2(a - hf.x, b - hf.y);
+        s8[(i / 2) & 7] = (i < 16) ? a + b : s8[(i / 2) & 7] + (a + b);
       }
 #pragma unroll
       for (int h = 4; h >= 1; h >>= 1)
@@ -328,7 +327,8 @@ __global__ void __launch_bounds__(THREADS, 2)
           }
         }
       }
-      // P_j: row tid of the K-major tile, 128-byte swizzle (chunk u at u ^ (row & 7))
+      // Phi_j, Plo_j: row tid of each K-major tile, 128-byte swizzle (chunk u
+      // at u ^ (row & 7))
       {
         const uint32_t rowaddr = sP + tid * 128;
 #pragma unroll
@@ -336,6 +336,9 @@ __global__ void __launch_bounds__(THREADS, 2)
           const uint32_t dst = rowaddr + ((u ^ (tid & 7)) << 4);
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(ph[4 * u]),
                        "r"(ph[4 * u + 1]), "r"(ph[4 * u + 2]), "r"(ph[4 * u + 3])
+                       : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst + P_BYTES),
+                       "r"(pl[4 * u]), "r"(pl[4 * u + 1]), "r"(pl[4 * u + 2]), "r"(pl[4 * u + 3])
                        : "memory");
         }
       }
