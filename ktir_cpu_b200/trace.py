@@ -1448,16 +1448,27 @@ def _region_rounds(tr, t, acc, dim, n, region, names, part) -> Node:
         finally:
             tr.core.pop()
         c = r.values[0] if isinstance(r, _Yield) else r
-        if not _is_tile(c) or c.dtype != t.dtype:
-            raise NotImplementedError("linalg.reduce: a combiner region that changes the "
-                                      "element type or yields a scalar")
+        if not _is_tile(c):
+            raise NotImplementedError("linalg.reduce: a combiner region that yields a scalar")
         if n % 2:
+            # the odd slice joins the combined one as NumPy's concatenate joins
+            # them: both in the wider of the two element types
+            tail = part(acc, 2 * h, n)
+            dt = np.result_type(c.dtype, tail.dtype)
+            if c.dtype != dt:
+                c = tr.node("ew", c.shape, dt, (c,), {"op": "cast"}, t.label)
+            if tail.dtype != dt:
+                tail = tr.node("ew", tail.shape, dt, (tail,), {"op": "cast"}, t.label)
             shape = tuple(h + 1 if i == dim else s for i, s in enumerate(c.shape))
             tail_at = tuple(h if i == dim else 0 for i in range(len(shape)))
-            c = tr.node("assemble", shape, t.dtype, (c, part(acc, 2 * h, n)),
+            c = tr.node("assemble", shape, dt, (c, tail),
                         {"at": [(0,) * len(shape), tail_at]}, t.label)
         acc = c
         n = h + (n % 2)
+    if acc.dtype != t.dtype:
+        # a combiner that changes the element type: the folded value is cast
+        # back to the input's type (linalg_ops.py:196-204)
+        acc = tr.node("ew", acc.shape, t.dtype, (acc,), {"op": "cast"}, t.label)
     shape = tuple(s for i, s in enumerate(acc.shape) if i != dim)
     return tr.node("reshape", shape, t.dtype, (acc,), {}, t.label, pyscalar=not shape)
 

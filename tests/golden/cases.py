@@ -884,3 +884,27 @@ case("fptoui_unsigned", _fn("fpu", ["x", "u", "w", "s"], [
     f"ktdp.store %s, %st : {_tt((128,), 'i32')}, {_at((128,))}",
 ]), "fpu", {"x": _fu.astype(np.float32), "u": np.zeros(128, np.int32),
             "w": np.zeros(128, np.float32), "s": np.zeros(128, np.int32)})
+
+# a combiner region that widens: f16 halves extended to f32 and added; the
+# rounds after the first see f32 data, the odd tails are joined in f32, and
+# the folded rows are cast back to f16 (linalg_ops.py:110-124, 196-204)
+case("reduce_region_widening", _fn("rwid", ["x", "m"], [
+    "%c0 = arith.constant 0 : index",
+    _view("%xv", "%x", (24, 300), "f16"),
+    _view("%mv", "%m", (24,), "f16"),
+    _tile("%xt", "%xv", ["%c0", "%c0"], (24, 300), "f16", (24, 300)),
+    f"%x = ktdp.load %xt : {_at((24, 300))} -> {_tt((24, 300), 'f16')}",
+    "%z = arith.constant 0.0 : f16",
+    f"%m0 = tensor.splat %z : {_tt((24,), 'f16')}",
+    f"%sm = linalg.reduce ins(%x : {_tt((24, 300), 'f16')}) outs(%m0 : {_tt((24,), 'f16')}) dimensions = [1]\n"
+    "      {\n"
+    "      ^bb0(%in: f16, %out: f16):\n"
+    "        %a = arith.extf %in : f16 to f32\n"
+    "        %b = arith.extf %out : f16 to f32\n"
+    "        %s = arith.addf %a, %b : f32\n"
+    "        linalg.yield %s : f32\n"
+    "      }",
+    _tile("%mt", "%mv", ["%c0"], (24,), "f16", (24,)),
+    f"ktdp.store %sm, %mt : {_tt((24,), 'f16')}, {_at((24,))}",
+]), "rwid", {"x": (8 * rng.standard_normal((24, 300))).astype(np.float16),
+             "m": np.zeros(24, np.float16)})
