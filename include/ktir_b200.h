@@ -187,6 +187,39 @@ typedef struct {
   int32_t* status;             /* device status word (KTIR_STATUS_TIMEOUT) */
 } KtirFmhaDesc;
 
+/* One step of an attention call split over the sequence (query tiles on this
+ * GPU, key tiles arriving from others).  Q and O are [bh*seq, 128] f16
+ * row-major; the call computes query tiles qtiles[0..n_qtiles) (128 rows
+ * each) of every head.  Key tile kt (128 rows) of head h is row
+ * ((kv_owner[kt] * bh + h) * kv_tiles + kv_local[kt]) * 128 of K and V
+ * (kv_rows rows of 128 f16 each): the blocks of each GPU's share of the
+ * sequence are stored together, one share after the other.  Only key tiles
+ * in key_mask (bit kt) are added, up to the query tile when causal.  The
+ * online-softmax state of each (head, query tile) is carried between steps in
+ * o_acc (bh * n_qtiles blocks of [128 columns][128 rows] f32) and ml (bh *
+ * n_qtiles * 128 (max, sum) f32 pairs); flags bit 0 = first step (no state
+ * read), bit 1 = last step (O written as f16, no state written).  seq <= 4096. */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  int64_t bh, seq, d;
+  int64_t kv_rows;
+  float scale;
+  int32_t causal;
+  int32_t n_qtiles;
+  int32_t kv_tiles;
+  uint32_t key_mask;
+  int32_t flags;
+  float* o_acc;
+  float* ml;
+  int32_t* status;
+  uint8_t qtiles[32];
+  uint8_t kv_owner[32];
+  uint8_t kv_local[32];
+} KtirFmhaPartDesc;
+
 /* ----------------------------------------------------------------------- */
 
 /* Library version (major*100 + minor). */
@@ -257,6 +290,29 @@ int ktir_gemm_f16(const KtirGemmDesc* desc, void* stream);
 /* Causal attention (replaces the online-softmax scf.for of matmul / reduce /
  * exp ops the attention rewrite recognises). */
 int ktir_fmha_f16(const KtirFmhaDesc* desc, void* stream);
+
+/* `rows` device-to-device copies of `width` bytes, row i from src + i *
+ * src_pitch to dst + i * dst_pitch, on `stream` (packs the K/V rows of one
+ * GPU's query tiles into its share of the ring's staging buffer; no
+ * counterpart in the reference, whose memory is one NumPy array). */
+int ktir_copy_blocks(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                     int64_t width, int64_t rows, void* stream);
+
+/* dst = a - b (subtract != 0) or a + b, byte by byte modulo 256, over n
+ * bytes on `stream`.  A call split across GPUs returns whole tensors by
+ * summing, over the GPUs, each one's byte differences from the tensor as it
+ * was uploaded (every byte changes on at most one GPU); the sum is an NCCL
+ * all-reduce between the two calls.  (No counterpart in the reference, which
+ * runs on one host.) */
+int ktir_bytes_delta(void* dst, const void* a, const void* b, int64_t n, int32_t subtract,
+                     void* stream);
+
+/* One step of a sequence-split attention call (see KtirFmhaPartDesc): the
+ * online-softmax K/V loop of the attention rewrite restricted to the key
+ * tiles one GPU holds at that step of the ring that passes K/V blocks
+ * between GPUs (the reference passes no data between cores: every core reads
+ * HBM, ktir_cpu/ops/memory_ops.py:438-587). */
+int ktir_fmha_f16_part(const KtirFmhaPartDesc* desc, void* stream);
 
 /* Host staging for calls made with host buffers (the reference keeps a
  * call's arrays in host memory, ktir_cpu/interpreter.py:137-177 and

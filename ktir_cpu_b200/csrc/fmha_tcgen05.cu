@@ -58,6 +58,7 @@ constexpr int KV_BYTES = 2 * KV_HALF;           // 16 KiB: 64 rows x 128 columns
 constexpr int P_BYTES = BQ * BKV * 2;           // 16 KiB: 128 rows x 64 keys
 constexpr int TILE_BYTES = Q_BYTES + (KST + VST) * KV_BYTES + 2 * P_BYTES;   // Phi, Plo
 constexpr int ALIGN_SLACK = 896;
+constexpr int MAX_TILES = 32;   // 128-row tiles of a sequence in a partial call (seq <= 4096)
 
 struct Bars {
   uint64_t q_full;
@@ -85,9 +86,22 @@ struct FmhaParams {
   long long row_stride;
   float scale_log2;   // scale * log2(e)
   int causal;
-  int n_qtiles;
+  int n_qtiles;       // query tiles per head this launch computes
   long long bh;
   int* status;
+  // partial calls (part != 0): the query tiles are qtiles[0..n_qtiles), key
+  // tile kt lives at row ((kv_owner[kt] * bh + head) * kv_tiles + kv_local[kt])
+  // * 128 of K and V, only key tiles in key_mask are added, and the softmax
+  // state of each (head, query tile) is carried between calls in o_acc / ml
+  int part;
+  int flags;          // bit 0: first call (no carried state); bit 1: last call (write O)
+  int kv_tiles;
+  unsigned key_mask;
+  float* o_acc;       // per (head, query tile): O as [128 columns][128 rows] f32
+  float2* ml;         // per (head, query tile): (running max, row sum) per row
+  unsigned char qtiles[MAX_TILES];
+  unsigned char kv_owner[MAX_TILES];
+  unsigned char kv_local[MAX_TILES];
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -138,11 +152,13 @@ __global__ void __launch_bounds__(THREADS, 2)
   const long long grp = lin / gsize;
   const long long heads = p.bh - grp * HEAD_GROUP < HEAD_GROUP ? p.bh - grp * HEAD_GROUP : HEAD_GROUP;
   const long long w = lin - grp * gsize;
-  const int qt = p.n_qtiles - 1 - (int)(w / heads);
+  const int qi = p.n_qtiles - 1 - (int)(w / heads);
+  const int qt = p.part ? (int)p.qtiles[qi] : qi;
   const long long head = grp * HEAD_GROUP + w % heads;
   const long long row0 = head * p.seq + (long long)qt * BQ;
   const int q0 = qt * BQ;
-  const int n_kv = p.causal ? (q0 + BQ) / BKV : (int)(p.seq / BKV);
+  const bool first = !p.part || (p.flags & 1);
+  const bool last = !p.part || (p.flags & 2);
 
   if (tid == 0) {
     B.abort_flag = 0;
@@ -168,12 +184,27 @@ __global__ void __launch_bounds__(THREADS, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = B.tmem_base;
+  // partial calls: the key tiles this CTA adds are those of the mask up to
+  // its own query tile when causal; each gives two key blocks, in order
+  const unsigned n_seq_tiles = (unsigned)(p.seq / BQ);
+  unsigned kmask = p.key_mask & (n_seq_tiles >= 32 ? ~0u : ((1u << n_seq_tiles) - 1u));
+  if (p.causal && qt < 31) kmask &= (2u << qt) - 1u;
+  const int n_kv = p.part ? 2 * __popc(kmask) : (p.causal ? (q0 + BQ) / BKV : (int)(p.seq / BKV));
+  // key block j of this CTA: its index in the sequence and its row in K / V
+  auto kv_block = [&](int j) -> int {
+    return p.part ? 2 * (int)__fns(kmask, 0, (j >> 1) + 1) + (j & 1) : j;
+  };
+  auto kv_row = [&](int j) -> int {
+    if (!p.part) return (int)(head * p.seq) + j * BKV;
+    const int kt = (int)__fns(kmask, 0, (j >> 1) + 1);
+    return (int)((((long long)p.kv_owner[kt] * p.bh + head) * p.kv_tiles + p.kv_local[kt]) * BQ) +
+           (j & 1) * BKV;
+  };
 
   if (warp == 4 || warp == 6) {
     // ---------------- TMA producers: warp 4 Q and K, warp 6 V ----------------
     if (lane == 0) {
       const bool is_k = warp == 4;
-      const int kv_row0 = (int)(head * p.seq);
       if (is_k) {
         tma_prefetch_desc(&tq);
         tma_prefetch_desc(&tk);
@@ -190,7 +221,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       const int stages = is_k ? KST : VST;
       const uint32_t ring = is_k ? sK : sV;
       for (int j = 0; j < n_kv && !*abort; ++j) {
-        const int kr = kv_row0 + j * BKV;
+        const int kr = kv_row(j);
         const int st = j % stages;
         if (j >= stages && !mbar_wait(smem_u32(&empty[st]), ((j / stages) - 1) & 1, abort)) break;
         const uint32_t fb = smem_u32(&full[st]);
@@ -237,7 +268,8 @@ __global__ void __launch_bounds__(THREADS, 2)
           const uint32_t pt = kk < BKV / 16 ? sP : sPl;
           const uint64_t ad = sdesc_sw128(pt + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(vb + (kk & 3) * 16 * 128, KV_HALF, 1024);
-          mma_f16(tmem + O_COL, ad, bd, idesc_pv, (j | kk) != 0);
+          // a partial call after the first adds onto the carried O
+          mma_f16(tmem + O_COL, ad, bd, idesc_pv, (j | kk) != 0 || !first);
         }
         mma_commit(smem_u32(&B.pv_done));
         mma_commit(smem_u32(&B.v_empty[vs]));
@@ -249,6 +281,26 @@ __global__ void __launch_bounds__(THREADS, 2)
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     const int qpos = q0 + tid;
     float m_used = -INFINITY, l_run = 0.f;
+    // carried state of a partial call ([128 columns][128 rows] f32, so a warp's
+    // 32 rows of one column are one 128-byte line)
+    const long long slot = head * p.n_qtiles + qi;
+    float* oacc = p.part ? p.o_acc + slot * (long long)(BQ * D) : nullptr;
+    float2* ml = p.part ? p.ml + slot * BQ : nullptr;
+    if (!first) {
+      const float2 st = ml[tid];
+      m_used = st.x;
+      l_run = st.y;
+      if (n_kv > 0) {
+        // O into TMEM before P_0 is handed over (the first PV adds onto it)
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          uint32_t r[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(oacc[(c + i) * BQ + tid]);
+          tmem_st32_wait(tmem + lane_base + O_COL + c, r);
+        }
+      }
+    }
     // waits are made warp-uniform: tcgen05.ld/st need the whole warp
     for (int j = 0; j < n_kv; ++j) {
       if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&B.s_full[j & 1]), (j >> 1) & 1, abort)))
@@ -261,7 +313,7 @@ __global__ void __launch_bounds__(THREADS, 2)
 #pragma unroll
         for (int i = 0; i < BKV; ++i) sv[i] = __uint_as_float(rs[i]);
       }
-      const int kpos0 = j * BKV;
+      const int kpos0 = kv_block(j) * BKV;
       const bool diag = p.causal && kpos0 + BKV - 1 > q0;
       if (diag) {
 #pragma unroll
@@ -310,12 +362,16 @@ __global__ void __launch_bounds__(THREADS, 2)
 #pragma unroll
         for (int i = 0; i < h; ++i) s8[i] += s8[i + h];
       l_run += s8[0];
-      // PV_{j-1} has read the P tile and finished adding into O
-      if (j >= 1) {
-        const bool ok = __all_sync(0xffffffffu,
-                                   mbar_wait(smem_u32(&B.pv_done), (j - 1) & 1, abort));
-        tc_fence_after();
-        if (!ok) break;
+      // PV_{j-1} has read the P tile and finished adding into O (at j = 0 of a
+      // call that carries state, O holds the carried values and may need the
+      // same rescale)
+      if (j >= 1 || !first) {
+        if (j >= 1) {
+          const bool ok = __all_sync(0xffffffffu,
+                                     mbar_wait(smem_u32(&B.pv_done), (j - 1) & 1, abort));
+          tc_fence_after();
+          if (!ok) break;
+        }
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
           for (int c = 0; c < D; c += 32) {
@@ -346,15 +402,37 @@ __global__ void __launch_bounds__(THREADS, 2)
       tc_fence_before();
       mbar_arrive(smem_u32(&B.p_full));
     }
-    const bool done = !*abort && mbar_wait(smem_u32(&B.pv_done), (n_kv - 1) & 1, abort);
-    if (__all_sync(0xffffffffu, done)) {
+    const bool done =
+        !*abort && (n_kv == 0 || mbar_wait(smem_u32(&B.pv_done), (n_kv - 1) & 1, abort));
+    // O of this CTA: from TMEM, or, with no key block in this call, the
+    // carried state (zero on a first call)
+    auto o_cols = [&](int c, uint32_t (&r)[32]) {
+      if (n_kv > 0) {
+        tmem_ld32_wait(tmem + lane_base + O_COL + c, r);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = first ? 0u : __float_as_uint(oacc[(c + i) * BQ + tid]);
+      }
+    };
+    if (__all_sync(0xffffffffu, done) && !last && (n_kv > 0 || first)) {
+      // carry the state to the next call
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t r[32];
+        o_cols(c, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) oacc[(c + i) * BQ + tid] = __uint_as_float(r[i]);
+      }
+      ml[tid] = make_float2(m_used, l_run);
+    } else if (__all_sync(0xffffffffu, done) && last) {
       tc_fence_after();
       const float inv = 1.f / l_run;
       __half* orow = p.o + (row0 + tid) * p.row_stride;
 #pragma unroll 1
       for (int c = 0; c < D; c += 32) {
         uint32_t r[32];
-        tmem_ld32_wait(tmem + lane_base + O_COL + c, r);
+        o_cols(c, r);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint4 v;
@@ -409,21 +487,10 @@ bool make_map(CUtensorMap* m, const void* base, long long rows, long long ld, in
 
 }  // namespace
 
-extern "C" int ktir_fmha_f16(const KtirFmhaDesc* d, void* stream) {
-  if (!d || !d->q || !d->k || !d->v || !d->o || !d->status) return KTIR_ERR_ARG;
-  // the row max is taken before scaling, which needs a positive scale
-  if (d->d != D || d->seq % BQ || d->bh < 1 || d->row_stride < D || (d->row_stride & 7) ||
-      !(d->scale > 0.f))
-    return KTIR_ERR_UNSUPPORTED;
-  if ((reinterpret_cast<uintptr_t>(d->q) | reinterpret_cast<uintptr_t>(d->k) |
-       reinterpret_cast<uintptr_t>(d->v) | reinterpret_cast<uintptr_t>(d->o)) & 15)
-    return KTIR_ERR_UNSUPPORTED;
-  const long long rows = d->bh * d->seq;
-  if (rows > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
-  CUtensorMap tq, tk, tv;
-  if (!make_map(&tq, d->q, rows, d->row_stride, BQ) || !make_map(&tk, d->k, rows, d->row_stride, BKV) ||
-      !make_map(&tv, d->v, rows, d->row_stride, BKV))
-    return KTIR_ERR_CUDA;
+namespace {
+
+int launch_fmha(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                const FmhaParams& p, cudaStream_t stream) {
   static bool attr = false;
   if (!attr) {
     // two CTAs per SM need the whole shared-memory carve-out
@@ -434,7 +501,30 @@ extern "C" int ktir_fmha_f16(const KtirFmhaDesc* d, void* stream) {
       return KTIR_ERR_CUDA;
     attr = true;
   }
-  FmhaParams p;
+  dim3 grid((unsigned)((long long)p.n_qtiles * p.bh));   // rows / 128 < 2^31
+  k_fmha_tcgen05<<<grid, THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  return cudaGetLastError() == cudaSuccess ? KTIR_OK : KTIR_ERR_CUDA;
+}
+
+bool aligned16(const void* a) { return (reinterpret_cast<uintptr_t>(a) & 15) == 0; }
+
+}  // namespace
+
+extern "C" int ktir_fmha_f16(const KtirFmhaDesc* d, void* stream) {
+  if (!d || !d->q || !d->k || !d->v || !d->o || !d->status) return KTIR_ERR_ARG;
+  // the row max is taken before scaling, which needs a positive scale
+  if (d->d != D || d->seq % BQ || d->bh < 1 || d->row_stride < D || (d->row_stride & 7) ||
+      !(d->scale > 0.f))
+    return KTIR_ERR_UNSUPPORTED;
+  if (!aligned16(d->q) || !aligned16(d->k) || !aligned16(d->v) || !aligned16(d->o))
+    return KTIR_ERR_UNSUPPORTED;
+  const long long rows = d->bh * d->seq;
+  if (rows > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
+  CUtensorMap tq, tk, tv;
+  if (!make_map(&tq, d->q, rows, d->row_stride, BQ) || !make_map(&tk, d->k, rows, d->row_stride, BKV) ||
+      !make_map(&tv, d->v, rows, d->row_stride, BKV))
+    return KTIR_ERR_CUDA;
+  FmhaParams p = {};
   p.o = static_cast<__half*>(d->o);
   p.seq = d->seq;
   p.row_stride = d->row_stride;
@@ -443,7 +533,55 @@ extern "C" int ktir_fmha_f16(const KtirFmhaDesc* d, void* stream) {
   p.n_qtiles = (int)(d->seq / BQ);
   p.bh = d->bh;
   p.status = d->status;
-  dim3 grid((unsigned)(p.n_qtiles * d->bh));   // rows / 128 < 2^31
-  k_fmha_tcgen05<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
-  return cudaGetLastError() == cudaSuccess ? KTIR_OK : KTIR_ERR_CUDA;
+  return launch_fmha(tq, tk, tv, p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ktir_fmha_f16_part(const KtirFmhaPartDesc* d, void* stream) {
+  if (!d || !d->q || !d->k || !d->v || !d->o || !d->status) return KTIR_ERR_ARG;
+  const bool first = d->flags & 1, last = d->flags & 2;
+  if ((!first || !last) && (!d->o_acc || !d->ml)) return KTIR_ERR_ARG;
+  if (d->d != D || d->seq % BQ || d->seq > MAX_TILES * BQ || d->bh < 1 || !(d->scale > 0.f))
+    return KTIR_ERR_UNSUPPORTED;
+  const int n_tiles = (int)(d->seq / BQ);
+  if (d->n_qtiles < 1 || d->n_qtiles > n_tiles || d->kv_tiles < 1 || d->kv_tiles > n_tiles)
+    return KTIR_ERR_UNSUPPORTED;
+  if (!aligned16(d->q) || !aligned16(d->k) || !aligned16(d->v) || !aligned16(d->o) ||
+      !aligned16(d->o_acc) || !aligned16(d->ml))
+    return KTIR_ERR_UNSUPPORTED;
+  const long long rows = d->bh * d->seq;
+  if (rows > 0x7fffffffLL || d->kv_rows < 1 || d->kv_rows > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
+  for (int i = 0; i < d->n_qtiles; ++i)
+    if (d->qtiles[i] >= n_tiles) return KTIR_ERR_UNSUPPORTED;
+  // every key tile the mask names must lie inside K / V
+  for (int kt = 0; kt < n_tiles; ++kt) {
+    if (!((d->key_mask >> kt) & 1u)) continue;
+    const long long end =
+        (((long long)d->kv_owner[kt] * d->bh + d->bh - 1) * d->kv_tiles + d->kv_local[kt] + 1) * BQ;
+    if (d->kv_local[kt] >= d->kv_tiles || end > d->kv_rows) return KTIR_ERR_UNSUPPORTED;
+  }
+  CUtensorMap tq, tk, tv;
+  if (!make_map(&tq, d->q, rows, D, BQ) || !make_map(&tk, d->k, d->kv_rows, D, BKV) ||
+      !make_map(&tv, d->v, d->kv_rows, D, BKV))
+    return KTIR_ERR_CUDA;
+  FmhaParams p = {};
+  p.o = static_cast<__half*>(d->o);
+  p.seq = d->seq;
+  p.row_stride = D;
+  p.scale_log2 = d->scale * 1.4426950408889634f;
+  p.causal = d->causal;
+  p.n_qtiles = d->n_qtiles;
+  p.bh = d->bh;
+  p.status = d->status;
+  p.part = 1;
+  p.flags = d->flags & 3;
+  p.kv_tiles = d->kv_tiles;
+  p.key_mask = d->key_mask;
+  p.o_acc = d->o_acc;
+  p.ml = reinterpret_cast<float2*>(d->ml);
+  for (int i = 0; i < MAX_TILES; ++i) {
+    p.qtiles[i] = d->qtiles[i];
+    p.kv_owner[i] = d->kv_owner[i];
+    p.kv_local[i] = d->kv_local[i];
+  }
+  return launch_fmha(tq, tk, tv, p, static_cast<cudaStream_t>(stream));
 }

@@ -46,6 +46,17 @@ int ktir_set_error(int code, const char* msg) { return set_err(code, msg); }
 
 extern "C" int ktir_version(void) { return 100; }
 extern "C" const char* ktir_last_error(void) { return g_err; }
+
+extern "C" int ktir_copy_blocks(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                                int64_t width, int64_t rows, void* stream) {
+  if (!dst || !src || width < 0 || rows < 0 || dst_pitch < width || src_pitch < width)
+    return set_err(KTIR_ERR_ARG, "ktir_copy_blocks: bad arguments");
+  if (width == 0 || rows == 0) return KTIR_OK;
+  cudaError_t e = cudaMemcpy2DAsync(dst, (size_t)dst_pitch, src, (size_t)src_pitch, (size_t)width,
+                                    (size_t)rows, cudaMemcpyDeviceToDevice, (cudaStream_t)stream);
+  if (e != cudaSuccess) return set_err(KTIR_ERR_CUDA, cudaGetErrorString(e));
+  return KTIR_OK;
+}
 extern "C" int ktir_device_count(int* count) {
   cudaError_t e = cudaGetDeviceCount(count);
   if (e != cudaSuccess) return set_err(KTIR_ERR_CUDA, cudaGetErrorString(e));
@@ -82,6 +93,40 @@ static inline int grid_x(int64_t work, int threads, int cap) {
   if (g < 1) g = 1;
   if (g > cap) g = cap;
   return (int)g;
+}
+
+// dst = a - b (sub != 0) or a + b, byte by byte modulo 256, four bytes per
+// SIMD op and sixteen per thread where all three pointers allow it
+__global__ void __launch_bounds__(256) k_bytes(uint8_t* __restrict__ dst, const uint8_t* __restrict__ a,
+                                               const uint8_t* __restrict__ b, int64_t n, int sub) {
+  const int64_t i0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 16;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 16;
+  const bool vec = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(a) |
+                     reinterpret_cast<uintptr_t>(b)) & 15) == 0;
+  for (int64_t i = i0; i < n; i += stride) {
+    if (vec && i + 16 <= n) {
+      const uint4 x = *reinterpret_cast<const uint4*>(a + i);
+      const uint4 y = *reinterpret_cast<const uint4*>(b + i);
+      uint4 z;
+      z.x = sub ? __vsub4(x.x, y.x) : __vadd4(x.x, y.x);
+      z.y = sub ? __vsub4(x.y, y.y) : __vadd4(x.y, y.y);
+      z.z = sub ? __vsub4(x.z, y.z) : __vadd4(x.z, y.z);
+      z.w = sub ? __vsub4(x.w, y.w) : __vadd4(x.w, y.w);
+      *reinterpret_cast<uint4*>(dst + i) = z;
+    } else {
+      for (int64_t k = i; k < n && k < i + 16; ++k)
+        dst[k] = (uint8_t)(sub ? a[k] - b[k] : a[k] + b[k]);
+    }
+  }
+}
+
+extern "C" int ktir_bytes_delta(void* dst, const void* a, const void* b, int64_t n, int32_t subtract,
+                                void* stream) {
+  if (!dst || !a || !b || n < 0) return set_err(KTIR_ERR_ARG, "ktir_bytes_delta: bad arguments");
+  if (n == 0) return KTIR_OK;
+  k_bytes<<<grid_x((n + 15) / 16, 256, 148 * 16), 256, 0, (cudaStream_t)stream>>>(
+      (uint8_t*)dst, (const uint8_t*)a, (const uint8_t*)b, n, subtract ? 1 : 0);
+  return check_launch("ktir_bytes_delta");
 }
 
 // ---------------------------------------------------------------------------

@@ -435,14 +435,26 @@ class KTIRInterpreter:
             pinned = [a.ctypes.data for _, a in staged]
             results = [a[:s_.size] for (_, a), s_ in zip(staged, src)]
         up = [i for i in range(n) if i not in skip and src[i].size]
-        xs = (R.KtirHostXfer * max(1, len(up)))()
-        for k, i in enumerate(up):
-            xs[k].host, xs[k].pinned = src[i].ctypes.data, pinned[i]
-            xs[k].device, xs[k].bytes = exe.dev_tensors[i].data_ptr(), src[i].size
-        R.check(lib.ktir_host_upload(xs, len(up), dev, sp), "ktir_host_upload")
+        # a split plan may read only parts of some tensors (its share of them)
+        ranges = exe.plan.info.get("upload_ranges", {}) if self._shard is not None else {}
+        xfer = []
+        for i in up:
+            for off, nb in ranges.get(i, [(0, src[i].size)]):
+                xfer.append((src[i].ctypes.data + off, pinned[i] + off,
+                             exe.dev_tensors[i].data_ptr() + off, nb))
+        xs = (R.KtirHostXfer * max(1, len(xfer)))()
+        for k, (h, p_, d_, nb) in enumerate(xfer):
+            xs[k].host, xs[k].pinned, xs[k].device, xs[k].bytes = h, p_, d_, nb
+        R.check(lib.ktir_host_upload(xs, len(xfer), dev, sp), "ktir_host_upload")
         if exe.plan.status_check:
             exe.status.zero_()
+        merge = self._shard is not None and self._shard[1] > 1
+        if merge:
+            back_all = [i for i in range(n) if (written is None or i in written) and src[i].size]
+            before = {i: exe.dev_tensors[i][:src[i].size].clone() for i in back_all}
         exe.launch(exe.dev_tensors, stream, exe.bufs)
+        if merge:
+            self._merge_shards(exe, before, sp)
         back = [i for i in range(n) if (written is None or i in written) and src[i].size]
         status = np.zeros(1, np.int32)
         ys = (R.KtirHostXfer * (len(back) + 1))()
@@ -454,9 +466,9 @@ class KTIRInterpreter:
             ys[n_y].host, ys[n_y].pinned = status.ctypes.data, exe.status_pinned.data_ptr()
             ys[n_y].device, ys[n_y].bytes = exe.status.data_ptr(), 4
             n_y += 1
-        # allocations neither written back nor already staged into their result
+        # allocations neither written back nor already staged whole into their result
         rest = [i for i in range(n) if i not in back and src[i].size
-                and (staged is None or i not in up)]
+                and (staged is None or i not in up or i in ranges)]
         cs = (R.KtirHostCopy * max(1, len(rest)))()
         for k, i in enumerate(rest):
             cs[k].dst, cs[k].src, cs[k].bytes = results[i].ctypes.data, src[i].ctypes.data, src[i].size
@@ -466,8 +478,30 @@ class KTIRInterpreter:
             fac, k = where[addr]
             fac.allocs[k] = results[i].view(arrays[i].dtype)
             fac.borrowed.add(k)
-        exe.last_h2d_bytes = sum(src[i].size for i in up)
+        exe.last_h2d_bytes = sum(x[3] for x in xfer)
         exe.last_d2h_bytes = sum(src[i].size for i in back)
+
+    def _merge_shards(self, exe: Executable, before, sp) -> None:
+        """Make every rank's tensors whole after a split call: each rank wrote
+        only its cores' elements, every other element still holds the uploaded
+        value (the same on every rank).  The byte differences from the upload,
+        summed over the ranks modulo 256 (NCCL all-reduce of uint8; at most one
+        rank changes a given byte), added back to the upload give every rank
+        the combined result, bit for bit."""
+        import torch.distributed as dist
+        lib = exe.lib
+        group = self._shard[2]
+        for i, orig in before.items():
+            cur = exe.dev_tensors[i][:orig.numel()]
+            delta = exe.torch.empty_like(orig)
+            R.check(lib.ktir_bytes_delta(C.c_void_p(delta.data_ptr()), C.c_void_p(cur.data_ptr()),
+                                         C.c_void_p(orig.data_ptr()), orig.numel(), 1, sp),
+                    "ktir_bytes_delta")
+            dist.all_reduce(delta, op=dist.ReduceOp.SUM, group=group)
+            R.check(lib.ktir_bytes_delta(C.c_void_p(cur.data_ptr()), C.c_void_p(orig.data_ptr()),
+                                         C.c_void_p(delta.data_ptr()), orig.numel(), 0, sp),
+                    "ktir_bytes_delta")
+
 
 
 class _PinnedPool:

@@ -362,6 +362,16 @@ class Plan:
     def kernel_launches(self) -> int:
         return sum(l.kernels for l in self.launches)
 
+    @property
+    def collective(self) -> bool:
+        """Whether a launch exchanges data with other ranks (NCCL calls, which
+        stay out of CUDA graphs)."""
+        return any(l.kind in COLLECTIVE_KINDS for l in self.launches)
+
+
+# launch kinds that are NCCL exchanges between ranks
+COLLECTIVE_KINDS = {"allreduce_counts", "kv_ring"}
+
 
 class DeviceData:
     """Owns the device-side copies of host index tables of a plan."""

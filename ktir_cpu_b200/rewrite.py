@@ -294,11 +294,13 @@ def _make_handler(info):
     return handler
 
 
-def match_attention_plan(low, stores):
-    """All stores are f16(acc / l) of attention nodes that tile a [bh*seq, d] problem."""
-    import ctypes as C
-    from . import runtime as R
-    from .lower import Launch, Plan
+def attention_problem(stores, seq_hint=None):
+    """The attention problem a list of stores computes, when every store is
+    f16(acc / l) of an attention node over one [bh*seq, d] Q/K/V/O set:
+    {q, k, v, o buffers, bq, d, causal, scale, seq, rows (query row of each
+    unit)}, else None.  A causal problem's sequence length is taken from its
+    last query block unless seq_hint gives it (a subset of the units, such as
+    one GPU's share of a split, need not contain the last block)."""
     from .trace import Node, RectTarget
     if not stores:
         return None
@@ -339,6 +341,7 @@ def match_attention_plan(low, stores):
     # infer seq from the causal offsets (last q block) or from the K sweep length
     seen = set()
     seq = None
+    last_end = 0
     for attn, t in units:
         q = attn.ins[0]
         if attn.attrs["scale"] != scale or (attn.attrs["causal_offsets"] is not None) != causal:
@@ -365,19 +368,44 @@ def match_attention_plan(low, stores):
                 return None
             if qrow - qoff != krow0 or len(ks) * bk != qoff + bq:
                 return None
-            seq = max(seq or 0, qoff + bq)
+            last_end = max(last_end, qoff + bq)
+            seq = seq_hint if seq_hint is not None else max(seq or 0, qoff + bq)
         else:
             seq_u = len(ks) * bk
             if seq is not None and seq != seq_u:
                 return None
             seq = seq_u
         seen.add(qrow)
-    if seq is None or seq % 128 or rows % seq or not scale > 0:
+    if seq is None or seq % 128 or rows % seq or not scale > 0 or last_end > seq:
         return None
+    return {"q": qbuf, "k": kbuf, "v": vbuf, "o": obuf, "bq": bq, "d": d, "causal": causal,
+            "scale": scale, "seq": seq, "n_rows": rows, "rows": seen}
+
+
+def match_attention_plan(low, stores):
+    """All stores are f16(acc / l) of attention nodes that tile a [bh*seq, d]
+    problem: whole heads (one GPU, or a split whose cores own whole heads) run
+    the fused kernel over those heads; a split whose cores own stretches of
+    every head's sequence runs the K/V ring across the GPUs."""
+    import ctypes as C
+    from . import runtime as R
+    from .lower import Launch, Plan
+    hint = None
+    if low.shard is not None:
+        whole = attention_problem(low.all_stores)
+        hint = whole["seq"] if whole is not None else None
+    prob = attention_problem(stores, hint)
+    if prob is None:
+        return None
+    qbuf, kbuf, vbuf, obuf = prob["q"], prob["k"], prob["v"], prob["o"]
+    bq, d, causal, scale, seq, seen = (prob[k] for k in ("bq", "d", "causal", "scale", "seq", "rows"))
     # the units must cover whole heads [h_lo, h_hi) (all heads, or a shard's)
     heads = sorted({q // seq for q in seen})
     h_lo, h_hi = heads[0], heads[-1] + 1
     if len(seen) * bq != (h_hi - h_lo) * seq or heads != list(range(h_lo, h_hi)):
+        if low.shard is not None:
+            from .ring import ring_attention_plan
+            return ring_attention_plan(low, prob)
         return None
     bh = h_hi - h_lo
     off = h_lo * seq * d * 2

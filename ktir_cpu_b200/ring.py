@@ -1,0 +1,195 @@
+"""Attention split over the sequence across GPUs, K/V blocks passed in a ring.
+
+A KTIR attention program whose cores own stretches of every head's sequence
+(the benchmark's zigzag layout: query blocks b and nq-1-b of every head on
+one core) is split across GPUs by contiguous core ranges.  Each GPU then
+owns some 128-row query tiles of every head, and needs the K/V rows of every
+earlier tile, most of which belong to other GPUs' query tiles.  The K/V rows
+of a GPU's own tiles ("its share") are packed into one contiguous block of a
+staging buffer that holds every GPU's share one after the other; in step t
+each GPU adds the key tiles of share (rank - t) mod world to its queries
+(the partial attention entry point, ktir_fmha_f16_part, carrying the
+online-softmax state between steps), while NCCL sends that share on to the
+next GPU and receives share (rank - t - 1) mod world from the previous one.
+After world steps every GPU has added every key tile and writes its query
+tiles of O.  The reference has no multi-device execution: its cores read
+K/V from one simulated HBM (ktir_cpu/ops/memory_ops.py:438-587); the ring is
+how the same reads reach a GPU that does not hold them.
+
+The pure functions here (tile ownership, staging layout, step masks) are
+the host logic, tested on CPU; ring_attention_plan builds the device plan.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, List, Optional, Sequence, Tuple
+
+TILE = 128
+
+
+def query_tiles(rows: Sequence[int], seq: int, bq: int) -> Optional[List[int]]:
+    """The 128-row query tiles that a set of query-block row offsets covers,
+    when every head covers the same tiles and every covered tile is whole;
+    else None."""
+    per_tile = TILE // bq if TILE % bq == 0 else 0
+    if per_tile == 0:
+        return None
+    heads: Dict[int, Dict[int, int]] = {}
+    for r in rows:
+        h, off = divmod(r, seq)
+        t = off // TILE
+        heads.setdefault(h, {})
+        heads[h][t] = heads[h].get(t, 0) + 1
+    if not heads:
+        return None
+    sets = {tuple(sorted(d)) for d in heads.values()}
+    if len(sets) != 1:
+        return None
+    if any(c != per_tile for d in heads.values() for c in d.values()):
+        return None
+    return list(next(iter(sets)))
+
+
+def staging_layout(tiles_of: Sequence[Sequence[int]], n_tiles: int):
+    """(kv_owner, kv_local, kv_tiles) for the staging buffer: key tile kt of a
+    head lives in share kv_owner[kt] at local index kv_local[kt]; every share
+    is kv_tiles tiles per head.  The shares must partition the tiles."""
+    owner = [-1] * n_tiles
+    local = [0] * n_tiles
+    for s, tiles in enumerate(tiles_of):
+        for i, t in enumerate(sorted(tiles)):
+            if not 0 <= t < n_tiles or owner[t] != -1:
+                raise ValueError(f"query tile {t} owned twice or out of range")
+            owner[t], local[t] = s, i
+    if -1 in owner:
+        raise ValueError("the shares do not cover every query tile")
+    return owner, local, max(len(t) for t in tiles_of)
+
+
+def step_shares(rank: int, world: int) -> List[int]:
+    """The share whose key tiles each step adds: share (rank - t) mod world at step t."""
+    return [(rank - t) % world for t in range(world)]
+
+
+def share_mask(tiles: Sequence[int]) -> int:
+    m = 0
+    for t in tiles:
+        m |= 1 << t
+    return m
+
+
+def ring_attention_plan(low, prob):
+    """Device plan for one rank of the ring (see the module docstring)."""
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    from . import runtime as R
+    from .lower import Launch, Plan, core_range
+    from .rewrite import attention_problem
+
+    rank, world, group = low.shard
+    seq, bq, d = prob["seq"], prob["bq"], prob["d"]
+    if d != 128 or seq % TILE or seq > 32 * TILE or not prob["causal"]:
+        return None
+    n_tiles = seq // TILE
+    bh = prob["n_rows"] // seq
+    nx, ny, nz = low.trace.grid
+    tiles_of = []
+    for r in range(world):
+        c0, c1 = core_range(r, world, nx * ny * nz)
+        pr = attention_problem([s for s in low.all_stores if c0 <= s.core < c1], seq)
+        if pr is None or pr["q"] is not prob["q"] or pr["k"] is not prob["k"]:
+            return None
+        tl = query_tiles(pr["rows"], seq, bq)
+        if tl is None:
+            return None
+        tiles_of.append(tl)
+    try:
+        owner, local, kv_tiles = staging_layout(tiles_of, n_tiles)
+    except ValueError:
+        return None
+    mine = tiles_of[rank]
+    dev = low.device
+    share_elems = bh * kv_tiles * TILE * d
+    k_sh = torch.empty(world * share_elems, dtype=torch.float16, device=dev)
+    v_sh = torch.empty(world * share_elems, dtype=torch.float16, device=dev)
+    o_acc = torch.empty(bh * len(mine) * TILE * d, dtype=torch.float32, device=dev)
+    ml = torch.empty(bh * len(mine) * TILE * 2, dtype=torch.float32, device=dev)
+    lib = R.load_library()
+    sq, sk, sv, so = (low.slots[b.index] for b in (prob["q"], prob["k"], prob["v"], prob["o"]))
+    row_bytes = d * 2
+    comm = torch.cuda.Stream(dev) if dev.type == "cuda" else None
+    descs = []
+    for t, s in enumerate(step_shares(rank, world)):
+        dsc = R.KtirFmhaPartDesc()
+        dsc.bh, dsc.seq, dsc.d = bh, seq, d
+        dsc.kv_rows = world * bh * kv_tiles * TILE
+        dsc.scale, dsc.causal = prob["scale"], 1
+        dsc.n_qtiles, dsc.kv_tiles = len(mine), kv_tiles
+        dsc.key_mask = share_mask(tiles_of[s])
+        dsc.flags = (1 if t == 0 else 0) | (2 if t == world - 1 else 0)
+        dsc.o_acc, dsc.ml = o_acc.data_ptr(), ml.data_ptr()
+        for i, qt in enumerate(mine):
+            dsc.qtiles[i] = qt
+        for kt in range(n_tiles):
+            dsc.kv_owner[kt], dsc.kv_local[kt] = owner[kt], local[kt]
+        dsc.k, dsc.v = k_sh.data_ptr(), v_sh.data_ptr()
+        descs.append(dsc)
+    nxt, prv = (rank + 1) % world, (rank - 1) % world
+    if group is not None:
+        nxt, prv = dist.get_global_rank(group, nxt), dist.get_global_rank(group, prv)
+
+    def share(buf, s):
+        return buf[s * share_elems:(s + 1) * share_elems]
+
+    def run(bufs, stream, status):
+        compute = (torch.cuda.ExternalStream(stream.value, device=dev) if stream.value
+                   else torch.cuda.default_stream(dev))
+        # this rank's share: K / V rows of its query tiles, every head
+        for i, qt in enumerate(mine):
+            for src_slot, dst in ((sk, k_sh), (sv, v_sh)):
+                R.check(lib.ktir_copy_blocks(
+                    C.c_void_p(dst.data_ptr() + ((rank * bh * kv_tiles + i) * TILE) * row_bytes),
+                    C.c_int64(kv_tiles * TILE * row_bytes),
+                    C.c_void_p(bufs.base[src_slot] + qt * TILE * row_bytes),
+                    C.c_int64(seq * row_bytes), C.c_int64(TILE * row_bytes), C.c_int64(bh),
+                    stream), "ktir_copy_blocks")
+        # the comm stream starts after this execution's packing and after the
+        # previous execution's kernels (which read the shares it overwrites)
+        comm.wait_stream(compute)
+        shares = step_shares(rank, world)
+        arrived = None
+        for t, s in enumerate(shares):
+            if arrived is not None:
+                compute.wait_event(arrived)
+            dsc = descs[t]
+            dsc.q, dsc.o = bufs.base[sq], bufs.base[so]
+            dsc.status = status
+            R.check(lib.ktir_fmha_f16_part(C.byref(dsc), stream), "ktir_fmha_f16_part")
+            if t < world - 1:
+                with torch.cuda.stream(comm):
+                    ops = [dist.P2POp(dist.isend, share(k_sh, s), nxt, group),
+                           dist.P2POp(dist.isend, share(v_sh, s), nxt, group),
+                           dist.P2POp(dist.irecv, share(k_sh, shares[t + 1]), prv, group),
+                           dist.P2POp(dist.irecv, share(v_sh, shares[t + 1]), prv, group)]
+                    for w in dist.batch_isend_irecv(ops):
+                        w.wait()
+                    arrived = torch.cuda.Event()
+                    arrived.record(comm)
+
+    plan = Plan("attention", [Launch(run, "kv_ring", world)], [], status_check=True)
+    plan.scratch.update(k_sh=k_sh, v_sh=v_sh, o_acc=o_acc, ml=ml, comm=comm)
+    flops = 4 * bh * seq * seq * d // 2
+    plan.info.update(bh=bh, seq=seq, d=d, causal=True, scale=prob["scale"], flops=flops,
+                     ring=dict(tiles=tiles_of, kv_tiles=kv_tiles,
+                               bytes_per_step=2 * share_elems * 2))
+    # this rank reads only its own query tiles and K/V share from the call's
+    # tensors (the rest arrives over NVLink): (buffer index, byte ranges)
+    ranges = []
+    for qt in mine:
+        for h in range(bh):
+            ranges.append(((h * seq + qt * TILE) * row_bytes, TILE * row_bytes))
+    plan.info["upload_ranges"] = {b.index: ranges for b in (prob["q"], prob["k"], prob["v"])}
+    return plan

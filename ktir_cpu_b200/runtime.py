@@ -113,6 +113,16 @@ class KtirFmhaDesc(C.Structure):
                 ("causal", C.c_int32), ("row_stride", C.c_int64), ("status", C.c_void_p)]
 
 
+class KtirFmhaPartDesc(C.Structure):
+    _fields_ = [("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("o", C.c_void_p),
+                ("bh", C.c_int64), ("seq", C.c_int64), ("d", C.c_int64), ("kv_rows", C.c_int64),
+                ("scale", C.c_float), ("causal", C.c_int32), ("n_qtiles", C.c_int32),
+                ("kv_tiles", C.c_int32), ("key_mask", C.c_uint32), ("flags", C.c_int32),
+                ("o_acc", C.c_void_p), ("ml", C.c_void_p), ("status", C.c_void_p),
+                ("qtiles", C.c_uint8 * 32), ("kv_owner", C.c_uint8 * 32),
+                ("kv_local", C.c_uint8 * 32)]
+
+
 class KtirHostXfer(C.Structure):
     _fields_ = [("host", C.c_void_p), ("pinned", C.c_void_p), ("device", C.c_void_p),
                 ("bytes", C.c_int64)]
@@ -125,7 +135,7 @@ class KtirHostCopy(C.Structure):
 EXPORTS = ["ktir_version", "ktir_last_error", "ktir_device_count", "ktir_ew",
            "ktir_softmax_rows", "ktir_gather_rmw", "ktir_reduce", "ktir_matmul",
            "ktir_offsets", "ktir_indirect", "ktir_gemm_f16", "ktir_fmha_f16",
-           "ktir_wait_selftest", "ktir_host_threads", "ktir_host_upload", "ktir_host_download"]
+           "ktir_fmha_f16_part", "ktir_copy_blocks", "ktir_bytes_delta", "ktir_wait_selftest", "ktir_host_threads", "ktir_host_upload", "ktir_host_download"]
 
 _LIB: Optional[C.CDLL] = None
 
@@ -162,6 +172,9 @@ def load_library(build_if_missing: bool = False) -> C.CDLL:
                                   vp, vp, vp]
     lib.ktir_gemm_f16.argtypes = [C.POINTER(KtirGemmDesc), vp]
     lib.ktir_fmha_f16.argtypes = [C.POINTER(KtirFmhaDesc), vp]
+    lib.ktir_fmha_f16_part.argtypes = [C.POINTER(KtirFmhaPartDesc), vp]
+    lib.ktir_copy_blocks.argtypes = [vp, C.c_int64, vp, C.c_int64, C.c_int64, C.c_int64, vp]
+    lib.ktir_bytes_delta.argtypes = [vp, vp, vp, C.c_int64, C.c_int32, vp]
     lib.ktir_wait_selftest.argtypes = [vp, C.c_uint32, vp]
     lib.ktir_host_threads.argtypes = []
     lib.ktir_host_upload.argtypes = [C.POINTER(KtirHostXfer), C.c_int, C.c_int, vp]

@@ -215,11 +215,18 @@ def gather_add(rows: int = 1048576, cols: int = 128, n_idx: int = 262144, grid: 
 
 
 def attention(batch: int = 4, heads: int = 32, seq: int = 2048, dim: int = 128, grid: int = 32,
-              bq: int = 64, bk: int = 64) -> str:
-    """Causal attention; Q/K/V/O are [batch*heads*seq, dim] row-major views."""
+              bq: int = 64, bk: int = 64, layout: str = "zigzag") -> str:
+    """Causal attention; Q/K/V/O are [batch*heads*seq, dim] row-major views.
+
+    layout "heads": core c owns heads [c*bh/grid, (c+1)*bh/grid), all query blocks.
+    layout "zigzag": the query blocks of every head pair up as (b, nq-1-b), whose
+    causal work sums to the same nq+1 key blocks; the pairs are dealt to the
+    cores in order (with more cores than pairs, the heads of a pair are split
+    between consecutive cores), so any contiguous range of cores owns the same
+    amount of work and stretches of the sequence from both ends, and reads the
+    K/V blocks of query blocks other cores own."""
     bh = batch * heads
-    assert bh % grid == 0 and seq % bq == 0 and bq == bk
-    per = bh // grid
+    assert seq % bq == 0 and bq == bk
     rows = bh * seq
     nq = seq // bq
     qt, kt, st = f"{bq}x{dim}", f"{bk}x{dim}", f"{bq}x{bk}"
@@ -228,24 +235,62 @@ def attention(batch: int = 4, heads: int = 32, seq: int = 2048, dim: int = 128, 
               "affine_map<(d0, d1) -> (d0, d1)>]")
     vecmap = ("[affine_map<(d0) -> (d0)>, affine_map<(d0) -> (d0)>, "
               "affine_map<(d0) -> (d0)>]")
-    return f"""module {{
+    if layout == "heads":
+        assert bh % grid == 0
+        bounds = (f"    %per = arith.constant {bh // grid} : index\n"
+                  "    %h0 = arith.muli %core, %per : index\n"
+                  "    %h1 = arith.addi %h0, %per : index\n")
+        loops = ("    scf.for %h = %h0 to %h1 step %c1 {\n"
+                 "      %hbase = arith.muli %h, %seq : index\n"
+                 "      scf.for %qb = %c0 to %nq step %c1 {\n")
+        close = "        scf.yield\n      }\n      scf.yield\n    }\n"
+    elif layout == "zigzag":
+        assert nq % 2 == 0
+        npairs = nq // 2
+        if grid >= npairs:
+            assert grid % npairs == 0 and bh % (grid // npairs) == 0
+            split = grid // npairs
+            bounds = (f"    %split = arith.constant {split} : index\n"
+                      f"    %hper = arith.constant {bh // split} : index\n"
+                      "    %p0 = arith.divsi %core, %split : index\n"
+                      "    %p1 = arith.addi %p0, %c1 : index\n"
+                      "    %hpart = arith.remsi %core, %split : index\n"
+                      "    %h0 = arith.muli %hpart, %hper : index\n"
+                      "    %h1 = arith.addi %h0, %hper : index\n")
+        else:
+            assert npairs % grid == 0
+            bounds = (f"    %pper = arith.constant {npairs // grid} : index\n"
+                      "    %p0 = arith.muli %core, %pper : index\n"
+                      "    %p1 = arith.addi %p0, %pper : index\n"
+                      "    %h0 = arith.constant 0 : index\n"
+                      f"    %h1 = arith.constant {bh} : index\n")
+        bounds += ("    %c2 = arith.constant 2 : index\n"
+                   f"    %nqm1 = arith.constant {nq - 1} : index\n")
+        loops = ("    scf.for %h = %h0 to %h1 step %c1 {\n"
+                 "      %hbase = arith.muli %h, %seq : index\n"
+                 "      scf.for %pp = %p0 to %p1 step %c1 {\n"
+                 "        %pp2 = arith.muli %pp, %c2 : index\n"
+                 "        %span = arith.subi %nqm1, %pp2 : index\n"
+                 "        scf.for %side = %c0 to %c2 step %c1 {\n"
+                 "        %jump = arith.muli %side, %span : index\n"
+                 "        %qb = arith.addi %pp, %jump : index\n")
+        close = ("        scf.yield\n      }\n        scf.yield\n      }\n"
+                 "      scf.yield\n    }\n")
+    else:
+        raise ValueError(f"attention layout {layout!r}")
+    head = f"""module {{
   func.func @causal_attention(%q_ptr: index, %k_ptr: index, %v_ptr: index, %o_ptr: index) attributes {{grid = [{grid}]}} {{
     %core = ktdp.get_compute_tile_id : index
     %c0 = arith.constant 0 : index
     %c1 = arith.constant 1 : index
-    %per = arith.constant {per} : index
     %seq = arith.constant {seq} : index
     %nq = arith.constant {nq} : index
     %bq = arith.constant {bq} : index
-    %h0 = arith.muli %core, %per : index
-    %h1 = arith.addi %h0, %per : index
     %scale = arith.constant {sc!r} : f32
     %ninf = arith.constant 0xFF800000 : f32
 {_view('%qv', '%q_ptr', (rows, dim), 'f16')}{_view('%kv', '%k_ptr', (rows, dim), 'f16')}{_view('%vv', '%v_ptr', (rows, dim), 'f16')}{_view('%ov', '%o_ptr', (rows, dim), 'f16')}
-    scf.for %h = %h0 to %h1 step %c1 {{
-      %hbase = arith.muli %h, %seq : index
-      scf.for %qb = %c0 to %nq step %c1 {{
-        %qoff = arith.muli %qb, %bq : index
+"""
+    body = f"""        %qoff = arith.muli %qb, %bq : index
         %qrow = arith.addi %hbase, %qoff : index
         {_tile('%qt', '%qv', ['%qrow', '%c0'], (rows, dim), 'f16', (bq, dim))}
         %q16 = ktdp.load %qt : !ktdp.access_tile<{qt}xindex> -> tensor<{qt}xf16>
@@ -321,14 +366,8 @@ def attention(batch: int = 4, heads: int = 32, seq: int = 2048, dim: int = 128, 
         %o16 = arith.truncf %on : tensor<{qt}xf32> to tensor<{qt}xf16>
         {_tile('%otile', '%ov', ['%qrow', '%c0'], (rows, dim), 'f16', (bq, dim))}
         ktdp.store %o16, %otile : tensor<{qt}xf16>, !ktdp.access_tile<{qt}xindex>
-        scf.yield
-      }}
-      scf.yield
-    }}
-    return
-  }}
-}}
 """
+    return head + bounds + loops + body + close + "    return\n  }\n}\n"
 
 
 # ---------------------------------------------------------------------------

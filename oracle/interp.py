@@ -306,6 +306,12 @@ class OracleInterpreter:
         self.hbm: Optional[HBM] = None
         self.grid: Tuple[int, int, int] = (1, 1, 1)
         self.core_limit: Optional[int] = None   # run only the first k cores (bounded CPU samples)
+        # run only the first k iterations of each core's outermost scf.for
+        # (bounded CPU samples); loop_fraction records the share of that
+        # loop's iterations that ran
+        self.loop_limit: Optional[int] = None
+        self.loop_fraction = 1.0
+        self._for_depth = 0
 
     def load(self, src: str) -> None:
         p = KTIRParser()
@@ -1078,7 +1084,18 @@ class OracleInterpreter:
                 core.track(name, v.nbytes())
         body = op.regions[0]
         iv = op.attributes["iter_var"]
-        for i in range(lb, ub, max(st, 1)):
+        its = range(lb, ub, max(st, 1))
+        if self.loop_limit is not None and self._for_depth == 0 and len(its) > self.loop_limit:
+            self.loop_fraction = self.loop_limit / len(its)
+            its = its[:self.loop_limit]
+        self._for_depth += 1
+        try:
+            return self._for_iterations(core, op, its, body, iv, names, cur)
+        finally:
+            self._for_depth -= 1
+
+    def _for_iterations(self, core, op, its, body, iv, names, cur):
+        for i in its:
             core.push()
             core.set(iv, i)
             r = self.run_region(core, body)

@@ -14,7 +14,8 @@ HEADER = os.path.join(ROOT, "include", "ktir_b200.h")
 
 STRUCTS = ["KtirBuffers", "KtirView", "KtirInstr", "KtirEwProgram", "KtirSoftmaxDesc",
            "KtirGatherRmwDesc", "KtirReduceDesc", "KtirMatmulDesc", "KtirOffsetsDesc",
-           "KtirIndirectDesc", "KtirGemmDesc", "KtirFmhaDesc", "KtirHostXfer", "KtirHostCopy"]
+           "KtirIndirectDesc", "KtirGemmDesc", "KtirFmhaDesc", "KtirFmhaPartDesc", "KtirHostXfer",
+           "KtirHostCopy"]
 
 
 def declared_functions():

@@ -83,3 +83,60 @@ def test_fmha_no_corrupted_rows_across_shapes_and_seeds():
             assert not torch.isnan(o).any().item(), (seed, bh, seq, causal)
             _check(f"seed {seed} bh{bh} s{seq} causal={causal}", o, q, k, v, bh, seq, scale,
                    causal)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fmha_partial_steps_of_the_ring(world):
+    """The steps one GPU of the K/V ring runs (ktir_fmha_f16_part), emulated for
+    every rank on one GPU: each rank's query tiles take the key tiles share by
+    share in its ring order, the softmax state carried between steps; the
+    query tiles of all ranks together must equal whole attention."""
+    import torch
+    from ktir_cpu_b200 import runtime as R
+    from ktir_cpu_b200.ring import share_mask, staging_layout, step_shares
+    lib = R.load_library()
+    bh, seq, d = 3, 2048, 128
+    n_tiles = seq // 128
+    pairs = [(t, n_tiles - 1 - t) for t in range(n_tiles // 2)]
+    per = len(pairs) // world
+    tiles_of = [sorted(x for pr in pairs[r * per:(r + 1) * per] for x in pr) for r in range(world)]
+    owner, local, kv_tiles = staging_layout(tiles_of, n_tiles)
+    g = torch.Generator(device="cpu").manual_seed(world)
+    q, k, v = (torch.randn(bh * seq, d, generator=g).half().cuda() for _ in range(3))
+    scale = float(1.0 / math.sqrt(128))
+    # the staging buffers: share s holds the K / V rows of rank s's tiles, every head
+    share = bh * kv_tiles * 128
+    k_sh = torch.zeros(world * share, d, dtype=torch.float16, device="cuda")
+    v_sh = torch.zeros_like(k_sh)
+    for s, tl in enumerate(tiles_of):
+        for i, t in enumerate(tl):
+            for h in range(bh):
+                dst = slice(((s * bh + h) * kv_tiles + i) * 128, ((s * bh + h) * kv_tiles + i + 1) * 128)
+                src = slice(h * seq + t * 128, h * seq + (t + 1) * 128)
+                k_sh[dst] = k[src]
+                v_sh[dst] = v[src]
+    o = torch.full((bh * seq, d), float("nan"), dtype=torch.float16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for rank in range(world):
+        mine = tiles_of[rank]
+        o_acc = torch.full((bh * len(mine) * 128 * d,), float("nan"), device="cuda")
+        ml = torch.full((bh * len(mine) * 128 * 2,), float("nan"), device="cuda")
+        for t, s in enumerate(step_shares(rank, world)):
+            dsc = R.KtirFmhaPartDesc()
+            dsc.q, dsc.k, dsc.v, dsc.o = q.data_ptr(), k_sh.data_ptr(), v_sh.data_ptr(), o.data_ptr()
+            dsc.bh, dsc.seq, dsc.d, dsc.kv_rows = bh, seq, d, world * share
+            dsc.scale, dsc.causal = scale, 1
+            dsc.n_qtiles, dsc.kv_tiles = len(mine), kv_tiles
+            dsc.key_mask = share_mask(tiles_of[s])
+            dsc.flags = (1 if t == 0 else 0) | (2 if t == world - 1 else 0)
+            dsc.o_acc, dsc.ml, dsc.status = o_acc.data_ptr(), ml.data_ptr(), status.data_ptr()
+            for i, qt in enumerate(mine):
+                dsc.qtiles[i] = qt
+            for kt in range(n_tiles):
+                dsc.kv_owner[kt], dsc.kv_local[kt] = owner[kt], local[kt]
+            R.check(lib.ktir_fmha_f16_part(C.byref(dsc), stream), "ktir_fmha_f16_part")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert not torch.isnan(o).any().item()
+    _check(f"ring emulated over {world} GPUs", o, q, k, v, bh, seq, scale, True)

@@ -1,8 +1,10 @@
 """One call's core grid split across two GPUs (one process per GPU, NCCL),
-against the oracle.  Each rank returns the tensors as its shard left them;
-the shards write disjoint elements, so merging the elements each rank
-changed must give the single-GPU (oracle) result.  Skipped with fewer than
-two GPUs."""
+against the oracle.  Each rank executes its contiguous range of cores and
+the ranks combine their writes, so every rank returns the whole result,
+which must equal the single-GPU (oracle) result.  The attention cases cover
+cores that own whole heads (no exchange) and cores that own zigzag stretches
+of every head's sequence (K/V passed between the GPUs in a ring).  Skipped
+with fewer than two GPUs."""
 
 import os
 import socket
@@ -11,7 +13,7 @@ from datetime import timedelta
 import numpy as np
 import pytest
 
-from golden_util import assert_matches
+from golden_util import assert_contraction, assert_matches, contraction_mag
 from ktir_cpu_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
@@ -19,7 +21,9 @@ pytestmark = pytest.mark.gpu
 CASES = [("softmax", dict(rows=256, cols=1024, grid=8, chunk=32), 1e-2),
          ("gather_add", dict(rows=4096, cols=128, n_idx=16384, grid=8, chunk=1024), None),
          ("gemm", dict(m=512, n=512, k=512, grid=(4, 2)), 1e-2),
+         ("attention", dict(batch=1, heads=4, seq=512, dim=128, grid=4, layout="heads"), 1e-2),
          ("attention", dict(batch=1, heads=4, seq=512, dim=128, grid=4), 1e-2)]
+IDS = ["softmax", "gather_add", "gemm", "attention_heads", "attention_ring"]
 
 
 def _free_port():
@@ -45,13 +49,14 @@ def _worker(rank, world, port, name, p, q):
         kw = W.inputs(name, seed=3, **p)
         out = interp.execute_function(W.FUNC[name], **{k: v.copy() for k, v in kw.items()})
         torch.cuda.synchronize(dev)
-        q.put((rank, interp.last_executable.plan.kind, out))
+        plan = interp.last_executable.plan
+        q.put((rank, plan.kind, [l.kind for l in plan.launches], out))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name,p,tol", CASES, ids=[c[0] for c in CASES])
+@pytest.mark.parametrize("name,p,tol", CASES, ids=IDS)
 def test_two_gpu_shards_merge_to_oracle(name, p, tol):
     import torch
     import torch.multiprocessing as mp
@@ -76,13 +81,14 @@ def test_two_gpu_shards_merge_to_oracle(name, p, tol):
     ora = OracleInterpreter()
     ora.load(W.source(name, **p))
     want = ora.execute_function(W.FUNC[name], **{k: v.copy() for k, v in kw.items()})
-    kinds = {kind for _, kind, _ in got}
+    kinds = {kind for _, kind, _, _ in got}
     assert len(kinds) == 1 and kinds != {"generic"}, kinds
-    for k, w in want.items():
-        merged = kw[k].copy()
-        base = kw[k].view(np.uint8).reshape(kw[k].size, -1)
-        for _, _, out in got:
-            o = out[k]
-            changed = np.any(o.view(np.uint8).reshape(o.size, -1) != base, axis=1).reshape(o.shape)
-            merged[changed] = o[changed]
-        assert_matches(f"{name}:{k}", merged, w, tol)
+    if name == "attention" and "layout" not in p:
+        assert all(launches == ["kv_ring"] for _, _, launches, _ in got)
+    mags = contraction_mag(f"{name}_seq{p.get('seq', 0)}", kw) or {}
+    for rank, _, _, out in got:
+        for k, w in want.items():
+            if k in mags:
+                assert_contraction(f"rank {rank} {name}:{k}", out[k], w, mags[k], tol)
+            else:
+                assert_matches(f"rank {rank} {name}:{k}", out[k], w, tol)
