@@ -179,3 +179,42 @@ def contraction_mag(name, inputs):
         sabs = np.einsum("hqd,hkd->hqk", np.abs(q), np.abs(k)) * scale
         return {"o_ptr": np.einsum("hqk,hkd->hqd", pr * (1 + sabs), np.abs(v)).reshape(-1, d)}
     return None
+
+
+EXAMPLE_DIR = os.path.join(GOLDEN_DIR, "examples")
+
+
+def example_names():
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(EXAMPLE_DIR, "*.npz")))
+
+
+def load_example(name):
+    """A recorded reference example: its source, function, regenerated inputs
+    (and memory seeds), and the reference's outputs, digests or exception."""
+    import json
+    import sys
+    if GOLDEN_DIR not in sys.path:
+        sys.path.insert(0, GOLDEN_DIR)
+    import examples as E
+    ex = E.BY_NAME[name]
+    z = np.load(os.path.join(EXAMPLE_DIR, name + ".npz"), allow_pickle=False)
+    tol = float(z["tol"])
+    return {"src": str(z["src"]), "func": str(z["func"]), "inputs": E.inputs(ex),
+            "seed": E.seeds(ex), "reads": ex["reads"], "tol": None if tol < 0 else tol,
+            "error": str(z["error"]),
+            "outputs": {k[5:]: z[k] for k in z.files if k.startswith("out__")},
+            "digests": {k[8:]: json.loads(str(z[k])) for k in z.files if k.startswith("digest__")}}
+
+
+def digest_of(a):
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def example_mag(name, inputs):
+    """sum |a b| per output for the examples whose outputs are matmul results."""
+    if "matmul" in name:
+        a = np.abs(inputs["a_ptr"].astype(np.float64))
+        b = np.abs(inputs["b_ptr"].astype(np.float64))
+        return {"c_ptr": a @ b}
+    return {}

@@ -1,0 +1,48 @@
+"""The reference's own example kernels on the B200, against the reference's
+recorded results (tests/golden/examples): outputs bit-exact or within the
+example's tolerance; outputs recorded as digests against the oracle run here
+(test_oracle_examples.py pins the oracle to those digests); matmul outputs
+under the contraction rule (golden_util.assert_contraction); the reference's
+exception where it raised one.  Examples that address memory through
+constants are seeded at those addresses through _prepare_execution, as the
+reference's own tests do."""
+
+import numpy as np
+import pytest
+
+from golden_util import (assert_contraction, assert_matches, example_mag, example_names,
+                         load_example, run_seeded)
+from oracle.interp import OracleInterpreter
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", example_names())
+def test_b200_runs_reference_example(name):
+    from ktir_cpu_b200 import KTIRInterpreter
+    g = load_example(name)
+    interp = KTIRInterpreter()
+    interp.load(g["src"])
+    kw = {k: (v.copy() if isinstance(v, np.ndarray) else v) for k, v in g["inputs"].items()}
+    if g["error"]:
+        with pytest.raises(Exception) as ei:
+            interp.execute_function(g["func"], **kw)
+        assert type(ei.value).__name__ == g["error"]
+        return
+    if g["seed"] is not None:
+        out = run_seeded(interp, g)
+    else:
+        out = interp.execute_function(g["func"], **kw)
+    mags = example_mag(name, g["inputs"])
+    want = dict(g["outputs"])
+    if g["digests"]:
+        o = OracleInterpreter()
+        o.load(g["src"])
+        ref = o.execute_function(g["func"], **{k: (v.copy() if isinstance(v, np.ndarray) else v)
+                                               for k, v in g["inputs"].items()})
+        want.update({k: ref[k] for k in g["digests"]})
+    for k, w in want.items():
+        if k in mags and g["tol"] is not None:
+            assert_contraction(f"{name}:{k}", out[k], w, mags[k], g["tol"])
+        else:
+            assert_matches(f"{name}:{k}", out[k], w, g["tol"])
