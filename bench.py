@@ -271,7 +271,14 @@ class Env:
 
 def _busy(exe, sets, stream, seconds, dev, torch):
     """Keep the GPU on this workload for `seconds` (clock sampling, power-cap
-    steady state before a tensor-core kernel is timed)."""
+    steady state before a tensor-core kernel is timed).  A plan that exchanges
+    data between ranks runs a fixed number of executions instead, so every
+    rank issues the same collectives."""
+    if exe.plan.collective:
+        for i in range(int(seconds * 200)):
+            exe.launch(sets[i % len(sets)][0], stream, sets[i % len(sets)][1])
+        torch.cuda.synchronize(dev)
+        return
     t_end = time.time() + seconds
     i = 0
     while time.time() < t_end:
@@ -279,6 +286,39 @@ def _busy(exe, sets, stream, seconds, dev, torch):
             exe.launch(sets[i % len(sets)][0], stream, sets[i % len(sets)][1])
             i += 1
         torch.cuda.synchronize(dev)
+
+
+def measure_batched(env: Env, exe, host, steps: int, n: int = 65536):
+    """B independent add_kernel executions per launch (Executable.batched):
+    the GB/s figure of the 6 KB workload.  n * 6 KB = 384 MiB per launch, three
+    times the L2."""
+    torch = env.torch
+    bx = exe.batched(n)
+    ts = []
+    for arr in host:
+        t = torch.empty(arr.nbytes * n, dtype=torch.uint8, device=env.dev)
+        t.view(n, arr.nbytes).copy_(torch.from_numpy(arr.view(np.uint8).reshape(1, -1)).expand(n, -1))
+        ts.append(t)
+    bufs = bx.buffers(ts)
+    stream = torch.cuda.current_stream(env.dev)
+    for _ in range(3):
+        bx.launch(ts, stream, bufs)
+    torch.cuda.synchronize(env.dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        bx.launch(ts, stream, bufs)
+    b.record(stream)
+    torch.cuda.synchronize(env.dev)
+    ms = a.elapsed_time(b) / steps
+    (ms,) = env.max_over_ranks(ms)
+    hbm_peak = peaks()[0]
+    gbs = n * WORK["vector_add"][1] / (ms / 1000.0) / 1e9
+    per_rank = 1 if (env.mode == "split" and env.world > 1) else env.world
+    return {"executions_per_launch": n, "value": per_rank * n / (ms / 1000.0), "unit": UNIT,
+            "ms_per_launch": ms, "gpu_launches": steps * len(bx.progs),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": gbs / hbm_peak, "kernel": "k_ew_bin_f16"}}
 
 
 def measure(env: Env, name: str, steps: int, with_cpu: bool):
@@ -428,6 +468,8 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
                    else "host launch per step"},
         "clocks": clk.summary(),
     }
+    if name == "vector_add" and not split:
+        out["batched"] = measure_batched(env, exe, host, steps)
     if with_cpu and rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(name)
     # graphs are released before any process-group teardown
@@ -467,7 +509,6 @@ def main():
     if not args.only:
         for name in ORDER:
             if name != args.config:
-                # the other workloads: fewer steps where one step is long
                 per[name] = measure(env, name, args.steps, with_cpu=True)
     if env.rank == 0:
         line = {"metric": METRIC, "value": head["value"], "unit": UNIT, "n_gpus": env.world,
@@ -480,6 +521,8 @@ def main():
                 "long_window": head["long_window"], "method": head["method"]}
         if "cpu_baseline" in head:
             line["cpu_baseline"] = head["cpu_baseline"]
+        if "batched" in head:
+            line["batched"] = head["batched"]
         if not args.only:
             line["per_config"] = per
         print(json.dumps(line), flush=True)

@@ -80,7 +80,9 @@ typedef struct {
   int32_t n_instr;
   int32_t n_units;
   int32_t unit_cols;   /* columns of the per-unit offset table */
-  int32_t contiguous;  /* all views dense row-major over the iteration space */
+  int32_t contiguous;  /* all views dense row-major over the iteration space; 2: also
+                          every view's start a multiple of 8 elements and every access
+                          inside its buffer in every unit (16-byte vector access) */
   int64_t numel;       /* elements of the iteration space per unit */
   int64_t shape[KTIR_MAX_RANK];
   KtirView view[KTIR_MAX_VIEWS];
@@ -297,6 +299,14 @@ int ktir_fmha_f16(const KtirFmhaDesc* desc, void* stream);
  * counterpart in the reference, whose memory is one NumPy array). */
 int ktir_copy_blocks(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
                      int64_t width, int64_t rows, void* stream);
+
+/* Packs the K and V rows of the 128-row tiles in tile_mask (bit t = tile t
+ * of every head's seq rows) from [bh*seq, d] f16 K and V into dst as
+ * [K | V][head][i-th tile of the mask][128][d]: one GPU's share of the K/V
+ * blocks that the sequence-split attention passes between GPUs (no
+ * counterpart in the reference, which runs on one host). */
+int ktir_pack_kv(void* dst, const void* k, const void* v, int64_t bh, int64_t seq, int64_t d,
+                 uint32_t tile_mask, void* stream);
 
 /* dst = a - b (subtract != 0) or a + b, byte by byte modulo 256, over n
  * bytes on `stream`.  A call split across GPUs returns whole tensors by

@@ -129,6 +129,39 @@ extern "C" int ktir_bytes_delta(void* dst, const void* a, const void* b, int64_t
   return check_launch("ktir_bytes_delta");
 }
 
+// The K/V rows of the 128-row tiles in tile_mask, every head, packed as
+// [K | V][head][i-th tile of the mask][128 rows][d] f16 (one CTA per 128-row
+// block, 16-byte copies)
+__global__ void __launch_bounds__(256) k_pack_kv(uint4* __restrict__ dst, const uint4* __restrict__ k,
+                                                 const uint4* __restrict__ v, int64_t bh, int64_t seq,
+                                                 unsigned tile_mask, int n_tiles, int64_t row_vecs) {
+  const int64_t blk = blockIdx.x;                  // (which, head, i)
+  const int i = (int)(blk % n_tiles);
+  const int64_t head = (blk / n_tiles) % bh;
+  const int which = (int)(blk / (n_tiles * bh));
+  const int tile = (int)__fns(tile_mask, 0, i + 1);
+  const int64_t n = 128 * row_vecs;                // 16-byte vectors per block
+  const uint4* src = (which ? v : k) + (head * seq + (int64_t)tile * 128) * row_vecs;
+  uint4* out = dst + blk * n;
+  for (int64_t e = threadIdx.x; e < n; e += blockDim.x) out[e] = src[e];
+}
+
+extern "C" int ktir_pack_kv(void* dst, const void* k, const void* v, int64_t bh, int64_t seq,
+                            int64_t d, uint32_t tile_mask, void* stream) {
+  const int n = __builtin_popcount(tile_mask);
+  if (!dst || !k || !v || bh < 1 || seq < 128 || seq % 128 || d < 8 || d % 8 || n == 0 ||
+      (seq / 128 < 32 && (tile_mask >> (seq / 128)) != 0))
+    return set_err(KTIR_ERR_ARG, "ktir_pack_kv: bad arguments");
+  if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(k) |
+        reinterpret_cast<uintptr_t>(v)) & 15) != 0)
+    return set_err(KTIR_ERR_UNSUPPORTED, "ktir_pack_kv: pointers must be 16-byte aligned");
+  const int64_t blocks = 2 * bh * n;
+  if (blocks > 0x7fffffffLL) return set_err(KTIR_ERR_UNSUPPORTED, "ktir_pack_kv: too many blocks");
+  k_pack_kv<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      (uint4*)dst, (const uint4*)k, (const uint4*)v, bh, seq, tile_mask, n, d * 2 / 16);
+  return check_launch("ktir_pack_kv");
+}
+
 // ---------------------------------------------------------------------------
 // fused elementwise
 // ---------------------------------------------------------------------------
@@ -181,6 +214,79 @@ __global__ void __launch_bounds__(256) k_ew(const __grid_constant__ KtirEwProgra
   }
 }
 
+// y = a op b over f16 views that are dense, 16-byte aligned and inside their
+// buffers in every unit (the lowering marks such programs contiguous == 2):
+// eight elements per thread in 16-byte loads and stores.  + - * on f16 pairs
+// round the exact result once, which is what NumPy's f16 loops give (they
+// compute in f32, whose 24 bits hold the exact sum or product of two f16s);
+// the quotient goes through f32 (24 >= 2 * 11 + 2 bits: rounding to f32 and
+// then to f16 equals rounding once).
+template <int OP>
+__global__ void __launch_bounds__(256) k_ew_bin_f16(const __grid_constant__ KtirEwProgram p,
+                                                    const __grid_constant__ KtirBuffers b,
+                                                    const int64_t* __restrict__ ut, int va, int vb,
+                                                    int vo) {
+  pdl_prologue();
+  const int64_t chunks = p.numel >> 3;
+  const int64_t items = chunks * p.n_units;
+  const KtirView& A = p.view[va];
+  const KtirView& Bv = p.view[vb];
+  const KtirView& O = p.view[vo];
+  const __half* pa = (const __half*)b.base[A.slot];
+  const __half* pb = (const __half*)b.base[Bv.slot];
+  __half* po = (__half*)b.base[O.slot];
+  for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t unit = it / chunks;
+    const int64_t c = (it - unit * chunks) << 3;
+    const int64_t* row = ut + unit * p.unit_cols;
+    const int64_t oa = A.off + (A.unit_col >= 0 ? row[A.unit_col] : 0) + c;
+    const int64_t ob = Bv.off + (Bv.unit_col >= 0 ? row[Bv.unit_col] : 0) + c;
+    const int64_t oo = O.off + (O.unit_col >= 0 ? row[O.unit_col] : 0) + c;
+    uint4 x = *reinterpret_cast<const uint4*>(pa + oa);
+    const uint4 y = *reinterpret_cast<const uint4*>(pb + ob);
+    __half2* hx = reinterpret_cast<__half2*>(&x);
+    const __half2* hy = reinterpret_cast<const __half2*>(&y);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (OP == OP_FADD) hx[q] = __hadd2(hx[q], hy[q]);
+      else if (OP == OP_FSUB) hx[q] = __hsub2(hx[q], hy[q]);
+      else if (OP == OP_FMUL) hx[q] = __hmul2(hx[q], hy[q]);
+      else {
+        const float2 fx = __half22float2(hx[q]), fy = __half22float2(hy[q]);
+        hx[q] = __floats2half2_rn(fx.x / fy.x, fx.y / fy.y);
+      }
+    }
+    *reinterpret_cast<uint4*>(po + oo) = x;
+  }
+}
+
+// the two-load binary f16 program the vector kernel covers: returns the op,
+// with the views of the operands and of the result
+static int match_bin_f16(const KtirEwProgram& p, int* va, int* vb, int* vo) {
+  if (p.contiguous != 2 || p.n_instr != 4 || (p.numel & 7)) return 0;
+  const KtirInstr* c = p.code;
+  if (c[0].op != OP_LD || c[1].op != OP_LD || c[3].op != OP_ST) return 0;
+  const int op = c[2].op;
+  if (op != OP_FADD && op != OP_FSUB && op != OP_FMUL && op != OP_FDIV) return 0;
+  if (c[2].dt != KTIR_F16 || c[3].a != c[2].dst || c[0].dst == c[1].dst) return 0;
+  if (c[2].a == c[0].dst && c[2].b == c[1].dst) {
+    *va = c[0].aux;
+    *vb = c[1].aux;
+  } else if (c[2].a == c[1].dst && c[2].b == c[0].dst) {
+    *va = c[1].aux;
+    *vb = c[0].aux;
+  } else {
+    return 0;
+  }
+  *vo = c[3].aux;
+  if (*va >= p.n_views || *vb >= p.n_views || *vo >= p.n_views) return 0;
+  if (p.view[*va].dtype != KTIR_F16 || p.view[*vb].dtype != KTIR_F16 ||
+      p.view[*vo].dtype != KTIR_F16 || c[3].dt != KTIR_F16)
+    return 0;
+  return op;
+}
+
 extern "C" int ktir_ew(const KtirEwProgram* prog, const KtirBuffers* bufs,
                        const int64_t* unit_table, void* stream) {
   if (!prog || !bufs) return set_err(KTIR_ERR_ARG, "ktir_ew: null descriptor");
@@ -188,8 +294,19 @@ extern "C" int ktir_ew(const KtirEwProgram* prog, const KtirBuffers* bufs,
       prog->rank > KTIR_MAX_RANK || prog->n_units < 1)
     return set_err(KTIR_ERR_ARG, "ktir_ew: descriptor out of range");
   if (prog->numel == 0) return KTIR_OK;
-  dim3 grid(grid_x(prog->numel, 256, 148 * 16), prog->n_units < 65535 ? prog->n_units : 65535);
   cudaStream_t s = (cudaStream_t)stream;
+  int va, vb, vo;
+  if (const int op = match_bin_f16(*prog, &va, &vb, &vo)) {
+    const int g = grid_x((prog->numel >> 3) * prog->n_units, 256, 148 * 8);
+    switch (op) {
+      case OP_FADD: launch_pdl(k_ew_bin_f16<OP_FADD>, dim3(g), dim3(256), 0, s, *prog, *bufs, unit_table, va, vb, vo); break;
+      case OP_FSUB: launch_pdl(k_ew_bin_f16<OP_FSUB>, dim3(g), dim3(256), 0, s, *prog, *bufs, unit_table, va, vb, vo); break;
+      case OP_FMUL: launch_pdl(k_ew_bin_f16<OP_FMUL>, dim3(g), dim3(256), 0, s, *prog, *bufs, unit_table, va, vb, vo); break;
+      default: launch_pdl(k_ew_bin_f16<OP_FDIV>, dim3(g), dim3(256), 0, s, *prog, *bufs, unit_table, va, vb, vo); break;
+    }
+    return check_launch("ktir_ew");
+  }
+  dim3 grid(grid_x(prog->numel, 256, 148 * 16), prog->n_units < 65535 ? prog->n_units : 65535);
   if (prog->contiguous)
     launch_pdl(k_ew<true>, grid, dim3(256), 0, s, *prog, *bufs, unit_table);
   else

@@ -199,6 +199,16 @@ class Executable:
                 self.launch(ts, s, b)
         return g
 
+    def batched(self, n: int) -> "BatchedExecutable":
+        """n independent executions of this call signature in one launch per
+        program (many small calls, such as candidate kernels evaluated on
+        many inputs).  Each tensor argument becomes one tensor n times its
+        size, execution i's copy at element offset i * its size.  Only
+        elementwise plans whose every access stays inside its tensor qualify:
+        a read past a tensor's end must see the reference's zero fill, not
+        the next execution's data."""
+        return BatchedExecutable(self, n)
+
     def check_status(self, value: Optional[int] = None) -> None:
         """Raise for the device status word (read here unless the caller has
         already downloaded it)."""
@@ -211,6 +221,58 @@ class Executable:
         if v & R.STATUS_TIMEOUT:
             self.status.zero_()
             raise RuntimeError("device wait timed out")
+
+
+class BatchedExecutable:
+    """An elementwise plan run as n independent executions per launch (see
+    Executable.batched)."""
+
+    def __init__(self, exe: Executable, n: int):
+        import copy
+        torch = exe.torch
+        plan = exe.plan
+        if plan.kind != "elementwise" or not plan.launches or n < 1 or \
+                any(l.kind != "ew" or l.meta.get("prog") is None or
+                    l.meta["prog"].contiguous != 2 for l in plan.launches):
+            raise NotImplementedError("batched execution needs an elementwise plan whose "
+                                      "accesses stay inside their tensors")
+        self.exe, self.n = exe, n
+        numel = [b.numel for b in exe.space.buffers]
+        self.numel = numel
+        self.progs, self.tables = [], []
+        for l in plan.launches:
+            p = copy.deepcopy(l.meta["prog"])
+            t = l.meta["table"]
+            units = t.shape[0]
+            # column j of the unit table offsets view(s) of one slot; execution
+            # i adds i times that slot's tensor size
+            add = np.zeros(t.shape[1], np.int64)
+            for v in range(p.n_views):
+                if p.view[v].unit_col >= 0:
+                    add[p.view[v].unit_col] = numel[p.view[v].slot]
+            big = (t[None, :, :] + np.arange(n, dtype=np.int64)[:, None, None] * add[None, None, :])
+            p.n_units = n * units
+            self.progs.append(p)
+            self.tables.append(torch.from_numpy(big.reshape(n * units, -1).copy()).to(exe.device))
+
+    def buffers(self, tensors) -> R.KtirBuffers:
+        b = R.KtirBuffers()
+        for i, t in enumerate(tensors):
+            b.base[i] = t.data_ptr()
+            b.numel[i] = self.numel[i] * self.n
+        return b
+
+    def launch(self, tensors, stream=None, bufs: Optional[R.KtirBuffers] = None) -> None:
+        """Enqueue the n executions over `tensors` (one per call tensor, each n
+        times its size, in argument address order)."""
+        torch = self.exe.torch
+        s = stream if stream is not None else torch.cuda.current_stream(self.exe.device)
+        sp = C.c_void_p(s.cuda_stream)
+        if bufs is None:
+            bufs = self.buffers(tensors)
+        lib = self.exe.lib
+        for p, t in zip(self.progs, self.tables):
+            R.check(lib.ktir_ew(C.byref(p), C.byref(bufs), C.c_void_p(t.data_ptr()), sp), "ktir_ew")
 
 
 class KTIRInterpreter:

@@ -344,6 +344,7 @@ class Launch:
     fn: Callable[..., None]       # fn(bufs, stream) issues the launch
     kind: str
     kernels: int = 1
+    meta: Dict[str, Any] = field(default_factory=dict)
 
 
 @dataclass
@@ -829,14 +830,31 @@ class Lowerer:
                 t = _s0.target
                 return mkview(self.slots[t.buf.index], t.dtype, 0, t.strides, _n)
             prog = program(bld, shape, len(members), n_ld + 1, vf, contiguous)
+            if contiguous and self._vector_ok(prog, table):
+                prog.contiguous = 2
             ut = self.dev.i64(table)
 
             def run(bufs, stream, status, _p=prog, _ut=ut):
                 R.check(lib.ktir_ew(C.byref(_p), C.byref(bufs), C.c_void_p(_ut), stream), "ktir_ew")
-            launches.append(Launch(run, "ew"))
+            launches.append(Launch(run, "ew", meta={"prog": prog, "table": table}))
         plan = Plan("elementwise", launches, [])
         plan.info.update(units=len(stores), elems=sum(int(np.prod(s.target.shape)) for s in stores))
         return plan
+
+    def _vector_ok(self, prog, table: np.ndarray) -> bool:
+        """Whether every view of a dense program is f16, starts on a multiple of 8
+        elements and stays inside its buffer in every unit (16-byte accesses, no
+        zero fill or truncation needed)."""
+        numel_of = {self.slots[b.index]: b.numel for b in self.trace.space.buffers}
+        n = int(prog.numel)
+        for i in range(prog.n_views):
+            v = prog.view[i]
+            if v.dtype != R.F16 or v.slot not in numel_of:
+                return False
+            offs = v.off + (table[:, v.unit_col] if v.unit_col >= 0 else np.zeros(1, np.int64))
+            if (offs % 8).any() or (offs < 0).any() or (offs + n > numel_of[v.slot]).any():
+                return False
+        return True
 
 
 def _collect_loads_in_order(root: Node, out: List[Node]) -> None:

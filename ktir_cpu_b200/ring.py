@@ -78,8 +78,17 @@ def share_mask(tiles: Sequence[int]) -> int:
     return m
 
 
-def ring_attention_plan(low, prob):
-    """Device plan for one rank of the ring (see the module docstring)."""
+def ring_attention_plan(low, prob, exchange: str = "allgather"):
+    """Device plan for one rank (see the module docstring).
+
+    Step 0 adds the rank's own key tiles straight from the call's K and V,
+    while the comm stream packs its share (ktir_pack_kv) and passes the
+    shares between the GPUs; the later steps add the other shares from the
+    staging buffer ([world][K | V][head][tile][128][d] f16).  exchange
+    "ring": world - 1 NCCL send/recv steps, each GPU forwarding the share it
+    last received, one kernel per arrived share; "allgather": one NCCL
+    all-gather of the shares (NCCL's own ring or NVLink SHARP), then one
+    kernel for every other share."""
     import ctypes as C
 
     import torch
@@ -110,81 +119,100 @@ def ring_attention_plan(low, prob):
         owner, local, kv_tiles = staging_layout(tiles_of, n_tiles)
     except ValueError:
         return None
+    if len({len(t) for t in tiles_of}) != 1:
+        return None                       # equal shares: NCCL all-gather and same-size sends
     mine = tiles_of[rank]
     dev = low.device
-    share_elems = bh * kv_tiles * TILE * d
-    k_sh = torch.empty(world * share_elems, dtype=torch.float16, device=dev)
-    v_sh = torch.empty(world * share_elems, dtype=torch.float16, device=dev)
+    share_rows = bh * kv_tiles * TILE
+    row_bytes = d * 2
+    kv_all = torch.empty(world * 2 * share_rows * d, dtype=torch.float16, device=dev)
     o_acc = torch.empty(bh * len(mine) * TILE * d, dtype=torch.float32, device=dev)
     ml = torch.empty(bh * len(mine) * TILE * 2, dtype=torch.float32, device=dev)
     lib = R.load_library()
     sq, sk, sv, so = (low.slots[b.index] for b in (prob["q"], prob["k"], prob["v"], prob["o"]))
-    row_bytes = d * 2
     comm = torch.cuda.Stream(dev) if dev.type == "cuda" else None
-    descs = []
-    for t, s in enumerate(step_shares(rank, world)):
+    own_mask = share_mask(mine)
+    all_mask = share_mask(range(n_tiles))
+
+    def desc(mask, first, last, staged):
         dsc = R.KtirFmhaPartDesc()
         dsc.bh, dsc.seq, dsc.d = bh, seq, d
-        dsc.kv_rows = world * bh * kv_tiles * TILE
         dsc.scale, dsc.causal = prob["scale"], 1
-        dsc.n_qtiles, dsc.kv_tiles = len(mine), kv_tiles
-        dsc.key_mask = share_mask(tiles_of[s])
-        dsc.flags = (1 if t == 0 else 0) | (2 if t == world - 1 else 0)
+        dsc.n_qtiles = len(mine)
+        dsc.key_mask = mask
+        dsc.flags = (1 if first else 0) | (2 if last else 0)
         dsc.o_acc, dsc.ml = o_acc.data_ptr(), ml.data_ptr()
         for i, qt in enumerate(mine):
             dsc.qtiles[i] = qt
-        for kt in range(n_tiles):
-            dsc.kv_owner[kt], dsc.kv_local[kt] = owner[kt], local[kt]
-        dsc.k, dsc.v = k_sh.data_ptr(), v_sh.data_ptr()
-        descs.append(dsc)
+        if staged:
+            # K of share s at rows ((2s * bh + h) * kv_tiles + i) * 128, V one share later
+            dsc.kv_tiles, dsc.kv_rows = kv_tiles, (2 * world - 1) * share_rows
+            dsc.k = kv_all.data_ptr()
+            dsc.v = kv_all.data_ptr() + share_rows * row_bytes
+            for kt in range(n_tiles):
+                dsc.kv_owner[kt], dsc.kv_local[kt] = 2 * owner[kt], local[kt]
+        else:
+            # the call's own K / V: tile kt of head h at row h * seq + kt * 128
+            dsc.kv_tiles, dsc.kv_rows = n_tiles, bh * seq
+            for kt in range(n_tiles):
+                dsc.kv_owner[kt], dsc.kv_local[kt] = 0, kt
+        return dsc
+
+    shares = step_shares(rank, world)
+    if exchange == "ring":
+        steps = [desc(own_mask, True, False, False)] + \
+            [desc(share_mask(tiles_of[s]), False, t == world - 1, True)
+             for t, s in enumerate(shares) if t > 0]
+    else:
+        steps = [desc(own_mask, True, False, False), desc(all_mask & ~own_mask, False, True, True)]
     nxt, prv = (rank + 1) % world, (rank - 1) % world
     if group is not None:
         nxt, prv = dist.get_global_rank(group, nxt), dist.get_global_rank(group, prv)
 
-    def share(buf, s):
-        return buf[s * share_elems:(s + 1) * share_elems]
+    def share(s):
+        return kv_all[s * 2 * share_rows * d:(s + 1) * 2 * share_rows * d]
 
     def run(bufs, stream, status):
         compute = (torch.cuda.ExternalStream(stream.value, device=dev) if stream.value
                    else torch.cuda.default_stream(dev))
-        # this rank's share: K / V rows of its query tiles, every head
-        for i, qt in enumerate(mine):
-            for src_slot, dst in ((sk, k_sh), (sv, v_sh)):
-                R.check(lib.ktir_copy_blocks(
-                    C.c_void_p(dst.data_ptr() + ((rank * bh * kv_tiles + i) * TILE) * row_bytes),
-                    C.c_int64(kv_tiles * TILE * row_bytes),
-                    C.c_void_p(bufs.base[src_slot] + qt * TILE * row_bytes),
-                    C.c_int64(seq * row_bytes), C.c_int64(TILE * row_bytes), C.c_int64(bh),
-                    stream), "ktir_copy_blocks")
-        # the comm stream starts after this execution's packing and after the
-        # previous execution's kernels (which read the shares it overwrites)
+        # the comm stream starts after the previous execution's kernels, which
+        # read the staging buffer it overwrites
         comm.wait_stream(compute)
-        shares = step_shares(rank, world)
-        arrived = None
-        for t, s in enumerate(shares):
-            if arrived is not None:
-                compute.wait_event(arrived)
-            dsc = descs[t]
-            dsc.q, dsc.o = bufs.base[sq], bufs.base[so]
-            dsc.status = status
-            R.check(lib.ktir_fmha_f16_part(C.byref(dsc), stream), "ktir_fmha_f16_part")
-            if t < world - 1:
-                with torch.cuda.stream(comm):
-                    ops = [dist.P2POp(dist.isend, share(k_sh, s), nxt, group),
-                           dist.P2POp(dist.isend, share(v_sh, s), nxt, group),
-                           dist.P2POp(dist.irecv, share(k_sh, shares[t + 1]), prv, group),
-                           dist.P2POp(dist.irecv, share(v_sh, shares[t + 1]), prv, group)]
+        k0 = steps[0]
+        k0.q, k0.o, k0.k, k0.v, k0.status = (bufs.base[sq], bufs.base[so], bufs.base[sk],
+                                              bufs.base[sv], status)
+        R.check(lib.ktir_fmha_f16_part(C.byref(k0), stream), "ktir_fmha_f16_part")
+        arrived = []
+        with torch.cuda.stream(comm):
+            cs = C.c_void_p(comm.cuda_stream)
+            R.check(lib.ktir_pack_kv(C.c_void_p(share(rank).data_ptr()), C.c_void_p(bufs.base[sk]),
+                                     C.c_void_p(bufs.base[sv]), bh, seq, d, own_mask, cs),
+                    "ktir_pack_kv")
+            if exchange == "ring":
+                for t in range(world - 1):
+                    ops = [dist.P2POp(dist.isend, share(shares[t]), nxt, group),
+                           dist.P2POp(dist.irecv, share(shares[t + 1]), prv, group)]
                     for w in dist.batch_isend_irecv(ops):
                         w.wait()
-                    arrived = torch.cuda.Event()
-                    arrived.record(comm)
+                    ev = torch.cuda.Event()
+                    ev.record(comm)
+                    arrived.append(ev)
+            else:
+                dist.all_gather_into_tensor(kv_all, share(rank), group=group)
+                ev = torch.cuda.Event()
+                ev.record(comm)
+                arrived.append(ev)
+        for ev, dsc in zip(arrived, steps[1:]):
+            compute.wait_event(ev)
+            dsc.q, dsc.o, dsc.status = bufs.base[sq], bufs.base[so], status
+            R.check(lib.ktir_fmha_f16_part(C.byref(dsc), stream), "ktir_fmha_f16_part")
 
-    plan = Plan("attention", [Launch(run, "kv_ring", world)], [], status_check=True)
-    plan.scratch.update(k_sh=k_sh, v_sh=v_sh, o_acc=o_acc, ml=ml, comm=comm)
+    plan = Plan("attention", [Launch(run, "kv_ring", len(steps) + 1)], [], status_check=True)
+    plan.scratch.update(kv_all=kv_all, o_acc=o_acc, ml=ml, comm=comm)
     flops = 4 * bh * seq * seq * d // 2
     plan.info.update(bh=bh, seq=seq, d=d, causal=True, scale=prob["scale"], flops=flops,
-                     ring=dict(tiles=tiles_of, kv_tiles=kv_tiles,
-                               bytes_per_step=2 * share_elems * 2))
+                     ring=dict(tiles=tiles_of, kv_tiles=kv_tiles, exchange=exchange,
+                               share_bytes=2 * share_rows * row_bytes))
     # this rank reads only its own query tiles and K/V share from the call's
     # tensors (the rest arrives over NVLink): (buffer index, byte ranges)
     ranges = []

@@ -135,7 +135,8 @@ class KtirHostCopy(C.Structure):
 EXPORTS = ["ktir_version", "ktir_last_error", "ktir_device_count", "ktir_ew",
            "ktir_softmax_rows", "ktir_gather_rmw", "ktir_reduce", "ktir_matmul",
            "ktir_offsets", "ktir_indirect", "ktir_gemm_f16", "ktir_fmha_f16",
-           "ktir_fmha_f16_part", "ktir_copy_blocks", "ktir_bytes_delta", "ktir_wait_selftest", "ktir_host_threads", "ktir_host_upload", "ktir_host_download"]
+           "ktir_fmha_f16_part", "ktir_copy_blocks", "ktir_pack_kv", "ktir_bytes_delta",
+           "ktir_wait_selftest", "ktir_host_threads", "ktir_host_upload", "ktir_host_download"]
 
 _LIB: Optional[C.CDLL] = None
 
@@ -175,6 +176,7 @@ def load_library(build_if_missing: bool = False) -> C.CDLL:
     lib.ktir_fmha_f16_part.argtypes = [C.POINTER(KtirFmhaPartDesc), vp]
     lib.ktir_copy_blocks.argtypes = [vp, C.c_int64, vp, C.c_int64, C.c_int64, C.c_int64, vp]
     lib.ktir_bytes_delta.argtypes = [vp, vp, vp, C.c_int64, C.c_int32, vp]
+    lib.ktir_pack_kv.argtypes = [vp, vp, vp, C.c_int64, C.c_int64, C.c_int64, C.c_uint32, vp]
     lib.ktir_wait_selftest.argtypes = [vp, C.c_uint32, vp]
     lib.ktir_host_threads.argtypes = []
     lib.ktir_host_upload.argtypes = [C.POINTER(KtirHostXfer), C.c_int, C.c_int, vp]

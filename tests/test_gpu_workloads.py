@@ -86,3 +86,26 @@ def test_softmax_row_lengths(cols):
     assert_matches("out", got["out_ptr"], want["out_ptr"], 1e-2)
     s = got["out_ptr"].astype(np.float64).sum(axis=1)
     assert np.all(np.abs(s - 1.0) < 1e-2)
+
+
+def test_vector_add_batched_executions_bitexact():
+    """Executable.batched: 3000 independent add_kernel executions in one launch,
+    each on its own inputs, every result bit-exact (f16 x + y)."""
+    import torch
+    from ktir_cpu_b200 import KTIRInterpreter
+    kw = W.inputs("vector_add", seed=1)
+    dev = KTIRInterpreter()
+    dev.load(W.source("vector_add"))
+    dev.execute_function("add_kernel", **{k: v.copy() for k, v in kw.items()})
+    exe = dev.last_executable
+    n = 3000
+    bx = exe.batched(n)
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((n, 1024)).astype(np.float16)
+    y = rng.standard_normal((n, 1024)).astype(np.float16)
+    # tensors in argument address order: x, y, out
+    ts = [torch.from_numpy(a.view(np.uint8).reshape(-1).copy()).cuda() for a in (x, y, np.zeros_like(x))]
+    bx.launch(ts)
+    torch.cuda.synchronize()
+    out = ts[2].cpu().numpy().view(np.float16).reshape(n, 1024)
+    assert np.array_equal(out, x + y)
