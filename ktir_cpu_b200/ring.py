@@ -130,7 +130,9 @@ def ring_attention_plan(low, prob, exchange: str = "allgather"):
     ml = torch.empty(bh * len(mine) * TILE * 2, dtype=torch.float32, device=dev)
     lib = R.load_library()
     sq, sk, sv, so = (low.slots[b.index] for b in (prob["q"], prob["k"], prob["v"], prob["o"]))
-    comm = torch.cuda.Stream(dev) if dev.type == "cuda" else None
+    # high priority: the packing and NCCL kernels take their SMs ahead of the
+    # attention kernel's CTAs, which would otherwise fill every SM first
+    comm = torch.cuda.Stream(dev, priority=-1) if dev.type == "cuda" else None
     own_mask = share_mask(mine)
     all_mask = share_mask(range(n_tiles))
 
@@ -176,12 +178,9 @@ def ring_attention_plan(low, prob, exchange: str = "allgather"):
         compute = (torch.cuda.ExternalStream(stream.value, device=dev) if stream.value
                    else torch.cuda.default_stream(dev))
         # the comm stream starts after the previous execution's kernels, which
-        # read the staging buffer it overwrites
+        # read the staging buffer it overwrites; its work is queued before the
+        # first attention step so that it reaches the SMs first
         comm.wait_stream(compute)
-        k0 = steps[0]
-        k0.q, k0.o, k0.k, k0.v, k0.status = (bufs.base[sq], bufs.base[so], bufs.base[sk],
-                                              bufs.base[sv], status)
-        R.check(lib.ktir_fmha_f16_part(C.byref(k0), stream), "ktir_fmha_f16_part")
         arrived = []
         with torch.cuda.stream(comm):
             cs = C.c_void_p(comm.cuda_stream)
@@ -202,6 +201,10 @@ def ring_attention_plan(low, prob, exchange: str = "allgather"):
                 ev = torch.cuda.Event()
                 ev.record(comm)
                 arrived.append(ev)
+        k0 = steps[0]
+        k0.q, k0.o, k0.k, k0.v, k0.status = (bufs.base[sq], bufs.base[so], bufs.base[sk],
+                                              bufs.base[sv], status)
+        R.check(lib.ktir_fmha_f16_part(C.byref(k0), stream), "ktir_fmha_f16_part")
         for ev, dsc in zip(arrived, steps[1:]):
             compute.wait_event(ev)
             dsc.q, dsc.o, dsc.status = bufs.base[sq], bufs.base[so], status

@@ -113,12 +113,11 @@ example("ex_rfc_add_control_flow", "rfc/add-with-control-flow.mlir", "add", lamb
         seed=lambda r: [("HBM", 0, 1024, _n(r, (96, 64))), ("HBM", 0, 12288, _n(r, (96, 64))),
                         ("HBM", 0, 18432, np.zeros((96, 64), np.float16))],
         reads=[("C", "HBM", 0, 18432, 96 * 64, "f16")])
-example("ex_rfc_distributed_view_copy", "rfc/distributed-view-copy.mlir", "distributed_view_copy",
-        lambda r: {},
-        seed=lambda r: [("HBM", 0, 0, _n(r, (96, 64))), ("LX", 0, 12288, _n(r, (64, 32))),
-                        ("LX", 1, 16384, _n(r, (64, 64))),
-                        ("HBM", 0, 24576, np.zeros((192, 64), np.float16))],
-        reads=[("B", "HBM", 0, 24576, 192 * 64, "f16")])
+# rfc/distributed-view-copy.mlir is left out: its header notes that the
+# reference resolves every <LX, core = N> view to the executing core's own
+# scratchpad (its test is an expected failure), so its output depends on
+# which core ran last and what that core's scratchpad held; the distributed
+# and LX views are covered by the dist_* golden cases instead.
 example("ex_rfc_indirect_access_copy", "rfc/indirect-access-copy.mlir", "indirect_access_copy",
         lambda r: {},
         seed=lambda r: [("HBM", 0, 0, _n(r, (64, 64))),

@@ -45,7 +45,8 @@ def run_seeded(interp, g):
             mem = interp.memory.hbm if sp == "HBM" else interp.memory.get_lx(core)
             mem.write(addr, arr.copy())
     interp._prepare_execution = prep
-    interp.execute_function(g["func"], **{k: v.copy() for k, v in g["inputs"].items()})
+    interp.execute_function(g["func"], **{k: (v.copy() if isinstance(v, np.ndarray) else v)
+                                          for k, v in g["inputs"].items()})
     out = {}
     for name, sp, core, addr, n, dt in g["reads"]:
         mem = interp.memory.hbm if sp == "HBM" else interp.memory.get_lx(core)
