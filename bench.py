@@ -86,6 +86,18 @@ def peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
+# variants measured beside the five workloads when the grid is split over GPUs:
+# the attention program with cores that own whole heads (no K/V exchange)
+VARIANTS = {"attention_heads": ("attention", {"layout": "heads"})}
+WORKLOAD["attention_heads"] = ("causal MHA B4 H32 S2048 D128 f16, grid 32, cores own whole "
+                               "heads")
+
+
+def base_of(name: str):
+    """(workload, extra KTIR generator parameters) of a bench entry."""
+    return VARIANTS.get(name, (name, {}))
+
+
 def config_dict(name: str, world: int, mode: str):
     """The workload's description; both arms emit exactly this dict."""
     if world == 1:
@@ -94,8 +106,10 @@ def config_dict(name: str, world: int, mode: str):
         par = f"replicas x{world}"
     else:
         par = f"core grid split over {world} GPUs by contiguous core ranges"
+    base, extra = base_of(name)
+    params = dict(W.FULL[base], **extra)
     return {"workload": WORKLOAD[name], "name": name,
-            "params": {k: (list(v) if isinstance(v, tuple) else v) for k, v in W.FULL[name].items()},
+            "params": {k: (list(v) if isinstance(v, tuple) else v) for k, v in params.items()},
             "parallelism": par}
 
 
@@ -327,9 +341,10 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
     from ktir_cpu_b200 import KTIRInterpreter
     args, dev, world, rank = env.args, env.dev, env.world, env.rank
     split = env.mode == "split" and world > 1
-    src = W.source(name)
-    fname = W.FUNC[name]
-    kw = W.inputs(name, seed=0 if split else rank)
+    base, extra = base_of(name)
+    src = W.source(base, **extra)
+    fname = W.FUNC[base]
+    kw = W.inputs(base, seed=0 if split else rank)
     interp = KTIRInterpreter(device=dev, shard=(rank, world, None) if split else None)
     interp.load(src)
     # first call traces + lowers (cached) and runs the path once
@@ -435,7 +450,7 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
     e2e = per_step_execs * e2e_steps / e2e_s
 
     hbm_peak, tc_peak, tc_sustained, src_peak = peaks()
-    bound, work = WORK[name]
+    bound, work = WORK[base]
     if split:
         work = work / world   # each rank's share of one execution
     kern_ms = k_ms / steps
@@ -451,11 +466,11 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
         "long_window": {"steps": steps * reps, "ms": long_ms, "value": long_value,
                         "ms_per_step": long_ms / (steps * reps)},
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                     "frac": achieved / peak, "traffic": read_traffic(name),
+                     "frac": achieved / peak, "traffic": read_traffic(base),
                      "peak_source": src_peak + (" (sustained; timed after 1.5 s of load)"
                                                 if bound == "tensor" else ""),
                      "frac_of_burst": (achieved / tc_peak if bound == "tensor" else None),
-                     "kernel": DOMINANT[name], "kernel_ms": kern_ms,
+                     "kernel": DOMINANT[base], "kernel_ms": kern_ms,
                      "isolated_launch_ms": iso_ms, "plan_kernels": plan.kernel_launches},
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": e2e_exe.last_h2d_bytes,
                 "d2h_bytes_per_step": e2e_exe.last_d2h_bytes,
@@ -471,7 +486,7 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
     if name == "vector_add" and not split:
         out["batched"] = measure_batched(env, exe, host, steps)
     if with_cpu and rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(name)
+        out["cpu_baseline"] = cpu_baseline(base)
     # graphs are released before any process-group teardown
     del graph
     return out
@@ -507,7 +522,8 @@ def main():
     head = measure(env, args.config, args.steps, with_cpu=True)
     per = {args.config: head}
     if not args.only:
-        for name in ORDER:
+        extra = list(VARIANTS) if env.mode == "split" and env.world > 1 else []
+        for name in ORDER + extra:
             if name != args.config:
                 per[name] = measure(env, name, args.steps, with_cpu=True)
     if env.rank == 0:
