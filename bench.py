@@ -373,8 +373,13 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
         for i in range(steps):
             exe.launch(sets[i % n_sets][0], stream, sets[i % n_sets][1])
         torch.cuda.synchronize(dev)
-        return {"profile_run": name, "plan": plan.kind,
-                "launches": (args.warmup + steps) * plan.kernel_launches}
+        out = {"profile_run": name, "plan": plan.kind,
+               "launches": (args.warmup + steps) * plan.kernel_launches}
+        if name == "vector_add" and not split:
+            # then the batched variant: warmup + steps launches of 65536 executions
+            b = measure_batched(env, exe, host, steps)
+            out["batched_launches"] = 3 + steps + b["gpu_launches"]
+        return out
     # the K timed executions, recorded once as a CUDA graph so the host's
     # per-launch cost does not pace the device (plans with an NCCL exchange
     # keep plain launches)

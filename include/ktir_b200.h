@@ -178,6 +178,22 @@ typedef struct {
   int32_t* status;             /* device status word (KTIR_STATUS_TIMEOUT) */
 } KtirGemmDesc;
 
+/* GEMM of any shape with the reference's rounding of each K block: C (f16) =
+ * the running sum over K blocks of block_k of f16(A_blk @ B_blk) (each block
+ * product summed in f32 and rounded to f16, as NumPy multiplies f16 tiles),
+ * the running sum rounded to f16 after each block when acc_f16, else kept in
+ * f32 and rounded once at the end.  block_k = 0: one block of all of K.  Rows,
+ * columns and k past the matrix read as zero; only C[0:m, 0:n] is written.
+ * lda, ldb multiples of 8 elements; a, b 16-byte aligned. */
+typedef struct {
+  void* a; void* b; void* c;
+  int64_t lda, ldb, ldc;
+  int64_t m, n, k;
+  int32_t block_k;             /* multiple of 16, or 0 */
+  int32_t acc_f16;
+  int32_t* status;
+} KtirGemmBlockedDesc;
+
 /* Causal flash attention over [bh, seq, d] f16 tensors laid out as
  * [bh*seq, d] rows; scale applied to S in f32; online softmax in f32. */
 typedef struct {
@@ -288,6 +304,12 @@ int ktir_wait_selftest(int32_t* status, uint32_t spin_limit, void* stream);
 /* tcgen05 GEMM (replaces the linalg.matmul K loop, ktir_cpu/dialects/linalg_ops.py:273-297
  * with ops/arith_ops.py:403-419, for whole-matrix tilings). */
 int ktir_gemm_f16(const KtirGemmDesc* desc, void* stream);
+
+/* tcgen05 GEMM of any shape with per-block f16 rounding (see
+ * KtirGemmBlockedDesc): linalg.matmul of f16 tiles inside a K loop, and
+ * whole-matrix tilings the aligned kernel does not take
+ * (ktir_cpu/dialects/linalg_ops.py:273-297, ops/arith_ops.py:403-419). */
+int ktir_gemm_f16_blocked(const KtirGemmBlockedDesc* desc, void* stream);
 
 /* Causal attention (replaces the online-softmax scf.for of matmul / reduce /
  * exp ops the attention rewrite recognises). */

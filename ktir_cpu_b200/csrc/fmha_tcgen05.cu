@@ -5,19 +5,24 @@
 // 64 rows with three warp roles that meet only at mbarriers; two CTAs share
 // an SM, so while one CTA's softmax warps work the other's keep the tensor
 // cores busy:
-//   warps 4, 6 (TMA)  warp 4 loads Q once and K_j into a 2-stage ring, warp 6
-//                     loads V_j into a 1-stage ring, every slot refilled as soon
-//                     as the MMA that read it completes
+//   warps 4, 6 (TMA)  warp 4 loads Q once and K_j, warp 6 loads V_j, each into
+//                     its own 2-stage ring, every slot refilled as soon as the
+//                     MMA that read it completes
 //   warp 5 (MMA)      S_j = Q K_j^T (M=128 N=64 K=128) into TMEM S buffer
 //                     j & 1; as soon as the softmax warps hand over P_j it
-//                     issues O += Phi_j V_j + Plo_j V_j (M=128 N=128 K=2x64)
-//                     and S_{j+2} into the buffer S_j has just left, so the
-//                     next two S blocks are always computed ahead of the softmax
+//                     issues O += Phi_j V_j + Plo_j V_j (M=128 N=128 K=2x64,
+//                     P read from TMEM) and then S_{j+2} into the same TMEM
+//                     buffer: the tensor pipe runs one thread's tcgen05.mma in
+//                     issue order, so the PV product has read P_j before
+//                     S_{j+2} is written over it; the next two S blocks are
+//                     always computed ahead of the softmax
 //   warps 0-3         thread t owns query row t = TMEM lane t: tcgen05.ld of
 //                     S_j, masked max of x = s * scale * log2(e), P = 2^(x - m)
 //                     in f32, split into Phi = f16(P) and Plo = f16(P - Phi),
-//                     each written as one 128-byte swizzled row of its tile in
-//                     shared memory; row sum l in f32.  The two f16 halves
+//                     written with tcgen05.st over S_j's TMEM columns (S_j is
+//                     in registers by then): Phi in columns 0..31, Plo in
+//                     32..63, two f16 per column; row sum l in f32.  The two
+//                     f16 halves
 //                     carry P to about 22 bits, so the PV product keeps the
 //                     f32 probabilities of the reference's online softmax
 //                     (an f16 P alone moves outputs that cancel by more than
@@ -26,10 +31,11 @@
 // only moves when a row's max exceeds it by more than 2^8; then the softmax
 // warp waits for the previous PV and rescales its O rows in TMEM
 // (warp-uniform), otherwise O and l keep sharing m.
-// Shared memory (Q, K and V rings, Phi, Plo, mbarriers) fills exactly half an SM, so
-// the dynamic allocation keeps only 896 bytes for aligning the tiles to the
-// 1024 bytes the 128-byte swizzle needs; a CTA whose window cannot be aligned
-// within that reports KTIR_STATUS_TIMEOUT and does nothing.
+// Shared memory (Q, K and V rings, mbarriers) fits two CTAs per SM with 896
+// bytes for aligning the tiles to the 1024 bytes the 128-byte swizzle needs; a
+// CTA whose window cannot be aligned within that reports KTIR_STATUS_TIMEOUT
+// and does nothing.  With P in TMEM no shared memory carries P: the tensor
+// pipe reads only Q, K and V there.
 // Every wait is bounded; a timed-out wait raises the CTA's abort flag, every
 // role then leaves its loop, and the CTA still frees its TMEM.
 #include <cuda.h>
@@ -48,15 +54,14 @@ constexpr int D = 128;          // head dim
 constexpr int BQ = 128;         // query rows per CTA
 constexpr int BKV = 64;         // key rows per block
 constexpr int KST = 2;          // K ring stages
-constexpr int VST = 1;          // V ring stages
+constexpr int VST = 2;          // V ring stages
 constexpr int THREADS = 224;
 constexpr int HEAD_GROUP = 16;   // heads per group of the CTA order (16 MiB of K/V at S=2048)
 constexpr int Q_HALF = BQ * 64 * 2;             // 16 KiB: 128 rows x 64 columns
 constexpr int Q_BYTES = 2 * Q_HALF;             // 32 KiB
 constexpr int KV_HALF = BKV * 64 * 2;           // 8 KiB: 64 rows x 64 columns
 constexpr int KV_BYTES = 2 * KV_HALF;           // 16 KiB: 64 rows x 128 columns
-constexpr int P_BYTES = BQ * BKV * 2;           // 16 KiB: 128 rows x 64 keys
-constexpr int TILE_BYTES = Q_BYTES + (KST + VST) * KV_BYTES + 2 * P_BYTES;   // Phi, Plo
+constexpr int TILE_BYTES = Q_BYTES + (KST + VST) * KV_BYTES;
 constexpr int ALIGN_SLACK = 896;
 constexpr int MAX_TILES = 32;   // 128-row tiles of a sequence in a partial call (seq <= 4096)
 
@@ -138,8 +143,6 @@ __global__ void __launch_bounds__(THREADS, 2)
   const uint32_t sQ = base;
   const uint32_t sK = base + Q_BYTES;
   const uint32_t sV = sK + KST * KV_BYTES;
-  const uint32_t sP = sV + VST * KV_BYTES;
-  const uint32_t sPl = sP + P_BYTES;
   Bars& B = *reinterpret_cast<Bars*>(smem_raw + (base - raw) + TILE_BYTES);
   volatile int* abort = &B.abort_flag;
 
@@ -262,14 +265,16 @@ __global__ void __launch_bounds__(THREADS, 2)
         if (!mbar_wait(smem_u32(&B.v_full[vs]), (j / VST) & 1, abort)) break;
         tc_fence_after();
         const uint32_t vb = sV + vs * KV_BYTES;
-        // O += Phi V + Plo V: the K steps of both halves read the same V rows
+        // O += Phi V + Plo V: A from TMEM (S_j's columns: Phi 0..31, Plo
+        // 32..63, 8 columns per 16 keys); the K steps of both halves read the
+        // same V rows
+        const uint32_t pbuf = tmem + (uint32_t)((j & 1) * BKV);
 #pragma unroll
         for (int kk = 0; kk < 2 * (BKV / 16); ++kk) {
-          const uint32_t pt = kk < BKV / 16 ? sP : sPl;
-          const uint64_t ad = sdesc_sw128(pt + (kk & 3) * 32, 16, 1024);
+          const uint32_t at = pbuf + (uint32_t)((kk >> 2) * 32 + (kk & 3) * 8);
           const uint64_t bd = sdesc_sw128(vb + (kk & 3) * 16 * 128, KV_HALF, 1024);
           // a partial call after the first adds onto the carried O
-          mma_f16(tmem + O_COL, ad, bd, idesc_pv, (j | kk) != 0 || !first);
+          mma_f16_ts(tmem + O_COL, at, bd, idesc_pv, (j | kk) != 0 || !first);
         }
         mma_commit(smem_u32(&B.pv_done));
         mma_commit(smem_u32(&B.v_empty[vs]));
@@ -362,17 +367,19 @@ __global__ void __launch_bounds__(THREADS, 2)
 #pragma unroll
         for (int i = 0; i < h; ++i) s8[i] += s8[i + h];
       l_run += s8[0];
-      // PV_{j-1} has read the P tile and finished adding into O (at j = 0 of a
-      // call that carries state, O holds the carried values and may need the
-      // same rescale)
-      if (j >= 1 || !first) {
+      // a rescale of O waits for PV_{j-1} to finish adding into O (at j = 0
+      // of a call that carries state, O holds the carried values and may need
+      // the same rescale)
+      bool waited = false;
+      if ((j >= 1 || !first) && __any_sync(0xffffffffu, rescale)) {
         if (j >= 1) {
           const bool ok = __all_sync(0xffffffffu,
                                      mbar_wait(smem_u32(&B.pv_done), (j - 1) & 1, abort));
           tc_fence_after();
           if (!ok) break;
+          waited = true;
         }
-        if (__any_sync(0xffffffffu, rescale)) {
+        {
 #pragma unroll 1
           for (int c = 0; c < D; c += 32) {
             uint32_t r[32];
@@ -383,24 +390,21 @@ __global__ void __launch_bounds__(THREADS, 2)
           }
         }
       }
-      // Phi_j, Plo_j: row tid of each K-major tile, 128-byte swizzle (chunk u
-      // at u ^ (row & 7))
-      {
-        const uint32_t rowaddr = sP + tid * 128;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint32_t dst = rowaddr + ((u ^ (tid & 7)) << 4);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(ph[4 * u]),
-                       "r"(ph[4 * u + 1]), "r"(ph[4 * u + 2]), "r"(ph[4 * u + 3])
-                       : "memory");
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst + P_BYTES),
-                       "r"(pl[4 * u]), "r"(pl[4 * u + 1]), "r"(pl[4 * u + 2]), "r"(pl[4 * u + 3])
-                       : "memory");
-        }
-      }
-      fence_proxy_async();
+      // Phi_j, Plo_j over S_j's columns of this warp's lanes (S_j is in
+      // registers); the stores complete before the arrival (tcgen05.wait::st)
+      const uint32_t pcol = tmem + lane_base + (uint32_t)((j & 1) * BKV);
+      tmem_st32_wait(pcol, ph);
+      tmem_st32_wait(pcol + 32, pl);
       tc_fence_before();
       mbar_arrive(smem_u32(&B.p_full));
+      // keep in step with the PV products: PV_{j-1} completes before S_{j+1}
+      // (issued after it), which this warp waits for next anyway
+      if (j >= 1 && !waited) {
+        const bool ok = __all_sync(0xffffffffu,
+                                   mbar_wait(smem_u32(&B.pv_done), (j - 1) & 1, abort));
+        tc_fence_after();
+        if (!ok) break;
+      }
     }
     const bool done =
         !*abort && (n_kv == 0 || mbar_wait(smem_u32(&B.pv_done), (n_kv - 1) & 1, abort));

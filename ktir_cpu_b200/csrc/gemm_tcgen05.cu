@@ -190,6 +190,191 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0 && abort_flag) atomicOr(p.status, KTIR_STATUS_TIMEOUT);
 }
 
+// ---------------------------------------------------------------------------
+// GEMM of any shape with the reference's rounding of each K block: KTIR that
+// multiplies f16 tiles without widening them first gets each block product
+// as an f16 tile (NumPy's f16 matmul: the sum in f32, one f16 rounding) and
+// adds it to an f16 or f32 running sum (ktir_cpu/dialects/linalg_ops.py:273-297
+// with ops/arith_ops.py:403-419).  One CTA per 128x128 output tile: warp 0
+// streams A (64 k x 128 m) and B (two 64 n x 64 k boxes) through a 4-stage TMA
+// ring (rows, columns and k past the matrix read as zero), warp 1 issues the
+// block's tcgen05.mma (M128 N128 K16) into one of two TMEM buffers and
+// commits each finished block, warps 2..5 round each block product to f16
+// and add it to their rows' running sums in registers while the next block
+// accumulates in the other buffer, then store the rows and columns inside C.
+// block_k = 0: one block of all of K (one f16 rounding at the end, the
+// product of f16 tiles widened to f32).
+constexpr int GB_BM = 128, GB_BN = 128, GB_BK = 64, GB_STAGES = 4;
+constexpr int GB_A_BYTES = GB_BM * GB_BK * 2;          // 16 KiB
+constexpr int GB_B_BYTES = GB_BK * GB_BN * 2;          // 16 KiB
+constexpr int GB_STAGE_BYTES = GB_A_BYTES + GB_B_BYTES;
+constexpr int GB_SMEM_BYTES = GB_STAGES * GB_STAGE_BYTES + 1024;
+constexpr uint32_t GB_TMEM_COLS = 256;                 // two 128-column block products
+
+struct GemmBlockedParams {
+  __half* c;
+  long long ldc;
+  int m, n, k;
+  int block_steps;   // 16-wide k steps per block
+  int round_blocks;  // each block product rounded to f16 (else one block, widened operands)
+  int acc_f16;       // running sum rounded to f16 after each block
+  int* status;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    k_gemm_blocked(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                   const __grid_constant__ GemmBlockedParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[GB_STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[GB_STAGES];
+  __shared__ __align__(8) uint64_t x_full[2];
+  __shared__ __align__(8) uint64_t x_empty[2];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t smem = (raw + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * GB_BM;
+  const int n0 = blockIdx.y * GB_BN;
+  const int KT = (p.k + GB_BK - 1) / GB_BK;
+  const int n_steps = (p.k + 15) / 16;
+  const int spb = p.block_steps;
+  const int n_blocks = (n_steps + spb - 1) / spb;
+  volatile int* abort = &abort_flag;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < GB_STAGES; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&x_full[b]), 1);
+      mbar_init(smem_u32(&x_empty[b]), 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&tmem_base), GB_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&ta);
+      tma_prefetch_desc(&tb);
+      for (int kt = 0; kt < KT && !*abort; ++kt) {
+        const int s = kt % GB_STAGES;
+        if (!mbar_wait(smem_u32(&empty_bar[s]), ((kt / GB_STAGES) & 1) ^ 1, abort)) break;
+        const uint32_t fb = smem_u32(&full_bar[s]);
+        mbar_arrive_expect_tx(fb, GB_STAGE_BYTES);
+        const uint32_t a_dst = smem + s * GB_STAGE_BYTES;
+        const uint32_t b_dst = a_dst + GB_A_BYTES;
+        tma_load_2d(a_dst, &ta, fb, kt * GB_BK, m0);
+        tma_load_2d(b_dst, &tb, fb, n0, kt * GB_BK);
+        tma_load_2d(b_dst + B_BOX_BYTES, &tb, fb, n0 + 64, kt * GB_BK);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(GB_BM, GB_BN, 0, 1);
+      bool ok = true;
+      for (int kt = 0; kt < KT && ok; ++kt) {
+        const int s = kt % GB_STAGES;
+        if (!mbar_wait(smem_u32(&full_bar[s]), (kt / GB_STAGES) & 1, abort)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem + s * GB_STAGE_BYTES;
+        const uint32_t b_addr = a_addr + GB_A_BYTES;
+        for (int kk = 0; kk < GB_BK / 16; ++kk) {
+          const int step = kt * (GB_BK / 16) + kk;
+          if (step >= n_steps) break;
+          const int blk = step / spb;
+          const int in_blk = step - blk * spb;
+          const uint32_t xb = (uint32_t)(blk & 1);
+          if (in_blk == 0 && blk >= 2) {
+            // the epilogue has read block blk - 2 out of this buffer
+            if (!mbar_wait(smem_u32(&x_empty[xb]), ((blk - 2) >> 1) & 1, abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+          const uint64_t ad = sdesc_sw128(a_addr + kk * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(b_addr + kk * 16 * 128, B_BOX_BYTES, 1024);
+          mma_f16(tmem + xb * GB_BN, ad, bd, idesc, in_blk != 0);
+          if (in_blk == spb - 1 || step == n_steps - 1) mma_commit(smem_u32(&x_full[xb]));
+        }
+        mma_commit(smem_u32(&empty_bar[s]));
+      }
+    }
+  } else {
+    // epilogue warps 2..5: warp w reads TMEM lanes 32*(w%4) .. +31 (rows)
+    const int q = warp & 3;
+    const int row = 32 * q + lane;
+    float acc[GB_BN];
+#pragma unroll
+    for (int i = 0; i < GB_BN; ++i) acc[i] = 0.f;
+    bool ok = true;
+    for (int blk = 0; blk < n_blocks; ++blk) {
+      const uint32_t xb = (uint32_t)(blk & 1);
+      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&x_full[xb]), (blk >> 1) & 1, abort));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t x = tmem + ((uint32_t)(32 * q) << 16) + xb * GB_BN;
+#pragma unroll
+      for (int c = 0; c < GB_BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32_wait(x + c, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float v = __uint_as_float(r[i]);
+          if (!p.round_blocks) {
+            acc[c + i] = 0.f + v;            // one block of all of K, widened operands
+          } else {
+            const float b16 = __half2float(__float2half_rn(v));   // the block's f16 product
+            const float s = acc[c + i] + b16;
+            acc[c + i] = p.acc_f16 ? __half2float(__float2half_rn(s)) : s;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&x_empty[xb]));
+    }
+    if (ok && m0 + row < p.m) {
+      __half* crow = p.c + (long long)(m0 + row) * p.ldc;
+      const bool vec = (p.ldc & 7) == 0 && ((reinterpret_cast<uintptr_t>(p.c) & 15) == 0);
+#pragma unroll
+      for (int c = 0; c < GB_BN; c += 8) {
+        const int col = n0 + c;
+        if (vec && col + 8 <= p.n) {
+          __half2 h[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(acc[c + 2 * j], acc[c + 2 * j + 1]);
+          *reinterpret_cast<uint4*>(crow + col) = *reinterpret_cast<const uint4*>(h);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (col + j < p.n) crow[col + j] = __float2half_rn(acc[c + j]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, GB_TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && abort_flag) atomicOr(p.status, KTIR_STATUS_TIMEOUT);
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -265,5 +450,43 @@ extern "C" int ktir_gemm_f16(const KtirGemmDesc* d, void* stream) {
   if (tiles > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
   const unsigned grid = (unsigned)(tiles < n_sm ? tiles : n_sm);
   k_gemm_tcgen05<<<grid, 192, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  return cudaGetLastError() == cudaSuccess ? KTIR_OK : KTIR_ERR_CUDA;
+}
+
+extern "C" int ktir_gemm_f16_blocked(const KtirGemmBlockedDesc* d, void* stream) {
+  if (!d || !d->a || !d->b || !d->c || !d->status) return KTIR_ERR_ARG;
+  if (d->m < 1 || d->n < 1 || d->k < 1 || d->block_k < 0 || (d->block_k & 15))
+    return KTIR_ERR_UNSUPPORTED;
+  if (d->m > 0x7fffffffLL || d->n > 0x7fffffffLL || d->k > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(d->a) | reinterpret_cast<uintptr_t>(d->b)) & 15)
+    return KTIR_ERR_UNSUPPORTED;
+  if ((d->lda | d->ldb) & 7 || d->lda < d->k || d->ldb < d->n || d->ldc < d->n)
+    return KTIR_ERR_UNSUPPORTED;
+  const long long gy = (d->n + GB_BN - 1) / GB_BN, gx = (d->m + GB_BM - 1) / GB_BM;
+  if (gy > 65535 || gx > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
+  CUtensorMap ta, tb;
+  if (!make_map(&ta, d->a, d->m, d->k, d->lda, 64, GB_BM) ||
+      !make_map(&tb, d->b, d->k, d->n, d->ldb, 64, GB_BK))
+    return KTIR_ERR_CUDA;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(k_gemm_blocked, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             GB_SMEM_BYTES) != cudaSuccess)
+      return KTIR_ERR_CUDA;
+    attr = true;
+  }
+  GemmBlockedParams p;
+  p.c = static_cast<__half*>(d->c);
+  p.ldc = d->ldc;
+  p.m = (int)d->m;
+  p.n = (int)d->n;
+  p.k = (int)d->k;
+  const int n_steps = (int)((d->k + 15) / 16);
+  p.block_steps = d->block_k ? (int)(d->block_k / 16) : n_steps;
+  p.round_blocks = d->block_k ? 1 : 0;
+  p.acc_f16 = d->acc_f16 ? 1 : 0;
+  p.status = static_cast<int*>(d->status);
+  k_gemm_blocked<<<dim3((unsigned)gx, (unsigned)gy), 192, GB_SMEM_BYTES,
+                   static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   return cudaGetLastError() == cudaSuccess ? KTIR_OK : KTIR_ERR_CUDA;
 }

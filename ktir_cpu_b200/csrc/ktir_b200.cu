@@ -847,6 +847,78 @@ __global__ void __launch_bounds__(256) k_rmw_apply(const __grid_constant__ KtirG
   }
 }
 
+// Phase 2 for the common y = x op imm on f16 rows: an 8-lane group owns one
+// index position and each lane moves two 16-byte vectors of the row (loads of
+// both issued before either store), so twice as many row bytes are in flight
+// per thread as with one vector per lane; f16 pairs as in k_rmw_apply.
+template <int SOP>
+__global__ void __launch_bounds__(256) k_rmw_apply_pairs(const __grid_constant__ KtirGatherRmwDesc d,
+                                                         const __grid_constant__ KtirBuffers b,
+                                                         int* __restrict__ counts, int64_t n_rows,
+                                                         float simple_imm) {
+  pdl_prologue();
+  const int sub = threadIdx.x & 7;
+  const int group = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 3);
+  const int ngroups = (int)((gridDim.x * blockDim.x) >> 3);
+  const int total = d.n_units * d.unit_len;
+  const bool dense_units = d.idx_unit_stride == d.unit_len;
+  const int64_t row_lo = d.row_hi > 0 ? d.row_lo : 0;
+  const int64_t row_hi = d.row_hi > 0 ? d.row_hi : n_rows;
+  __half* table = (__half*)b.base[d.table_slot];
+  const int64_t tnumel = b.numel[d.table_slot];
+  const __half2 imm2 = __float2half2_rn(simple_imm);
+  const unsigned gmask = 0xffu << (threadIdx.x & 24);
+  for (int g = group; g < total; g += ngroups) {
+    int64_t pos;
+    if (dense_units) {
+      pos = d.idx_off + g;
+    } else {
+      const int unit = g / d.unit_len;
+      pos = d.idx_off + (int64_t)unit * d.idx_unit_stride + (g - unit * d.unit_len);
+    }
+    const int64_t row = read_index(b, d.idx_slot, d.idx_dtype, pos);
+    int m = 0;
+    if (sub == 0 && row >= 0 && row < n_rows) m = atomicExch(&counts[row], 0);
+    m = __shfl_sync(gmask, m, 0, 8);
+    if (m <= 0 || row < row_lo || row >= row_hi) continue;
+    const int64_t rb = d.table_off + row * d.row_stride;
+    for (int c0 = sub * 16; c0 < d.row_len; c0 += 128) {
+      uint4 raw[2];
+      bool vec[2];
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        const int c = c0 + 8 * v;
+        const int64_t e = rb + c;
+        vec[v] = (c + 8 <= d.row_len) && ((e & 7) == 0) && (e + 8 <= tnumel) && e >= 0;
+        if (vec[v]) raw[v] = *reinterpret_cast<const uint4*>(table + e);
+      }
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        const int c = c0 + 8 * v;
+        const int64_t e = rb + c;
+        if (vec[v]) {
+          __half2* h2 = reinterpret_cast<__half2*>(&raw[v]);
+          for (int rep = 0; rep < m; ++rep) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              h2[q] = SOP == OP_FADD ? __hadd2(h2[q], imm2)
+                                     : (SOP == OP_FSUB ? __hsub2(h2[q], imm2) : __hmul2(h2[q], imm2));
+          }
+          *reinterpret_cast<uint4*>(table + e) = raw[v];
+        } else {
+          // a ragged or unaligned stretch: element by element, f32 op rounded to f16
+          for (int k = 0; k < 8; ++k) {
+            if (c + k >= d.row_len || e + k < 0 || e + k >= tnumel) continue;
+            float x = __half2float(table[e + k]);
+            for (int rep = 0; rep < m; ++rep) x = __half2float(__float2half_rn(binf(SOP, x, simple_imm)));
+            table[e + k] = __float2half_rn(x);
+          }
+        }
+      }
+    }
+  }
+}
+
 extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* d, const KtirBuffers* bufs, int32_t* counts,
                                int64_t n_rows, int32_t* status, void* stream) {
   if (!d || !bufs || !counts || !status) return set_err(KTIR_ERR_ARG, "ktir_gather_rmw: null argument");
@@ -887,15 +959,16 @@ extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* d, const KtirBuffers* bu
   }
   const int64_t groups = (int64_t)d->n_units * d->unit_len;
   const int blocks = grid_x(groups * 16, 256, 148 * 64);
+  const int blocks8 = grid_x(groups * 8, 256, 148 * 64);
   switch (simple_op) {
     case OP_FADD:
-      launch_pdl(k_rmw_apply<OP_FADD>, dim3(blocks), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
+      launch_pdl(k_rmw_apply_pairs<OP_FADD>, dim3(blocks8), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
       break;
     case OP_FSUB:
-      launch_pdl(k_rmw_apply<OP_FSUB>, dim3(blocks), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
+      launch_pdl(k_rmw_apply_pairs<OP_FSUB>, dim3(blocks8), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
       break;
     case OP_FMUL:
-      launch_pdl(k_rmw_apply<OP_FMUL>, dim3(blocks), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
+      launch_pdl(k_rmw_apply_pairs<OP_FMUL>, dim3(blocks8), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
       break;
     default:
       launch_pdl(k_rmw_apply<0>, dim3(blocks), dim3(256), 0, s, *d, *bufs, counts, n_rows, 0.f);

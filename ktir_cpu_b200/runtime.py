@@ -113,6 +113,13 @@ class KtirFmhaDesc(C.Structure):
                 ("causal", C.c_int32), ("row_stride", C.c_int64), ("status", C.c_void_p)]
 
 
+class KtirGemmBlockedDesc(C.Structure):
+    _fields_ = [("a", C.c_void_p), ("b", C.c_void_p), ("c", C.c_void_p),
+                ("lda", C.c_int64), ("ldb", C.c_int64), ("ldc", C.c_int64),
+                ("m", C.c_int64), ("n", C.c_int64), ("k", C.c_int64),
+                ("block_k", C.c_int32), ("acc_f16", C.c_int32), ("status", C.c_void_p)]
+
+
 class KtirFmhaPartDesc(C.Structure):
     _fields_ = [("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("o", C.c_void_p),
                 ("bh", C.c_int64), ("seq", C.c_int64), ("d", C.c_int64), ("kv_rows", C.c_int64),
@@ -134,7 +141,7 @@ class KtirHostCopy(C.Structure):
 
 EXPORTS = ["ktir_version", "ktir_last_error", "ktir_device_count", "ktir_ew",
            "ktir_softmax_rows", "ktir_gather_rmw", "ktir_reduce", "ktir_matmul",
-           "ktir_offsets", "ktir_indirect", "ktir_gemm_f16", "ktir_fmha_f16",
+           "ktir_offsets", "ktir_indirect", "ktir_gemm_f16", "ktir_gemm_f16_blocked", "ktir_fmha_f16",
            "ktir_fmha_f16_part", "ktir_copy_blocks", "ktir_pack_kv", "ktir_bytes_delta",
            "ktir_wait_selftest", "ktir_host_threads", "ktir_host_upload", "ktir_host_download"]
 
@@ -172,6 +179,7 @@ def load_library(build_if_missing: bool = False) -> C.CDLL:
     lib.ktir_indirect.argtypes = [C.POINTER(KtirIndirectDesc), C.POINTER(KtirBuffers), vp, vp,
                                   vp, vp, vp]
     lib.ktir_gemm_f16.argtypes = [C.POINTER(KtirGemmDesc), vp]
+    lib.ktir_gemm_f16_blocked.argtypes = [C.POINTER(KtirGemmBlockedDesc), vp]
     lib.ktir_fmha_f16.argtypes = [C.POINTER(KtirFmhaDesc), vp]
     lib.ktir_fmha_f16_part.argtypes = [C.POINTER(KtirFmhaPartDesc), vp]
     lib.ktir_copy_blocks.argtypes = [vp, C.c_int64, vp, C.c_int64, C.c_int64, C.c_int64, vp]

@@ -1,14 +1,22 @@
 """Tensor-core programs: GEMM and attention matchers over the traced graph.
 
-GEMM: every store must be ``truncf(acc_K)`` with ``acc_k = acc_{k-1} +
-extf(A_k) @ extf(B_k)`` (the K loop of ``linalg.matmul`` with an f32
-iter_arg accumulator, ktir_cpu/dialects/linalg_ops.py:273-297), starting from
-a zero constant, where the A_k / B_k loads sweep K contiguously, and the
-stores must tile the output matrix exactly.  The whole call then becomes one
-tcgen05 GEMM launch over C = A @ B (f32 accumulation, f16 store).  Numerics:
-the reference accumulates per 128-wide K tile in OpenBLAS order; the tensor
-cores accumulate the full K in their own order — equal within the stated
-tolerance, not bit-exact.
+GEMM: every store must be the K loop of ``linalg.matmul`` over one output
+tile, starting from a zero constant, with the A_k / B_k loads sweeping K
+contiguously, and the stores must tile one rectangle of C exactly.  Two
+forms (ktir_cpu/dialects/linalg_ops.py:273-297, ops/arith_ops.py:403-419):
+
+* widened: ``truncf(acc_K)``, ``acc_k = acc_{k-1} + extf(A_k) @ extf(B_k)``
+  (f32 tiles, f32 accumulator): one f32 sum over all of K, rounded once;
+* f16 products: ``acc_k = acc_{k-1} + A_k @ B_k`` with f16 tiles, where
+  NumPy rounds each block product to f16 and the accumulator is f16 (each
+  sum rounded) or f32 (the reference's matmul_fwd example, and matmuls of
+  f16 tiles into f32 outs).
+
+The whole call becomes one tcgen05 GEMM launch: the aligned persistent
+kernel for widened tilings of 128 x 256 x 64 multiples, else the blocked
+kernel (any shape, per-block rounding).  Numerics: the reference sums each
+tile in OpenBLAS / NumPy order, the tensor cores in their own order — equal
+within the stated tolerance, not bit-exact.
 
 Attention: see :mod:`ktir_cpu_b200.rewrite`.
 """
@@ -36,38 +44,74 @@ def _rect2d(n) -> bool:
         len(n.shape) == 2 and n.attrs["strides"][1] == 1
 
 
+def _is_zero(n) -> bool:
+    return isinstance(n, Node) and n.kind == "const" and float(n.attrs["value"]) == 0.0
+
+
+def _block_term(n):
+    """(kind, A load, B load) when n is one K block's product: "wide" for
+    extf(A) @ extf(B), "f16" for A @ B of f16 tiles (rounded to f16)."""
+    if not (isinstance(n, Node) and n.kind == "matmul"):
+        return None
+    a, b = n.ins
+    if _is_cast(a, np.float16, np.float32) and _is_cast(b, np.float16, np.float32) and \
+            _rect2d(a.ins[0]) and _rect2d(b.ins[0]):
+        return "wide", a.ins[0], b.ins[0]
+    if n.dtype == np.float16 and _rect2d(a) and _rect2d(b) and \
+            a.dtype == np.float16 and b.dtype == np.float16:
+        return "f16", a, b
+    return None
+
+
 def gemm_chain(store: Store):
-    """(i0, j0, bm, bn, [(A load, B load), ...]) for one output tile, or None."""
+    """(i0, j0, bm, bn, [(A load, B load), ...], kind, accumulator dtype) for
+    one output tile, or None."""
     t = store.target
     if not isinstance(t, RectTarget) or len(t.shape) != 2 or t.strides[1] != 1 or \
             t.dtype != np.float16:
         return None
     root = store.value
-    if not _is_cast(root, np.float32, np.float16):
+    if _is_cast(root, np.float32, np.float16):
+        acc, acc_dt = root.ins[0], np.dtype(np.float32)
+    elif isinstance(root, Node) and root.dtype == np.float16:
+        acc, acc_dt = root, np.dtype(np.float16)
+    else:
         return None
-    acc = root.ins[0]
-    pairs = []
-    while isinstance(acc, Node) and acc.kind == "ew" and acc.attrs.get("matmul_accumulate"):
-        prev, mm = acc.ins
-        if not (isinstance(mm, Node) and mm.kind == "matmul"):
+    pairs, kinds = [], set()
+    while not _is_zero(acc):
+        if not (isinstance(acc, Node) and acc.kind == "ew" and acc.attrs.get("op") == "add" and
+                acc.dtype == acc_dt and len(acc.ins) == 2):
             return None
-        a, b = mm.ins
-        if not (_is_cast(a, np.float16, np.float32) and _is_cast(b, np.float16, np.float32)):
+        prev, term = acc.ins
+        if acc.attrs.get("matmul_accumulate"):
+            bt = _block_term(term)                       # outs + A @ B
+        else:
+            # acc + (empty + A @ B): the block product added to the running sum
+            if _block_term(prev) is not None or (isinstance(prev, Node) and
+                                                 prev.attrs.get("matmul_accumulate")):
+                prev, term = term, prev
+            inner = term
+            if isinstance(term, Node) and term.kind == "ew" and term.attrs.get("matmul_accumulate") \
+                    and _is_zero(term.ins[0]):
+                inner = term.ins[1]
+            bt = _block_term(inner)
+            if bt is not None and bt[0] != "f16":
+                return None
+        if bt is None:
             return None
-        la, lb = a.ins[0], b.ins[0]
-        if not (_rect2d(la) and _rect2d(lb)):
-            return None
-        pairs.append((la, lb))
+        kinds.add(bt[0])
+        pairs.append((bt[1], bt[2]))
         acc = prev
-    if not (isinstance(acc, Node) and acc.kind == "const" and float(acc.attrs["value"]) == 0.0):
+    if not pairs or len(kinds) != 1:
         return None
-    if not pairs:
+    kind = kinds.pop()
+    if kind == "wide" and acc_dt != np.float32:
         return None
     pairs.reverse()
     ldc = t.strides[0]
     i0, j0 = divmod(t.off, ldc)
     bm, bn = t.shape
-    return i0, j0, bm, bn, pairs
+    return i0, j0, bm, bn, pairs, kind, acc_dt
 
 
 def match_gemm(low, stores: List[Store]):
@@ -77,11 +121,18 @@ def match_gemm(low, stores: List[Store]):
     abuf = bbuf = cbuf = None
     lda = ldb = ldc = None
     K = None
+    mode = None
     for s in stores:
         ch = gemm_chain(s)
         if ch is None:
             return None
-        i0, j0, bm, bn, pairs = ch
+        i0, j0, bm, bn, pairs, kind, acc_dt = ch
+        widths = {la.shape[1] for la, _ in pairs}
+        m = (kind, acc_dt, widths.pop() if len(widths) == 1 else None)
+        if mode is None:
+            mode = m
+        elif mode != m:
+            return None
         la0, lb0 = pairs[0]
         if abuf is None:
             abuf, bbuf, cbuf = la0.attrs["buf"], lb0.attrs["buf"], s.target.buf
@@ -110,7 +161,7 @@ def match_gemm(low, stores: List[Store]):
         return None
     Mfull = cbuf.numel // ldc
     Nfull = ldc
-    if lda != K or abuf.numel != Mfull * K or bbuf.numel != K * Nfull or ldb != Nfull:
+    if abuf.numel != Mfull * lda or lda < K or bbuf.numel < K * ldb or ldb < Nfull:
         return None
     # the stores must tile one rectangle of C exactly (all of C, or the block
     # a shard of the core grid owns)
@@ -129,11 +180,33 @@ def match_gemm(low, stores: List[Store]):
             cover[i0 - i_lo:i0 - i_lo + bm, j0 - j_lo:j0 - j_lo + bn] += 1
     if area != M * N or (cover is not None and not np.all(cover == 1)):
         return None
-    if M % GEMM_TILE_M or N % GEMM_TILE_N or K % GEMM_TILE_K:
-        return None
     lib = R.load_library()
     sa, sb, sc = low.slots[abuf.index], low.slots[bbuf.index], low.slots[cbuf.index]
     a_off, b_off, c_off = i_lo * lda * 2, j_lo * 2, (i_lo * ldc + j_lo) * 2
+    kind, acc_dt, width = mode
+    from .lower import Launch, Plan
+    aligned = not (M % GEMM_TILE_M or N % GEMM_TILE_N or K % GEMM_TILE_K) and lda == K and \
+        ldb == Nfull
+    if kind != "wide" or not aligned:
+        # f16 block products (rounded per block), or a shape the aligned kernel does not take
+        block_k = 0 if kind == "wide" else width
+        if block_k is None or block_k % 16 or lda % 8 or ldb % 8 or \
+                (a_off | b_off) % 16:
+            return None
+
+        def run_blocked(bufs, stream, status):
+            d = R.KtirGemmBlockedDesc()
+            d.a, d.b, d.c = bufs.base[sa] + a_off, bufs.base[sb] + b_off, bufs.base[sc] + c_off
+            d.lda, d.ldb, d.ldc = lda, ldb, ldc
+            d.m, d.n, d.k = M, N, K
+            d.block_k = block_k
+            d.acc_f16 = 1 if acc_dt == np.float16 else 0
+            d.status = status
+            R.check(lib.ktir_gemm_f16_blocked(C.byref(d), stream), "ktir_gemm_f16_blocked")
+        plan = Plan("gemm", [Launch(run_blocked, "gemm_blocked")], [], status_check=True)
+        plan.info.update(m=M, n=N, k=K, tiles=len(tiles), flops=2 * M * N * K, block_k=block_k,
+                         acc=str(acc_dt))
+        return plan
 
     def run(bufs, stream, status):
         d = R.KtirGemmDesc()
@@ -144,7 +217,6 @@ def match_gemm(low, stores: List[Store]):
         d.status = status
         R.check(lib.ktir_gemm_f16(C.byref(d), stream), "ktir_gemm_f16")
 
-    from .lower import Launch, Plan
     plan = Plan("gemm", [Launch(run, "gemm")], [], status_check=True)
     plan.info.update(m=M, n=N, k=K, tiles=len(tiles), flops=2 * M * N * K)
     return plan

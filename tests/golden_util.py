@@ -105,7 +105,7 @@ def assert_matches(name, got, want, tol):
 U32 = 2.0 ** -24
 
 
-def assert_contraction(name, got, want, mag, tol=1e-2, c=8.0):
+def assert_contraction(name, got, want, mag, tol=1e-2, c=8.0, u=None):
     """Parity rule for f16 outputs of an f32-accumulated contraction (matmul,
     attention) against a reference computed exactly (float64) or by another f32
     order of accumulation.
@@ -117,11 +117,14 @@ def assert_contraction(name, got, want, mag, tol=1e-2, c=8.0):
     below ~1e-4 of their terms, which no f32 implementation -- the reference's
     NumPy/OpenBLAS one included -- reproduces to 1e-2 relative.  The true max
     relative error (no noise term) and the number of outputs above tol are
-    reported beside it; returns (max rel err, count above tol, max f16 ulp)."""
+    reported beside it; returns (max rel err, count above tol, max f16 ulp).
+    For sums of f16-rounded block products the noise is that of f16 (u = 2^-11)
+    times the sum of the block products' magnitudes."""
     g = got.astype(np.float64)
     w = want.astype(np.float64)
     err = np.abs(g - w)
-    bound = tol * np.maximum(np.abs(w), F16_TINY) + c * U32 * mag.astype(np.float64)
+    bound = tol * np.maximum(np.abs(w), F16_TINY) + c * (U32 if u is None else u) * \
+        mag.astype(np.float64)
     rel, n_bad, ulp = err_report(got, want, tol)
     worst = float(np.max(err / bound)) if err.size else 0.0
     print(f"{name}: max rel err {rel:.3e} ({n_bad} of {w.size} outputs above {tol}), "
@@ -213,9 +216,15 @@ def digest_of(a):
 
 
 def example_mag(name, inputs):
-    """sum |a b| per output for the examples whose outputs are matmul results."""
-    if "matmul" in name:
-        a = np.abs(inputs["a_ptr"].astype(np.float64))
-        b = np.abs(inputs["b_ptr"].astype(np.float64))
-        return {"c_ptr": a @ b}
-    return {}
+    """({output: magnitude}, u) for the examples whose outputs are matmul
+    results: they multiply f16 tiles, so each K block's product is rounded to
+    f16 (u = 2^-11) and the magnitude is the sum over blocks of |A_blk @ B_blk|."""
+    if "matmul" not in name:
+        return {}, None
+    a = inputs["a_ptr"].astype(np.float64)
+    b = inputs["b_ptr"].astype(np.float64)
+    bk = int(inputs["BLOCK_SIZE_K"])
+    mag = np.zeros((a.shape[0], b.shape[1]))
+    for k0 in range(0, a.shape[1], bk):
+        mag += np.abs(a[:, k0:k0 + bk] @ b[k0:k0 + bk])
+    return {"c_ptr": mag}, 2.0 ** -11

@@ -14,7 +14,7 @@ HEADER = os.path.join(ROOT, "include", "ktir_b200.h")
 
 STRUCTS = ["KtirBuffers", "KtirView", "KtirInstr", "KtirEwProgram", "KtirSoftmaxDesc",
            "KtirGatherRmwDesc", "KtirReduceDesc", "KtirMatmulDesc", "KtirOffsetsDesc",
-           "KtirIndirectDesc", "KtirGemmDesc", "KtirFmhaDesc", "KtirFmhaPartDesc", "KtirHostXfer",
+           "KtirIndirectDesc", "KtirGemmDesc", "KtirGemmBlockedDesc", "KtirFmhaDesc", "KtirFmhaPartDesc", "KtirHostXfer",
            "KtirHostCopy"]
 
 

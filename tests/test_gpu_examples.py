@@ -33,7 +33,7 @@ def test_b200_runs_reference_example(name):
         out = run_seeded(interp, g)
     else:
         out = interp.execute_function(g["func"], **kw)
-    mags = example_mag(name, g["inputs"])
+    mags, u = example_mag(name, g["inputs"])
     want = dict(g["outputs"])
     if g["digests"]:
         o = OracleInterpreter()
@@ -43,6 +43,6 @@ def test_b200_runs_reference_example(name):
         want.update({k: ref[k] for k in g["digests"]})
     for k, w in want.items():
         if k in mags and g["tol"] is not None:
-            assert_contraction(f"{name}:{k}", out[k], w, mags[k], g["tol"])
+            assert_contraction(f"{name}:{k}", out[k], w, mags[k], g["tol"], u=u)
         else:
             assert_matches(f"{name}:{k}", out[k], w, g["tol"])

@@ -109,3 +109,13 @@ def test_vector_add_batched_executions_bitexact():
     torch.cuda.synchronize()
     out = ts[2].cpu().numpy().view(np.float16).reshape(n, 1024)
     assert np.array_equal(out, x + y)
+
+
+def test_gemm_odd_shape_uses_tensor_cores():
+    """A GEMM tiling the aligned kernel does not take (192 x 320 x 96, K in
+    32-wide steps) runs on the blocked tcgen05 kernel, against the oracle."""
+    p = dict(m=192, n=320, k=96, grid=(2, 2), sub=(96, 160), bk=32)
+    kw, got, want, dev = _run_both("gemm", **p)
+    plan = dev.last_executable.plan
+    assert plan.kind == "gemm" and plan.launches[0].kind == "gemm_blocked"
+    assert_contraction("c", got["c_ptr"], want["c_ptr"], contraction_mag("gemm", kw)["c_ptr"], 1e-2)
