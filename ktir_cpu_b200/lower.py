@@ -1146,6 +1146,25 @@ class GenericExecutor:
             return mkview(dst.slot, dst_dtype if dst_dtype is not None else dst.dtype, dst.off, st)
         self._launch_ew(program(b, shape, 1, 0, vf))
 
+    def _offsets(self, dense: _Val, tile: _Val, positions: np.ndarray, scatter: bool) -> None:
+        """Gather tile[positions] into dense, or scatter dense into
+        tile[positions]; both are dense arena values."""
+        if positions.size == 0:
+            return
+        optr = self.low.dev.i64(positions)
+        d = R.KtirOffsetsDesc()
+        d.buf = mkview(R.ARENA_SLOT, tile.dtype, tile.off, ())
+        d.dense = mkview(R.ARENA_SLOT, dense.dtype, dense.off, ())
+        d.count = positions.size
+        d.n_units = 1
+        d.scatter = 1 if scatter else 0
+        lib = self.lib
+
+        def run(bufs, stream, status, _d=d, _o=optr):
+            R.check(lib.ktir_offsets(C.byref(_d), C.byref(bufs), None, C.c_void_p(_o), stream),
+                    "ktir_offsets")
+        self.launches.append(Launch(run, "scatter" if scatter else "gather"))
+
     def _launch_ew(self, prog) -> None:
         lib = self.lib
 
@@ -1180,13 +1199,23 @@ class GenericExecutor:
         elif k in ("bcast", "transpose", "reshape", "splat", "extract", "slice"):
             self.view_node(n)
         elif k == "assemble":
-            # zero tile with each piece copied in at its offset (distributed load)
+            # zero tile with each piece copied in at its offset (distributed load);
+            # a piece of scattered points is placed element by element
             out = self.arena_dense(n)
             self._ew_copy(n, _Val(imm=n.dtype.type(0), dtype=n.dtype), out)
             for piece, at in zip(n.ins, n.attrs["at"]):
+                if isinstance(at, np.ndarray):
+                    self._offsets(self.materialize(piece), out, at, scatter=True)
+                    continue
                 off = out.off + sum(a * st for a, st in zip(at, out.strides))
                 self._ew_copy(piece, self.view_of(piece), _Val(R.ARENA_SLOT, off, out.strides,
                                                                n.dtype))
+            self.vals[n.id] = out
+        elif k == "pick":
+            # the elements at row-major positions of a tile, in order
+            out = self.arena_dense(n)
+            src = self.materialize(n.ins[0])
+            self._offsets(out, src, n.attrs["positions"], scatter=False)
             self.vals[n.id] = out
         elif k == "reduce":
             self.reduce(n)

@@ -667,7 +667,20 @@ class Tracer:
             if not isinstance(part, MemRefV):
                 raise ValueError(f"construct_distributed_memory_view: operand {i} is "
                                  f"{type(part).__name__}, expected MemRef")
-        return DistMemRefV(parts, tuple(op.attributes["shape"]), op.attributes["dtype"])
+        if "shape" not in op.attributes or "dtype" not in op.attributes:
+            raise ValueError("construct_distributed_memory_view: missing required attributes "
+                             "'shape'/'dtype'")
+        dtype = op.attributes["dtype"]
+        # partition checks of DistributedMemRef (ktir_cpu/ir_types.py:140-152)
+        if not parts:
+            raise ValueError("DistributedMemRef requires at least one partition")
+        for i, part in enumerate(parts):
+            if part.cset is None:
+                raise ValueError(f"DistributedMemRef partition {i} must have a coordinate_set")
+            if part.dtype != dtype:
+                raise ValueError(f"DistributedMemRef partition {i} dtype {part.dtype!r} "
+                                 f"does not match view dtype {dtype!r}")
+        return DistMemRefV(parts, tuple(op.attributes["shape"]), dtype)
 
     def op_ktdp_construct_access_tile(self, op):
         parent = self.core.get(op.operands[0])
@@ -688,31 +701,67 @@ class Tracer:
     def _dist_access(self, dist: DistMemRefV, idx, a):
         """Partition routing of MemoryOps.distributed_tile_access
         (ktir_cpu/ops/memory_ops.py:651-756): C_i = B_i ∩ (x + A) per partition,
-        empty intersections dropped.  Rectangular partitions and access sets."""
+        empty intersections dropped.  Where B_i and A are both boxes C_i is a
+        box; otherwise C_i is the points of B_i (enumerated over the global
+        shape, in its order) that lie in x + A, and the partition's origin is
+        the per-axis minimum over B_i's points."""
         x = tuple(int(v) for v in a["base_map"].eval(idx))
         shape = tuple(a["shape"])
+        nd = len(shape)
         acc = a["coordinate_set"]
+        xa = None
         if acc is None:
-            lo, hi = x, tuple(x[d] + shape[d] for d in range(len(shape)))
+            xa = (x, tuple(x[d] + shape[d] for d in range(nd)))
         elif isinstance(acc, BoxSet) and acc.is_concrete:
-            lo = tuple(x[d] + acc.lo[d] for d in range(len(shape)))
-            hi = tuple(x[d] + acc.hi[d] for d in range(len(shape)))
-        else:
-            raise NotImplementedError("distributed access with a non-rectangular access set")
+            xa = (tuple(x[d] + acc.lo[d] for d in range(nd)),
+                  tuple(x[d] + acc.hi[d] for d in range(nd)))
+        elif isinstance(acc, BoxSet):
+            raise NotImplementedError("distributed access with a symbolic access set")
         pieces = []
         for part in dist.parts:
             b = part.cset
-            if not (isinstance(b, BoxSet) and b.is_concrete):
-                raise NotImplementedError("distributed view with a non-rectangular partition")
-            clo = tuple(max(lo[d], b.lo[d]) for d in range(len(lo)))
-            chi = tuple(min(hi[d], b.hi[d]) for d in range(len(lo)))
-            if any(clo[d] >= chi[d] for d in range(len(lo))):
+            if isinstance(b, BoxSet) and b.is_concrete and xa is not None:
+                clo = tuple(max(xa[0][d], b.lo[d]) for d in range(nd))
+                chi = tuple(min(xa[1][d], b.hi[d]) for d in range(nd))
+                if any(clo[d] >= chi[d] for d in range(nd)):
+                    continue
+                pieces.append((part, BoxSet(clo, chi), tuple(b.lo)))
                 continue
-            pieces.append((part, BoxSet(clo, chi), tuple(b.lo)))
+            if isinstance(b, BoxSet) and not b.is_concrete:
+                raise NotImplementedError("distributed view with a symbolic partition")
+            pts = b.enumerate_array(tuple(dist.shape))
+            if not len(pts):
+                continue
+            origin = tuple(int(v) for v in pts.min(0))
+            rel = pts - np.asarray(x, np.int64)
+            if xa is not None:
+                keep = np.all((pts >= np.asarray(xa[0])) & (pts < np.asarray(xa[1])), axis=1)
+            else:
+                keep = np.asarray(np.broadcast_to(acc._mask(list(rel.T)), (len(pts),)), bool)
+            if not keep.any():
+                continue
+            pieces.append((part, pts[keep], origin))
         if not pieces:
             raise ValueError(f"distributed_tile_access: no partition covers access region "
                              f"global_base={x} shape={shape}")
         return DistAccessV(x, shape, dist.dtype, pieces)
+
+    def _points(self, part: MemRefV, pts: np.ndarray, origin, what: str):
+        """(buffer, element offset, element offsets) of a partition's points
+        (global coordinates), laid out by the partition's strides from its origin."""
+        buf, eoff = self._resolve(part.byte_address, part.dtype, what)
+        local = pts - np.asarray(origin, np.int64)
+        offs = (local * np.asarray(part.strides[:pts.shape[1]], np.int64)).sum(1)
+        return buf, eoff, offs
+
+    @staticmethod
+    def _positions(pts: np.ndarray, base, shape) -> np.ndarray:
+        """Row-major positions, inside a tile of `shape`, of global points
+        taken relative to the access origin `base`."""
+        rel = pts - np.asarray(base, np.int64)
+        if rel.shape[1] != len(shape) or np.any(rel < 0) or np.any(rel >= np.asarray(shape)):
+            raise IndexError(f"distributed access: points outside the tile shape {shape}")
+        return np.ravel_multi_index(tuple(rel.T), tuple(shape)).astype(np.int64)
 
     def _piece(self, part: MemRefV, box: BoxSet, origin, what: str):
         """(buffer, element offset, shape, strides) of one partition's sub-box."""
@@ -787,6 +836,14 @@ class Tracer:
             dt = np_dtype(t.dtype)
             parts, places = [], []
             for part, box, origin in t.pieces:
+                if isinstance(box, np.ndarray):
+                    # scattered points: gathered in order, then placed one by one
+                    buf, eoff, offs = self._points(part, box, origin, "Read")
+                    parts.append(self.node("load", (len(offs),), dt, (),
+                                           {"mode": "coords", "buf": buf, "off": eoff,
+                                            "offsets": offs}))
+                    places.append(self._positions(box, t.base, shape))
+                    continue
                 buf, eoff, ext, strides = self._piece(part, box, origin, "Read")
                 parts.append(self.node("load", ext, dt, (), {"mode": "rect", "buf": buf,
                                                              "off": eoff, "strides": strides}))
@@ -828,6 +885,17 @@ class Tracer:
             # MemoryOps.distributed_store (ktir_cpu/ops/memory_ops.py:848-912): the
             # tile's slice over each covered box written to its partition
             for part, box, origin in t.pieces:
+                if isinstance(box, np.ndarray):
+                    buf, eoff, offs = self._points(part, box, origin, "Write")
+                    pos = self._positions(box, t.base, tuple(val.shape))
+                    sub = self.node("pick", (len(offs),), val.dtype, (val,), {"positions": pos},
+                                    val.label)
+                    self.trace.stores.append(Store(self.core.core_id, self.seq, sub,
+                                                   CoordTarget(buf, eoff, offs, (len(offs),),
+                                                               np_dtype(t.dtype)),
+                                                   len(self.trace.nodes)))
+                    self.seq += 1
+                    continue
                 buf, eoff, ext, strides = self._piece(part, box, origin, "Write")
                 at = tuple(box.lo[d] - t.base[d] for d in range(len(ext)))
                 sub = self.node("slice", ext, val.dtype, (val,), {"at": at}, val.label)
@@ -1449,7 +1517,10 @@ def _region_rounds(tr, t, acc, dim, n, region, names, part) -> Node:
             tr.core.pop()
         c = r.values[0] if isinstance(r, _Yield) else r
         if not _is_tile(c):
-            raise NotImplementedError("linalg.reduce: a combiner region that yields a scalar")
+            # the reference's fold takes the extent of the 0-d result along the
+            # reduced axis (ktir_cpu/dialects/linalg_ops.py:124-131), which fails
+            raise IndexError("linalg.reduce: the combiner region yields a scalar, which has "
+                             "no extent along the reduced dimension")
         if n % 2:
             # the odd slice joins the combined one as NumPy's concatenate joins
             # them: both in the wider of the two element types

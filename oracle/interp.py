@@ -124,6 +124,25 @@ class AccessTile:
 
 
 @dataclass
+class DistRef:
+    """A distributed memory view: partitions whose coordinate sets are in global
+    coordinates (ktir_cpu/ir_types.py:122-152)."""
+    parts: List[MemRef]
+    shape: Tuple[int, ...]
+    dtype: str
+
+
+@dataclass
+class DistTile:
+    """An access tile over a distributed view, routed to the partitions it
+    covers: (partition, covered set C_i, partition origin p_i); C_i is a
+    (lo, hi) box or an (N, ndim) array of global points."""
+    base: Tuple[int, ...]
+    shape: Tuple[int, ...]
+    survivors: List[Tuple[MemRef, Any, Tuple[int, ...]]]
+
+
+@dataclass
 class IndirectTile:
     parent: MemRef
     shape: Tuple[int, ...]
@@ -306,6 +325,9 @@ class OracleInterpreter:
         self.hbm: Optional[HBM] = None
         self.grid: Tuple[int, int, int] = (1, 1, 1)
         self.core_limit: Optional[int] = None   # run only the first k cores (bounded CPU samples)
+        # (stick, array) pairs written into HBM before the call's arguments,
+        # for programs that address memory through constants
+        self.preload: List[Tuple[int, np.ndarray]] = []
         # run only the first k iterations of each core's outermost scf.for
         # (bounded CPU samples); loop_fraction records the share of that
         # loop's iterations that ran
@@ -326,6 +348,8 @@ class OracleInterpreter:
         fn = self.module.get_function(func_name)
         self.grid = fn.grid
         self.hbm = HBM()
+        for stick, arr in self.preload:
+            self.hbm.write(stick, np.array(arr, copy=True))
         declared = fn.arg_names
         if kwargs and declared and not any(k in declared for k in kwargs):
             if len(kwargs) == len(declared):
@@ -492,12 +516,116 @@ class OracleInterpreter:
         return MemRef(int(ptr), tuple(int(s) for s in shape), [int(s) for s in strides],
                       a["memory_space"], a["dtype"], cset)
 
+    def op_ktdp_construct_distributed_memory_view(self, core, op):
+        """ktir_cpu/dialects/ktdp_ops.py:96-121 with the partition checks of
+        DistributedMemRef (ktir_cpu/ir_types.py:140-152)."""
+        parts = [core.get(o) for o in op.operands]
+        for i, p in enumerate(parts):
+            if not isinstance(p, MemRef):
+                raise ValueError(f"construct_distributed_memory_view: operand {i} "
+                                 f"is {type(p).__name__}, expected MemRef")
+        a = op.attributes
+        if "shape" not in a or "dtype" not in a:
+            raise ValueError("construct_distributed_memory_view: missing required attributes "
+                             "'shape'/'dtype'")
+        if not parts:
+            raise ValueError("DistributedMemRef requires at least one partition")
+        for i, p in enumerate(parts):
+            if p.coordinate_set is None:
+                raise ValueError(f"DistributedMemRef partition {i} must have a coordinate_set")
+            if p.dtype != a["dtype"]:
+                raise ValueError(f"DistributedMemRef partition {i} dtype {p.dtype!r} "
+                                 f"does not match view dtype {a['dtype']!r}")
+        return DistRef(parts, tuple(a["shape"]), a["dtype"])
+
+    @staticmethod
+    def _dist_route(dist: DistRef, shape, x, acc) -> DistTile:
+        """MemoryOps.distributed_tile_access (ktir_cpu/ops/memory_ops.py:651-733):
+        per partition C_i = B_i ∩ (x + A); boxes intersect directly, any other
+        set is enumerated over the global shape and filtered by membership."""
+        nd = len(shape)
+        xa = None
+        if acc is None:
+            xa = (tuple(x), tuple(x[d] + shape[d] for d in range(nd)))
+        elif isinstance(acc, BoxSet):
+            xa = (tuple(x[d] + acc.lo[d] for d in range(nd)),
+                  tuple(x[d] + acc.hi[d] for d in range(nd)))
+        out = []
+        for part in dist.parts:
+            b = part.coordinate_set
+            if isinstance(b, BoxSet) and xa is not None:
+                lo = tuple(max(b.lo[d], xa[0][d]) for d in range(nd))
+                hi = tuple(min(b.hi[d], xa[1][d]) for d in range(nd))
+                if any(h <= l for l, h in zip(lo, hi)):
+                    continue
+                out.append((part, (lo, hi), tuple(b.lo)))
+                continue
+            pts = b.enumerate_array(tuple(dist.shape))
+            if not len(pts):
+                continue
+            origin = tuple(int(v) for v in pts.min(0))
+            keep = np.array([acc.contains(tuple(int(v) for v in p - np.asarray(x)))
+                             if acc is not None else
+                             all(0 <= p[d] - x[d] < shape[d] for d in range(nd)) for p in pts],
+                            bool)
+            if keep.any():
+                out.append((part, pts[keep], origin))
+        if not out:
+            raise ValueError(f"distributed_tile_access: no partition covers access region "
+                             f"global_base={tuple(x)} shape={tuple(shape)}")
+        return DistTile(tuple(x), tuple(shape), out)
+
+    def _dist_refs(self, t: DistTile):
+        """Per survivor: (TileRef over the covered points, their coordinates
+        inside the access tile, box coordinates or None)."""
+        for part, cs, origin in t.survivors:
+            nd = len(origin)
+            if isinstance(cs, tuple):
+                lo, hi = cs
+                off = sum((lo[d] - origin[d]) * part.strides[d] for d in range(nd))
+                ref = TileRef(part.byte_address + off * bpe(part.dtype),
+                              tuple(hi[d] - lo[d] for d in range(nd)), list(part.strides),
+                              part.dtype, part.space)
+                yield ref, tuple(slice(lo[d] - t.base[d], hi[d] - t.base[d]) for d in range(nd)), None
+            else:
+                ref = TileRef(part.byte_address, (len(cs),), list(part.strides), part.dtype,
+                              part.space)
+                local = cs - np.asarray(origin, np.int64)
+                yield ref, tuple((cs - np.asarray(t.base, np.int64)).T), local
+
+    def _dist_load(self, t: DistTile, shape, dtype) -> np.ndarray:
+        """MemoryOps.distributed_load (ktir_cpu/ops/memory_ops.py:758-846)."""
+        out = np.zeros(shape, np_dtype(dtype))
+        for ref, at, local in self._dist_refs(t):
+            if local is None:
+                out[at] = self._load_ref(ref)
+            else:
+                offs = (local * np.asarray(ref.strides[:local.shape[1]], np.int64)).sum(1)
+                out[at] = self.hbm.read_gather(ref.byte, offs, ref.dtype)
+        return out
+
+    def _dist_store(self, t: DistTile, data: np.ndarray) -> None:
+        """MemoryOps.distributed_store (ktir_cpu/ops/memory_ops.py:848-912)."""
+        for ref, at, local in self._dist_refs(t):
+            if local is None:
+                self._store_ref(ref, np.ascontiguousarray(data[at]))
+            else:
+                offs = (local * np.asarray(ref.strides[:local.shape[1]], np.int64)).sum(1)
+                self.hbm.scatter(ref.byte, offs,
+                                 data[at].astype(np_dtype(ref.dtype), copy=False), ref.dtype)
+
     def op_ktdp_construct_access_tile(self, core, op):
         parent = core.get(op.operands[0])
-        if not isinstance(parent, MemRef):
-            raise NotImplementedError("access tiles over distributed views are not supported")
         idx = [int(core.get(o)) for o in op.operands[1:]]
         a = op.attributes
+        if isinstance(parent, DistRef):
+            cset = a["coordinate_set"]
+            if isinstance(cset, BoxSet) and not cset.is_concrete:
+                raise NotImplementedError("construct_access_tile: symbolic access_tile_set")
+            return self._dist_route(parent, tuple(a["shape"]),
+                                    tuple(int(v) for v in a["base_map"].eval(idx)), cset)
+        if not isinstance(parent, MemRef):
+            raise TypeError(f"construct_access_tile: parent is {type(parent).__name__}")
         base = a["base_map"].eval(idx)
         off = sum(int(c) * s for c, s in zip(base, parent.strides))
         ref = TileRef(parent.byte_address + off * bpe(parent.dtype), tuple(a["shape"]),
@@ -576,6 +704,10 @@ class OracleInterpreter:
     def op_ktdp_load(self, core, op):
         t = core.get(op.operands[0])
         rshape = op.attributes.get("result_shape")
+        if isinstance(t, DistTile):
+            dt = t.survivors[0][0].dtype
+            data = self._dist_load(t, tuple(rshape or t.shape), dt)
+            return Tile(data, dt, tuple(data.shape))
         if isinstance(t, IndirectTile):
             ref, coords = self._indirect_coords(t)
             data = self._load_ref(ref, coords, rshape or t.shape)
@@ -593,6 +725,9 @@ class OracleInterpreter:
         if not isinstance(tile, Tile):
             raise TypeError(f"ktdp.store expects a Tile, got {type(tile)}")
         t = core.get(op.operands[1])
+        if isinstance(t, DistTile):
+            self._dist_store(t, tile.data)
+            return None
         if isinstance(t, IndirectTile):
             if tuple(tile.shape) != tuple(t.shape):
                 raise ValueError(

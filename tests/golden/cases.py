@@ -415,16 +415,19 @@ _ring_case("ring_reduce_pairs_max", 6, 6, 64, 2, "i - 2*g >= 0, -i + 2*g + 1 >= 
 
 
 # --- distributed memory views (partitions in HBM and in a core's LX) -----------------------
-def _dist_case(name, gshape, parts, acc_shape, acc_idx, store=False):
-    """A [gshape] f16 tensor split into rectangular partitions `parts` =
-    [(row0, row1, col0, col1, space, strides, addr)] (inclusive bounds; addr is
-    a stick for HBM, a byte address for LX core 0), seeded with arange.  Load:
-    the access tile at acc_idx is copied to a dense HBM output.  Store: a dense
-    HBM input is stored through the access tile into the partitions."""
+def _dist_case(name, gshape, parts, acc_shape, acc_idx, store=False, acc_set=None):
+    """A [gshape] f16 tensor split into partitions `parts` =
+    [(row0, row1, col0, col1, space, strides, addr[, set])] (inclusive bounds of
+    the partition's bounding box, which its memory view holds; addr is a stick
+    for HBM, a byte address for LX core 0; `set`, in global coordinates, makes
+    the partition a non-rectangular part of that box), seeded with arange.
+    Load: the access tile at acc_idx (its access set `acc_set`, in access-local
+    coordinates, or the whole box) is copied to a dense HBM output.  Store: a
+    dense HBM input is stored through the access tile into the partitions."""
     out_stick = 0x400
     body = ["%c0 = arith.constant 0 : index"]
     names = []
-    for i, (r0, r1, c0, c1, space, strides, addr) in enumerate(parts):
+    for i, (r0, r1, c0, c1, space, strides, addr, *_) in enumerate(parts):
         nr, nc = r1 - r0 + 1, c1 - c0 + 1
         body.append(f"%p{i}_addr = arith.constant {addr} : index")
         body.append(
@@ -437,14 +440,14 @@ def _dist_case(name, gshape, parts, acc_shape, acc_idx, store=False):
                 f"{', '.join(t for _, t in names)}) : {g}")
     body.append(f"%b_addr = arith.constant {out_stick} : index")
     body.append(f"%B = ktdp.construct_memory_view %b_addr, sizes: [{acc_shape[0]}, {acc_shape[1]}], "
-                f"strides: [{acc_shape[1]}, 1] {{coordinate_set = #AC, memory_space = "
+                f"strides: [{acc_shape[1]}, 1] {{coordinate_set = #BC, memory_space = "
                 f"#ktdp.spyre_memory_space<HBM>}} : memref<{acc_shape[0]}x{acc_shape[1]}xf16>")
     body.append(f"%i0 = arith.constant {acc_idx[0]} : index")
     body.append(f"%i1 = arith.constant {acc_idx[1]} : index")
     at = _at(acc_shape)
     body.append(f"%A_at = ktdp.construct_access_tile %A[%i0, %i1] {{access_tile_set = #AC, "
                 f"access_tile_order = #ID}} : {g} -> {at}")
-    body.append(f"%B_at = ktdp.construct_access_tile %B[%c0, %c0] {{access_tile_set = #AC, "
+    body.append(f"%B_at = ktdp.construct_access_tile %B[%c0, %c0] {{access_tile_set = #BC, "
                 f"access_tile_order = #ID}} : memref<{acc_shape[0]}x{acc_shape[1]}xf16> -> {at}")
     tt = _tt(acc_shape, "f16")
     if store:
@@ -453,14 +456,16 @@ def _dist_case(name, gshape, parts, acc_shape, acc_idx, store=False):
     else:
         body.append(f"%d = ktdp.load %A_at : {at} -> {tt}")
         body.append(f"ktdp.store %d, %B_at : {tt}, {at}")
-    aliases = [(f"#P{i}", _box_incl(p[0], p[1], p[2], p[3])) for i, p in enumerate(parts)]
-    aliases += [("#AC", _box_incl(0, acc_shape[0] - 1, 0, acc_shape[1] - 1)),
+    aliases = [(f"#P{i}", p[7] if len(p) > 7 else _box_incl(p[0], p[1], p[2], p[3]))
+               for i, p in enumerate(parts)]
+    box = _box_incl(0, acc_shape[0] - 1, 0, acc_shape[1] - 1)
+    aliases += [("#AC", acc_set or box), ("#BC", box),
                 ("#ID", "affine_map<(d0, d1) -> (d0, d1)>")]
     src = (f"{''.join(f'{k} = {v}' + chr(10) for k, v in aliases)}module {{\n"
            f"  func.func @dist() {{\n    " + "\n    ".join(body) + "\n    return\n  }\n}\n")
     full = np.arange(gshape[0] * gshape[1], dtype=np.float16).reshape(gshape)
     seed, reads = [], []
-    for i, (r0, r1, c0, c1, space, strides, addr) in enumerate(parts):
+    for i, (r0, r1, c0, c1, space, strides, addr, *_) in enumerate(parts):
         block = full[r0:r1 + 1, c0:c1 + 1]
         if store:
             block = np.zeros_like(block) - 1
@@ -496,6 +501,26 @@ _dist_case("dist_load_partial_cover", (4, 8), [(0, 3, 0, 3, "HBM", [4, 1], 0x100
 _dist_case("dist_store_hbm_lx", (4, 8), [(0, 1, 0, 7, "LX", [8, 1], 0x400),
                                          (2, 3, 0, 7, "HBM", [1, 2], 0x200)], (3, 5), (1, 2),
            store=True)
+
+# non-rectangular partitions (the reference's enumerate-and-filter routing):
+# the lower triangle with the diagonal in one HBM view, the strict upper
+# triangle in a second, each view holding its bounding box
+_TRI = [(0, 7, 0, 7, "HBM", [8, 1], 0x100, "affine_set<(d0, d1) : (d0 - d1 >= 0, d0 >= 0, "
+         "-d0 + 7 >= 0, d1 >= 0, -d1 + 7 >= 0)>"),
+        (0, 6, 1, 7, "HBM", [7, 1], 0x200, "affine_set<(d0, d1) : (d1 - d0 - 1 >= 0, "
+         "d0 >= 0, -d0 + 6 >= 0, d1 - 1 >= 0, -d1 + 7 >= 0)>")]
+_dist_case("dist_load_triangular_parts", (8, 8), _TRI, (4, 6), (2, 1))
+_dist_case("dist_store_triangular_parts", (8, 8), _TRI, (5, 5), (1, 3), store=True)
+# a non-rectangular access set over row bands: only its points are read
+# (the rest of the tile is zero) or written
+_BANDS = [(0, 3, 0, 7, "HBM", [8, 1], 0x100), (4, 7, 0, 7, "LX", [1, 4], 0x800)]
+_ACC_TRI = "affine_set<(d0, d1) : (d0 - d1 + 1 >= 0, d0 >= 0, -d0 + 4 >= 0, d1 >= 0, -d1 + 5 >= 0)>"
+_dist_case("dist_load_triangular_access", (8, 8), _BANDS, (5, 6), (2, 1), acc_set=_ACC_TRI)
+_dist_case("dist_store_triangular_access", (8, 8), _BANDS, (5, 6), (2, 1), store=True,
+           acc_set=_ACC_TRI)
+# both: a triangular access set over triangular partitions
+_dist_case("dist_store_triangular_both", (8, 8), _TRI, (5, 6), (2, 1), store=True,
+           acc_set=_ACC_TRI)
 
 
 # --- model-style kernels through the generic executor ----------------------------------
@@ -843,6 +868,35 @@ case("reduce_region_inline_args", _region_reduce_case("rred2", [
     "linalg.yield %a : f32",
 ]), "rred2", {"x": _rx, "y": _ry, "m": np.zeros(24, np.float16), "q": np.zeros(24, np.float32)},
     expect_error="KeyError")
+
+# a combiner region that yields a scalar (a constant): the reference's fold
+# fails with IndexError on the 0-d result, whether the reduced extent is odd
+# (300 columns) or even (256)
+def _scalar_yield_case(name, cols, err):
+    case(name, _fn("rsc", ["x", "m"], [
+        "%c0 = arith.constant 0 : index",
+        _view("%xv", "%x", (24, cols), "f16"),
+        _view("%mv", "%m", (24,), "f16"),
+        _tile("%xt", "%xv", ["%c0", "%c0"], (24, cols), "f16", (24, cols)),
+        f"%x = ktdp.load %xt : {_at((24, cols))} -> {_tt((24, cols), 'f16')}",
+        "%z = arith.constant 0.0 : f16",
+        f"%m0 = tensor.splat %z : {_tt((24,), 'f16')}",
+        f"%sm = linalg.reduce ins(%x : {_tt((24, cols), 'f16')}) outs(%m0 : {_tt((24,), 'f16')}) "
+        "dimensions = [1]\n"
+        "      {\n"
+        "      ^bb0(%in: f16, %out: f16):\n"
+        "        %a = arith.addf %in, %out : f16\n"
+        "        %k = arith.constant 1.0 : f16\n"
+        "        linalg.yield %k : f16\n"
+        "      }",
+        _tile("%mt", "%mv", ["%c0"], (24,), "f16", (24,)),
+        f"ktdp.store %sm, %mt : {_tt((24,), 'f16')}, {_at((24,))}",
+    ]), "rsc", {"x": np.random.default_rng(cols).standard_normal((24, cols)).astype(np.float16),
+                "m": np.zeros(24, np.float16)}, expect_error=err)
+
+
+_scalar_yield_case("reduce_region_scalar_yield_odd", 300, "IndexError")
+_scalar_yield_case("reduce_region_scalar_yield_even", 256, "IndexError")
 
 # --- arith.convertf (f16 -> f32, f32 -> f16) and ktdp.coreid on a 2 x 2 grid
 # (the core ids of a grid row; the reference returns them as a list that this

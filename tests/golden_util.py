@@ -54,6 +54,18 @@ def run_seeded(interp, g):
     return out
 
 
+def run_seeded_oracle(oracle, g):
+    """run_seeded for the oracle, which holds HBM only: the seeds are written
+    into its HBM before the call.  Returns None for a case with memory in a
+    core's LX."""
+    if any(sp != "HBM" for sp, *_ in g["seed"]) or "spyre_memory_space<LX>" in g["src"]:
+        return None
+    oracle.preload = [(addr, arr) for _, _, addr, arr in g["seed"]]
+    oracle.execute_function(g["func"], **{k: (v.copy() if isinstance(v, np.ndarray) else v)
+                                          for k, v in g["inputs"].items()})
+    return {name: oracle.hbm.read(addr, n, dt) for name, _, _, addr, n, dt in g["reads"]}
+
+
 # smallest normal f16 (2^-14): relative errors are taken against at least this
 # magnitude, so an output in the subnormal range is judged by its absolute error
 # against that bound (one subnormal f16 step is about 1e-3 of it)
