@@ -61,7 +61,7 @@ WORK = {
     "gemm": ("tensor", 2 * 4096 ** 3),
     "attention": ("tensor", 4 * 4 * 32 * 2048 * 2048 * 128 // 2),
 }
-DOMINANT = {"vector_add": "k_ew", "softmax": "k_softmax_rows", "gather_add": "k_rmw_apply",
+DOMINANT = {"vector_add": "k_ew_bin_f16", "softmax": "k_softmax_rows", "gather_add": "k_rmw_apply",
             "gemm": "k_gemm_tcgen05", "attention": "k_fmha_tcgen05"}
 WORKLOAD = {"softmax": "row softmax f16 [4096,1024], grid 32, 128 rows/core, f32 max/sum",
             "vector_add": "add_kernel f16 (1024,)",
@@ -332,7 +332,8 @@ def measure_batched(env: Env, exe, host, steps: int, n: int = 65536):
     return {"executions_per_launch": n, "value": per_rank * n / (ms / 1000.0), "unit": UNIT,
             "ms_per_launch": ms, "gpu_launches": steps * len(bx.progs),
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": gbs / hbm_peak, "kernel": "k_ew_bin_f16"}}
+                         "frac": gbs / hbm_peak, "kernel": "k_ew_bin_f16",
+                         "traffic": read_traffic("vector_add")}}
 
 
 def measure(env: Env, name: str, steps: int, with_cpu: bool):
@@ -380,11 +381,15 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
             b = measure_batched(env, exe, host, steps)
             out["batched_launches"] = 3 + steps + b["gpu_launches"]
         return out
+    # a workload too small for its rotating sets to exceed L2 is timed with an
+    # L2 flush (a 256 MiB write) before every execution instead, each
+    # execution between its own pair of events
+    flush = n_sets * set_bytes < 2 * L2_BYTES
     # the K timed executions, recorded once as a CUDA graph so the host's
     # per-launch cost does not pace the device (plans with an NCCL exchange
     # keep plain launches)
     graph = None
-    if not plan.collective and not args.eager:
+    if not plan.collective and not args.eager and not flush:
         graph = exe.capture([sets[i % n_sets][0] for i in range(steps)])
         graph.replay()
         torch.cuda.synchronize(dev)
@@ -395,6 +400,22 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
         else:
             for i in range(steps):
                 exe.launch(sets[i % n_sets][0], stream, sets[i % n_sets][1])
+
+    if flush:
+        scrub = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+
+        def flushed(n):
+            """Device ms of n executions, each after an L2 flush."""
+            evs = []
+            for i in range(n):
+                scrub.fill_(i & 255)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                exe.launch(sets[i % n_sets][0], stream, sets[i % n_sets][1])
+                b.record(stream)
+                evs.append((a, b))
+            torch.cuda.synchronize(dev)
+            return float(sum(a.elapsed_time(b) for a, b in evs))
 
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     env.barrier()
@@ -408,21 +429,27 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
         # queued the K steps before the clock starts (the host's launch
         # latency is not device time)
         torch.cuda._sleep(200000)
-        ev[0].record(stream)
-        run_steps()
-        ev[1].record(stream)
-        torch.cuda.synchronize(dev)
-        k_ms = ev[0].elapsed_time(ev[1])
+        if flush:
+            k_ms = flushed(steps)
+        else:
+            ev[0].record(stream)
+            run_steps()
+            ev[1].record(stream)
+            torch.cuda.synchronize(dev)
+            k_ms = ev[0].elapsed_time(ev[1])
         # a second window of at least 10 ms of device time: the K steps repeated
         reps = max(1, int(math.ceil(10.0 / max(k_ms, 1e-3))))
         env.barrier()
         torch.cuda._sleep(200000)
-        ev[2].record(stream)
-        for _ in range(reps):
-            run_steps()
-        ev[3].record(stream)
-        torch.cuda.synchronize(dev)
-        long_ms = ev[2].elapsed_time(ev[3])
+        if flush:
+            long_ms = flushed(steps * reps)
+        else:
+            ev[2].record(stream)
+            for _ in range(reps):
+                run_steps()
+            ev[3].record(stream)
+            torch.cuda.synchronize(dev)
+            long_ms = ev[2].elapsed_time(ev[3])
         # per-execution event pairs, each execution alone between its events
         pairs = []
         for i in range(min(steps, 50)):
@@ -471,7 +498,10 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
         "long_window": {"steps": steps * reps, "ms": long_ms, "value": long_value,
                         "ms_per_step": long_ms / (steps * reps)},
         "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                     "frac": achieved / peak, "traffic": read_traffic(base),
+                     "frac": achieved / peak,
+                     # the vector add's ncu capture is of a batched launch: its
+                     # traffic belongs to the batched figure
+                     "traffic": read_traffic(base) if base != "vector_add" else None,
                      "peak_source": src_peak + (" (sustained; timed after 1.5 s of load)"
                                                 if bound == "tensor" else ""),
                      "frac_of_burst": (achieved / tc_peak if bound == "tensor" else None),
@@ -482,8 +512,11 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
                 "arg_bytes": sum(v.nbytes for v in kw.values())},
         "gpu_launches": steps * plan.kernel_launches,
         "method": {"plan": plan.kind,
-                   "l2": f"{n_sets} rotating buffer sets of {set_bytes / 2**20:.1f} MiB "
-                         f"(> 126 MB L2)",
+                   "l2": (f"flushed: a {2 * L2_BYTES >> 20} MiB write before every execution, "
+                          f"each execution timed between its own events ({set_bytes} bytes "
+                          f"of arguments, {n_sets} rotating sets)") if flush else
+                         (f"{n_sets} rotating buffer sets of {set_bytes / 2**20:.1f} MiB "
+                          f"(> 126 MB L2)"),
                    "launch": "cuda graph of the K steps" if graph is not None
                    else "host launch per step"},
         "clocks": clk.summary(),

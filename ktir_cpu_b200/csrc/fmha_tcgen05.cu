@@ -502,12 +502,13 @@ int launch_fmha(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap&
                              SMEM_BYTES) != cudaSuccess ||
         cudaFuncSetAttribute(k_fmha_tcgen05, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-      return KTIR_ERR_CUDA;
+      return ktir_set_error(KTIR_ERR_CUDA, "attention: shared-memory attributes refused");
     attr = true;
   }
   dim3 grid((unsigned)((long long)p.n_qtiles * p.bh));   // rows / 128 < 2^31
   k_fmha_tcgen05<<<grid, THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
-  return cudaGetLastError() == cudaSuccess ? KTIR_OK : KTIR_ERR_CUDA;
+  return cudaGetLastError() == cudaSuccess
+             ? KTIR_OK : ktir_set_error(KTIR_ERR_CUDA, "attention: launch failed");
 }
 
 bool aligned16(const void* a) { return (reinterpret_cast<uintptr_t>(a) & 15) == 0; }
@@ -515,19 +516,22 @@ bool aligned16(const void* a) { return (reinterpret_cast<uintptr_t>(a) & 15) == 
 }  // namespace
 
 extern "C" int ktir_fmha_f16(const KtirFmhaDesc* d, void* stream) {
-  if (!d || !d->q || !d->k || !d->v || !d->o || !d->status) return KTIR_ERR_ARG;
+  if (!d || !d->q || !d->k || !d->v || !d->o || !d->status)
+    return ktir_set_error(KTIR_ERR_ARG, "ktir_fmha_f16: null argument");
   // the row max is taken before scaling, which needs a positive scale
   if (d->d != D || d->seq % BQ || d->bh < 1 || d->row_stride < D || (d->row_stride & 7) ||
       !(d->scale > 0.f))
-    return KTIR_ERR_UNSUPPORTED;
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED,
+                          "ktir_fmha_f16: needs d = 128, seq a multiple of 128, a row stride "
+                          "of at least 128 in multiples of 8, and a positive scale");
   if (!aligned16(d->q) || !aligned16(d->k) || !aligned16(d->v) || !aligned16(d->o))
-    return KTIR_ERR_UNSUPPORTED;
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_fmha_f16: operands not 16-byte aligned");
   const long long rows = d->bh * d->seq;
-  if (rows > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
+  if (rows > 0x7fffffffLL) return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_fmha_f16: too many rows");
   CUtensorMap tq, tk, tv;
   if (!make_map(&tq, d->q, rows, d->row_stride, BQ) || !make_map(&tk, d->k, rows, d->row_stride, BKV) ||
       !make_map(&tv, d->v, rows, d->row_stride, BKV))
-    return KTIR_ERR_CUDA;
+    return ktir_set_error(KTIR_ERR_CUDA, "ktir_fmha_f16: tensor map encoding failed");
   FmhaParams p = {};
   p.o = static_cast<__half*>(d->o);
   p.seq = d->seq;
@@ -541,32 +545,41 @@ extern "C" int ktir_fmha_f16(const KtirFmhaDesc* d, void* stream) {
 }
 
 extern "C" int ktir_fmha_f16_part(const KtirFmhaPartDesc* d, void* stream) {
-  if (!d || !d->q || !d->k || !d->v || !d->o || !d->status) return KTIR_ERR_ARG;
+  if (!d || !d->q || !d->k || !d->v || !d->o || !d->status)
+    return ktir_set_error(KTIR_ERR_ARG, "ktir_fmha_f16_part: null argument");
   const bool first = d->flags & 1, last = d->flags & 2;
-  if ((!first || !last) && (!d->o_acc || !d->ml)) return KTIR_ERR_ARG;
+  if ((!first || !last) && (!d->o_acc || !d->ml))
+    return ktir_set_error(KTIR_ERR_ARG, "ktir_fmha_f16_part: a partial step needs o_acc and ml");
   if (d->d != D || d->seq % BQ || d->seq > MAX_TILES * BQ || d->bh < 1 || !(d->scale > 0.f))
-    return KTIR_ERR_UNSUPPORTED;
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED,
+                          "ktir_fmha_f16_part: needs d = 128, seq a multiple of 128 up to "
+                          "4096, and a positive scale");
   const int n_tiles = (int)(d->seq / BQ);
   if (d->n_qtiles < 1 || d->n_qtiles > n_tiles || d->kv_tiles < 1 || d->kv_tiles > n_tiles)
-    return KTIR_ERR_UNSUPPORTED;
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_fmha_f16_part: n_qtiles or kv_tiles out of range");
   if (!aligned16(d->q) || !aligned16(d->k) || !aligned16(d->v) || !aligned16(d->o) ||
       !aligned16(d->o_acc) || !aligned16(d->ml))
-    return KTIR_ERR_UNSUPPORTED;
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_fmha_f16_part: buffers not 16-byte aligned");
   const long long rows = d->bh * d->seq;
-  if (rows > 0x7fffffffLL || d->kv_rows < 1 || d->kv_rows > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
+  if (rows > 0x7fffffffLL || d->kv_rows < 1 || d->kv_rows > 0x7fffffffLL)
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_fmha_f16_part: row count out of range");
   for (int i = 0; i < d->n_qtiles; ++i)
-    if (d->qtiles[i] >= n_tiles) return KTIR_ERR_UNSUPPORTED;
+    if (d->qtiles[i] < 0 || d->qtiles[i] >= n_tiles)
+      return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_fmha_f16_part: query tile out of range");
   // every key tile the mask names must lie inside K / V
   for (int kt = 0; kt < n_tiles; ++kt) {
     if (!((d->key_mask >> kt) & 1u)) continue;
+    if (d->kv_owner[kt] < 0 || d->kv_local[kt] < 0 || d->kv_local[kt] >= d->kv_tiles)
+      return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_fmha_f16_part: key tile place out of range");
     const long long end =
         (((long long)d->kv_owner[kt] * d->bh + d->bh - 1) * d->kv_tiles + d->kv_local[kt] + 1) * BQ;
-    if (d->kv_local[kt] >= d->kv_tiles || end > d->kv_rows) return KTIR_ERR_UNSUPPORTED;
+    if (end > d->kv_rows)
+      return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_fmha_f16_part: key tile beyond kv_rows");
   }
   CUtensorMap tq, tk, tv;
   if (!make_map(&tq, d->q, rows, D, BQ) || !make_map(&tk, d->k, d->kv_rows, D, BKV) ||
       !make_map(&tv, d->v, d->kv_rows, D, BKV))
-    return KTIR_ERR_CUDA;
+    return ktir_set_error(KTIR_ERR_CUDA, "ktir_fmha_f16_part: tensor map encoding failed");
   FmhaParams p = {};
   p.o = static_cast<__half*>(d->o);
   p.seq = d->seq;

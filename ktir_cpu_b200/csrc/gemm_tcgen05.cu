@@ -414,21 +414,26 @@ thread_local char g_msg[256];
 extern "C" const char* ktir_gemm_error(void) { return g_msg; }
 
 extern "C" int ktir_gemm_f16(const KtirGemmDesc* d, void* stream) {
-  if (!d || !d->a || !d->b || !d->c || !d->status) return KTIR_ERR_ARG;
-  if (d->m % BM || d->n % BN || d->k % BK || d->k < BK) return KTIR_ERR_UNSUPPORTED;
+  if (!d || !d->a || !d->b || !d->c || !d->status)
+    return ktir_set_error(KTIR_ERR_ARG, "ktir_gemm_f16: null argument");
+  if (d->m % BM || d->n % BN || d->k % BK || d->k < BK)
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED,
+                          "ktir_gemm_f16: M, N, K must be multiples of 128, 256, 64");
   if ((reinterpret_cast<uintptr_t>(d->a) | reinterpret_cast<uintptr_t>(d->b) |
        reinterpret_cast<uintptr_t>(d->c)) & 15)
-    return KTIR_ERR_UNSUPPORTED;
-  if ((d->lda | d->ldb | d->ldc) & 7) return KTIR_ERR_UNSUPPORTED;
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_gemm_f16: operands not 16-byte aligned");
+  if ((d->lda | d->ldb | d->ldc) & 7)
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED,
+                          "ktir_gemm_f16: row strides must be multiples of 8 elements");
   CUtensorMap ta, tb;
   if (!make_map(&ta, d->a, d->m, d->k, d->lda, 64, BM) ||
       !make_map(&tb, d->b, d->k, d->n, d->ldb, 64, BK))
-    return KTIR_ERR_CUDA;
+    return ktir_set_error(KTIR_ERR_CUDA, "ktir_gemm_f16: tensor map encoding failed");
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(k_gemm_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              SMEM_BYTES) != cudaSuccess)
-      return KTIR_ERR_CUDA;
+      return ktir_set_error(KTIR_ERR_CUDA, "ktir_gemm_f16: shared-memory attribute refused");
     attr = true;
   }
   GemmParams p;
@@ -444,35 +449,42 @@ extern "C" int ktir_gemm_f16(const KtirGemmDesc* d, void* stream) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm < 1)
-      return KTIR_ERR_CUDA;
+      return ktir_set_error(KTIR_ERR_CUDA, "ktir_gemm_f16: no SM count for the current device");
   }
   const long long tiles = (d->m / BM) * (d->n / BN);
-  if (tiles > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
+  if (tiles > 0x7fffffffLL) return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_gemm_f16: too many tiles");
   const unsigned grid = (unsigned)(tiles < n_sm ? tiles : n_sm);
   k_gemm_tcgen05<<<grid, 192, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
-  return cudaGetLastError() == cudaSuccess ? KTIR_OK : KTIR_ERR_CUDA;
+  return cudaGetLastError() == cudaSuccess
+             ? KTIR_OK : ktir_set_error(KTIR_ERR_CUDA, "ktir_gemm_f16: launch failed");
 }
 
 extern "C" int ktir_gemm_f16_blocked(const KtirGemmBlockedDesc* d, void* stream) {
-  if (!d || !d->a || !d->b || !d->c || !d->status) return KTIR_ERR_ARG;
+  if (!d || !d->a || !d->b || !d->c || !d->status)
+    return ktir_set_error(KTIR_ERR_ARG, "ktir_gemm_f16_blocked: null argument");
   if (d->m < 1 || d->n < 1 || d->k < 1 || d->block_k < 0 || (d->block_k & 15))
-    return KTIR_ERR_UNSUPPORTED;
-  if (d->m > 0x7fffffffLL || d->n > 0x7fffffffLL || d->k > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED,
+                          "ktir_gemm_f16_blocked: empty matrix or block_k not a multiple of 16");
+  if (d->m > 0x7fffffffLL || d->n > 0x7fffffffLL || d->k > 0x7fffffffLL)
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_gemm_f16_blocked: dimension above 2^31");
   if ((reinterpret_cast<uintptr_t>(d->a) | reinterpret_cast<uintptr_t>(d->b)) & 15)
-    return KTIR_ERR_UNSUPPORTED;
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_gemm_f16_blocked: A or B not 16-byte aligned");
   if ((d->lda | d->ldb) & 7 || d->lda < d->k || d->ldb < d->n || d->ldc < d->n)
-    return KTIR_ERR_UNSUPPORTED;
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED,
+                          "ktir_gemm_f16_blocked: lda / ldb must be multiples of 8 elements, "
+                          "and no row stride below its row length");
   const long long gy = (d->n + GB_BN - 1) / GB_BN, gx = (d->m + GB_BM - 1) / GB_BM;
-  if (gy > 65535 || gx > 0x7fffffffLL) return KTIR_ERR_UNSUPPORTED;
+  if (gy > 65535 || gx > 0x7fffffffLL)
+    return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_gemm_f16_blocked: too many tiles");
   CUtensorMap ta, tb;
   if (!make_map(&ta, d->a, d->m, d->k, d->lda, 64, GB_BM) ||
       !make_map(&tb, d->b, d->k, d->n, d->ldb, 64, GB_BK))
-    return KTIR_ERR_CUDA;
+    return ktir_set_error(KTIR_ERR_CUDA, "ktir_gemm_f16_blocked: tensor map encoding failed");
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(k_gemm_blocked, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              GB_SMEM_BYTES) != cudaSuccess)
-      return KTIR_ERR_CUDA;
+      return ktir_set_error(KTIR_ERR_CUDA, "ktir_gemm_f16_blocked: shared-memory attribute refused");
     attr = true;
   }
   GemmBlockedParams p;
@@ -488,5 +500,6 @@ extern "C" int ktir_gemm_f16_blocked(const KtirGemmBlockedDesc* d, void* stream)
   p.status = static_cast<int*>(d->status);
   k_gemm_blocked<<<dim3((unsigned)gx, (unsigned)gy), 192, GB_SMEM_BYTES,
                    static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
-  return cudaGetLastError() == cudaSuccess ? KTIR_OK : KTIR_ERR_CUDA;
+  return cudaGetLastError() == cudaSuccess
+             ? KTIR_OK : ktir_set_error(KTIR_ERR_CUDA, "ktir_gemm_f16_blocked: launch failed");
 }

@@ -14,6 +14,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+// the library's thread-local last-error message (ktir_last_error); returns code
+int ktir_set_error(int code, const char* msg);
+
 namespace ktir {
 namespace tc {
 

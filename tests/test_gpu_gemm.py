@@ -20,7 +20,7 @@ def _gemm(a, b, c):
     status = torch.zeros(1, dtype=torch.int32, device=a.device)
     d = R.KtirGemmDesc()
     d.a, d.b, d.c = a.data_ptr(), b.data_ptr(), c.data_ptr()
-    d.lda, d.ldb, d.ldc = a.shape[1], b.shape[1], c.shape[1]
+    d.lda, d.ldb, d.ldc = a.stride(0), b.stride(0), c.stride(0)
     d.m, d.n, d.k = a.shape[0], b.shape[1], a.shape[1]
     d.add_zero = 1
     d.status = status.data_ptr()
@@ -66,7 +66,7 @@ def _blocked(a, b, c, block_k, acc_f16):
     status = torch.zeros(1, dtype=torch.int32, device=a.device)
     d = R.KtirGemmBlockedDesc()
     d.a, d.b, d.c = a.data_ptr(), b.data_ptr(), c.data_ptr()
-    d.lda, d.ldb, d.ldc = a.shape[1], b.shape[1], c.shape[1]
+    d.lda, d.ldb, d.ldc = a.stride(0), b.stride(0), c.stride(0)
     d.m, d.n, d.k = a.shape[0], b.shape[1], a.shape[1]
     d.block_k, d.acc_f16 = block_k, acc_f16
     d.status = status.data_ptr()
@@ -77,9 +77,10 @@ def _blocked(a, b, c, block_k, acc_f16):
 
 
 # shapes the aligned kernel does not take (M, N, K not multiples of 128, 256,
-# 64; M below one tile; K a multiple of 8, as TMA row strides are multiples
-# of 16 bytes), widened (block_k 0) and f16 block products rounded
-# per block into an f16 or f32 running sum (the reference's matmul_fwd example)
+# 64; M below one tile; the row strides of A and B multiples of 8 elements, as
+# TMA row strides are multiples of 16 bytes: N = 130 has B rows 136 apart),
+# widened (block_k 0) and f16 block products rounded per block into an f16 or
+# f32 running sum (the reference's matmul_fwd example)
 @pytest.mark.parametrize("m,n,k,block_k,acc_f16", [
     (64, 8192, 2048, 128, 1), (100, 200, 72, 0, 0), (257, 130, 296, 0, 0),
     (32, 512, 256, 32, 1), (200, 136, 512, 128, 0), (1, 8, 16, 16, 1)])
@@ -88,6 +89,8 @@ def test_blocked_gemm_matches_reference_rounding(m, n, k, block_k, acc_f16):
     g = torch.Generator(device="cpu").manual_seed(m + 3 * n + 7 * k)
     a = (torch.rand(m, k, generator=g) * 2 - 1).half().cuda()
     b = (torch.rand(k, n, generator=g) * 2 - 1).half().cuda()
+    if n % 8:
+        b = torch.zeros(k, (n + 7) // 8 * 8, dtype=torch.float16, device="cuda")[:, :n].copy_(b)
     c = torch.full((m, n), float("nan"), dtype=torch.float16, device="cuda")
     _blocked(a, b, c, block_k, acc_f16)
     if block_k == 0:
