@@ -70,7 +70,10 @@ struct Bars {
   uint64_t k_full[KST], k_empty[KST];
   uint64_t v_full[VST], v_empty[VST];
   uint64_t s_full[2];
-  uint64_t p_full, pv_done;
+  // P_j handed over / PV_j complete, one barrier per parity of j: a waiter
+  // names the phase it wants by (j >> 1) & 1, which stays unambiguous because
+  // a barrier's next phase (j + 2) needs this warp's own later work
+  uint64_t p_full[2], pv_done[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -175,8 +178,10 @@ __global__ void __launch_bounds__(THREADS, 2)
       mbar_init(smem_u32(&B.v_empty[s]), 1);
     }
     for (int b = 0; b < 2; ++b) mbar_init(smem_u32(&B.s_full[b]), 1);
-    mbar_init(smem_u32(&B.p_full), BQ);
-    mbar_init(smem_u32(&B.pv_done), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&B.p_full[b]), BQ);
+      mbar_init(smem_u32(&B.pv_done[b]), 1);
+    }
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -260,7 +265,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       for (int j = 0; ok && j < 2 && j < n_kv; ++j) ok = issue_s(j);
       for (int j = 0; ok && j < n_kv; ++j) {
         // softmax j has read S_j and written P_j
-        if (!mbar_wait(smem_u32(&B.p_full), j & 1, abort)) break;
+        if (!mbar_wait(smem_u32(&B.p_full[j & 1]), (j >> 1) & 1, abort)) break;
         const int vs = j % VST;
         if (!mbar_wait(smem_u32(&B.v_full[vs]), (j / VST) & 1, abort)) break;
         tc_fence_after();
@@ -276,7 +281,7 @@ __global__ void __launch_bounds__(THREADS, 2)
           // a partial call after the first adds onto the carried O
           mma_f16_ts(tmem + O_COL, at, bd, idesc_pv, (j | kk) != 0 || !first);
         }
-        mma_commit(smem_u32(&B.pv_done));
+        mma_commit(smem_u32(&B.pv_done[j & 1]));
         mma_commit(smem_u32(&B.v_empty[vs]));
         if (j + 2 < n_kv) ok = issue_s(j + 2);
       }
@@ -370,14 +375,12 @@ __global__ void __launch_bounds__(THREADS, 2)
       // a rescale of O waits for PV_{j-1} to finish adding into O (at j = 0
       // of a call that carries state, O holds the carried values and may need
       // the same rescale)
-      bool waited = false;
       if ((j >= 1 || !first) && __any_sync(0xffffffffu, rescale)) {
         if (j >= 1) {
-          const bool ok = __all_sync(0xffffffffu,
-                                     mbar_wait(smem_u32(&B.pv_done), (j - 1) & 1, abort));
+          const bool ok = __all_sync(
+              0xffffffffu, mbar_wait(smem_u32(&B.pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, abort));
           tc_fence_after();
           if (!ok) break;
-          waited = true;
         }
         {
 #pragma unroll 1
@@ -396,18 +399,14 @@ __global__ void __launch_bounds__(THREADS, 2)
       tmem_st32_wait(pcol, ph);
       tmem_st32_wait(pcol + 32, pl);
       tc_fence_before();
-      mbar_arrive(smem_u32(&B.p_full));
-      // keep in step with the PV products: PV_{j-1} completes before S_{j+1}
-      // (issued after it), which this warp waits for next anyway
-      if (j >= 1 && !waited) {
-        const bool ok = __all_sync(0xffffffffu,
-                                   mbar_wait(smem_u32(&B.pv_done), (j - 1) & 1, abort));
-        tc_fence_after();
-        if (!ok) break;
-      }
+      mbar_arrive(smem_u32(&B.p_full[j & 1]));
+      // no wait for PV_{j-1} here: S_{j+1}, which this warp waits for next, is
+      // issued after PV_{j-1} by the same thread, so its completion implies
+      // PV_{j-1}'s (and P_{j+1} may then overwrite P_{j-1})
     }
     const bool done =
-        !*abort && (n_kv == 0 || mbar_wait(smem_u32(&B.pv_done), (n_kv - 1) & 1, abort));
+        !*abort && (n_kv == 0 || mbar_wait(smem_u32(&B.pv_done[(n_kv - 1) & 1]),
+                                           ((n_kv - 1) >> 1) & 1, abort));
     // O of this CTA: from TMEM, or, with no key block in this call, the
     // carried state (zero on a first call)
     auto o_cols = [&](int c, uint32_t (&r)[32]) {
