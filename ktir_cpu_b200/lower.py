@@ -371,7 +371,7 @@ class Plan:
 
 
 # launch kinds that are NCCL exchanges between ranks
-COLLECTIVE_KINDS = {"allreduce_counts", "kv_ring"}
+COLLECTIVE_KINDS = {"reduce_scatter_counts", "kv_ring"}
 
 
 class DeviceData:
@@ -486,6 +486,15 @@ def units_independent(items: Sequence[Tuple[List[Tuple[int, Tuple[int, int]]],
 def core_range(rank: int, world: int, n_cores: int) -> Tuple[int, int]:
     """Contiguous block of cores owned by `rank` when a grid is split across `world` GPUs."""
     return (rank * n_cores) // world, ((rank + 1) * n_cores) // world
+
+
+def row_shard(rank: int, world: int, n_rows: int) -> Tuple[int, int, int]:
+    """(first row, end row, chunk) of the table rows `rank` owns in a split
+    gather-RMW: equal chunks of ceil(n_rows / world) rows, the last ones cut
+    at n_rows, which is the layout a reduce-scatter of the per-row counts
+    (padded to chunk * world entries) leaves on each rank."""
+    chunk = -(-n_rows // world)
+    return min(n_rows, rank * chunk), min(n_rows, (rank + 1) * chunk), chunk
 
 
 class Lowerer:
@@ -658,7 +667,12 @@ class Lowerer:
 
     def _gather_rmw_plan(self, full, local) -> Plan:
         d, n_rows, n_units, R_, C_ = full
-        counts = self.dev.zeros_i32(n_rows)
+        if self.shard is not None:
+            rank, world, group = self.shard
+            r0, r1, chunk = row_shard(rank, world, n_rows)
+            counts = self.dev.zeros_i32(chunk * world)
+        else:
+            counts = self.dev.zeros_i32(n_rows)
         lib = R.load_library()
         cptr = C.c_void_p(counts.data_ptr())
         if self.shard is None:
@@ -667,8 +681,6 @@ class Lowerer:
                                             C.c_void_p(status), stream), "ktir_gather_rmw")
             launches = [Launch(run, "gather_rmw", 2)]
         else:
-            rank, world, group = self.shard
-            r0, r1 = core_range(rank, world, n_rows)
             dl = None
             if local is not None:
                 dl = local[0]
@@ -682,14 +694,19 @@ class Lowerer:
                                                 C.c_void_p(status), stream), "ktir_gather_rmw(count)")
 
             def run_exchange(bufs, stream, status):
+                # each rank receives the summed counts of the rows it owns, in
+                # place (its own chunk of the count array); the apply pass
+                # consumes every count it finds, owned or not, so the array is
+                # zero again afterwards
                 import torch.distributed as dist
-                dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
+                dist.reduce_scatter_tensor(counts[rank * chunk:(rank + 1) * chunk], counts,
+                                           op=dist.ReduceOp.SUM, group=group)
 
             def run_apply(bufs, stream, status):
                 R.check(lib.ktir_gather_rmw(C.byref(d), C.byref(bufs), cptr, n_rows,
                                             C.c_void_p(status), stream), "ktir_gather_rmw(apply)")
             launches = [Launch(run_count, "gather_rmw_count", 1 if dl is not None else 0),
-                        Launch(run_exchange, "allreduce_counts", 0),
+                        Launch(run_exchange, "reduce_scatter_counts", 0),
                         Launch(run_apply, "gather_rmw_apply", 1)]
         plan = Plan("gather_rmw", launches, [], status_check=True)
         plan.scratch["counts"] = counts

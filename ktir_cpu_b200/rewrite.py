@@ -32,6 +32,8 @@ constant ops):
 
 from __future__ import annotations
 
+import os
+
 from typing import Any, Dict, List, Optional
 
 import numpy as np
@@ -405,7 +407,8 @@ def match_attention_plan(low, stores):
     if len(seen) * bq != (h_hi - h_lo) * seq or heads != list(range(h_lo, h_hi)):
         if low.shard is not None:
             from .ring import ring_attention_plan
-            return ring_attention_plan(low, prob)
+            # KTIR_KV_EXCHANGE picks how the K/V shares travel (ring.EXCHANGES)
+            return ring_attention_plan(low, prob, os.environ.get("KTIR_KV_EXCHANGE", "gather"))
         return None
     bh = h_hi - h_lo
     off = h_lo * seq * d * 2

@@ -78,17 +78,23 @@ def share_mask(tiles: Sequence[int]) -> int:
     return m
 
 
-def ring_attention_plan(low, prob, exchange: str = "allgather"):
+EXCHANGES = ("gather", "allgather", "ring")
+
+
+def ring_attention_plan(low, prob, exchange: str = "gather"):
     """Device plan for one rank (see the module docstring).
 
-    Step 0 adds the rank's own key tiles straight from the call's K and V,
-    while the comm stream packs its share (ktir_pack_kv) and passes the
-    shares between the GPUs; the later steps add the other shares from the
-    staging buffer ([world][K | V][head][tile][128][d] f16).  exchange
-    "ring": world - 1 NCCL send/recv steps, each GPU forwarding the share it
-    last received, one kernel per arrived share; "allgather": one NCCL
-    all-gather of the shares (NCCL's own ring or NVLink SHARP), then one
-    kernel for every other share."""
+    exchange "gather": the rank packs its share (ktir_pack_kv) into the
+    staging buffer ([world][K | V][head][tile][128][d] f16), one NCCL
+    all-gather fills in the others' shares, then one attention kernel adds
+    every key tile from the staging buffer (no carried state; the exchange
+    has the GPU to itself).  The overlapped forms: step 0 adds the rank's own
+    key tiles straight from the call's K and V while a high-priority comm
+    stream packs and passes the shares, and the later steps add the other
+    shares from the staging buffer, the softmax state carried between steps:
+    "allgather" passes them with one NCCL all-gather, then one kernel for
+    every other share; "ring" with world - 1 NCCL send/recv steps, each GPU
+    forwarding the share it last received, one kernel per arrived share."""
     import ctypes as C
 
     import torch
@@ -126,13 +132,19 @@ def ring_attention_plan(low, prob, exchange: str = "allgather"):
     share_rows = bh * kv_tiles * TILE
     row_bytes = d * 2
     kv_all = torch.empty(world * 2 * share_rows * d, dtype=torch.float16, device=dev)
-    o_acc = torch.empty(bh * len(mine) * TILE * d, dtype=torch.float32, device=dev)
-    ml = torch.empty(bh * len(mine) * TILE * 2, dtype=torch.float32, device=dev)
+    if exchange not in EXCHANGES:
+        raise ValueError(f"K/V exchange {exchange!r}: expected one of {EXCHANGES}")
+    # the overlapped forms carry the softmax state between their steps
+    o_acc = ml = None
+    if exchange != "gather":
+        o_acc = torch.empty(bh * len(mine) * TILE * d, dtype=torch.float32, device=dev)
+        ml = torch.empty(bh * len(mine) * TILE * 2, dtype=torch.float32, device=dev)
     lib = R.load_library()
     sq, sk, sv, so = (low.slots[b.index] for b in (prob["q"], prob["k"], prob["v"], prob["o"]))
     # high priority: the packing and NCCL kernels take their SMs ahead of the
     # attention kernel's CTAs, which would otherwise fill every SM first
-    comm = torch.cuda.Stream(dev, priority=-1) if dev.type == "cuda" else None
+    comm = (torch.cuda.Stream(dev, priority=-1) if dev.type == "cuda" and exchange != "gather"
+            else None)
     own_mask = share_mask(mine)
     all_mask = share_mask(range(n_tiles))
 
@@ -143,7 +155,8 @@ def ring_attention_plan(low, prob, exchange: str = "allgather"):
         dsc.n_qtiles = len(mine)
         dsc.key_mask = mask
         dsc.flags = (1 if first else 0) | (2 if last else 0)
-        dsc.o_acc, dsc.ml = o_acc.data_ptr(), ml.data_ptr()
+        if o_acc is not None:
+            dsc.o_acc, dsc.ml = o_acc.data_ptr(), ml.data_ptr()
         for i, qt in enumerate(mine):
             dsc.qtiles[i] = qt
         if staged:
@@ -161,7 +174,9 @@ def ring_attention_plan(low, prob, exchange: str = "allgather"):
         return dsc
 
     shares = step_shares(rank, world)
-    if exchange == "ring":
+    if exchange == "gather":
+        steps = [desc(all_mask, True, True, True)]
+    elif exchange == "ring":
         steps = [desc(own_mask, True, False, False)] + \
             [desc(share_mask(tiles_of[s]), False, t == world - 1, True)
              for t, s in enumerate(shares) if t > 0]
@@ -177,6 +192,17 @@ def ring_attention_plan(low, prob, exchange: str = "allgather"):
     def run(bufs, stream, status):
         compute = (torch.cuda.ExternalStream(stream.value, device=dev) if stream.value
                    else torch.cuda.default_stream(dev))
+        if exchange == "gather":
+            with torch.cuda.stream(compute):
+                R.check(lib.ktir_pack_kv(C.c_void_p(share(rank).data_ptr()),
+                                         C.c_void_p(bufs.base[sk]), C.c_void_p(bufs.base[sv]),
+                                         bh, seq, d, own_mask, stream), "ktir_pack_kv")
+                # the compute stream waits for the all-gather before the kernel
+                dist.all_gather_into_tensor(kv_all, share(rank), group=group)
+            k0 = steps[0]
+            k0.q, k0.o, k0.status = bufs.base[sq], bufs.base[so], status
+            R.check(lib.ktir_fmha_f16_part(C.byref(k0), stream), "ktir_fmha_f16_part")
+            return
         # the comm stream starts after the previous execution's kernels, which
         # read the staging buffer it overwrites; its work is queued before the
         # first attention step so that it reaches the SMs first

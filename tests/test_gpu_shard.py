@@ -3,8 +3,9 @@ against the oracle.  Each rank executes its contiguous range of cores and
 the ranks combine their writes, so every rank returns the whole result,
 which must equal the single-GPU (oracle) result.  The attention cases cover
 cores that own whole heads (no exchange) and cores that own zigzag stretches
-of every head's sequence (K/V passed between the GPUs in a ring).  Skipped
-with fewer than two GPUs."""
+of every head's sequence (K/V shares passed between the GPUs: gathered before
+one attention kernel, or passed while the first step runs, by all-gather or
+by send/recv, KTIR_KV_EXCHANGE).  Skipped with fewer than two GPUs."""
 
 import os
 import socket
@@ -18,12 +19,16 @@ from ktir_cpu_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
 
-CASES = [("softmax", dict(rows=256, cols=1024, grid=8, chunk=32), 1e-2),
-         ("gather_add", dict(rows=4096, cols=128, n_idx=16384, grid=8, chunk=1024), None),
-         ("gemm", dict(m=512, n=512, k=512, grid=(4, 2)), 1e-2),
-         ("attention", dict(batch=1, heads=4, seq=512, dim=128, grid=4, layout="heads"), 1e-2),
-         ("attention", dict(batch=1, heads=4, seq=512, dim=128, grid=4), 1e-2)]
-IDS = ["softmax", "gather_add", "gemm", "attention_heads", "attention_ring"]
+_ATT = dict(batch=1, heads=4, seq=512, dim=128, grid=4)
+CASES = [("softmax", dict(rows=256, cols=1024, grid=8, chunk=32), 1e-2, None),
+         ("gather_add", dict(rows=4096, cols=128, n_idx=16384, grid=8, chunk=1024), None, None),
+         ("gemm", dict(m=512, n=512, k=512, grid=(4, 2)), 1e-2, None),
+         ("attention", dict(_ATT, layout="heads"), 1e-2, None),
+         ("attention", _ATT, 1e-2, "gather"),
+         ("attention", _ATT, 1e-2, "allgather"),
+         ("attention", _ATT, 1e-2, "ring")]
+IDS = ["softmax", "gather_add", "gemm", "attention_heads", "attention_ring_gather",
+       "attention_ring_allgather", "attention_ring_sendrecv"]
 
 
 def _free_port():
@@ -34,10 +39,12 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, name, p, q):
+def _worker(rank, world, port, name, p, exchange, q):
     import torch
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    if exchange:
+        os.environ["KTIR_KV_EXCHANGE"] = exchange
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
@@ -56,8 +63,8 @@ def _worker(rank, world, port, name, p, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name,p,tol", CASES, ids=IDS)
-def test_two_gpu_shards_merge_to_oracle(name, p, tol):
+@pytest.mark.parametrize("name,p,tol,exchange", CASES, ids=IDS)
+def test_two_gpu_shards_merge_to_oracle(name, p, tol, exchange):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -66,7 +73,8 @@ def test_two_gpu_shards_merge_to_oracle(name, p, tol):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, name, p, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, name, p, exchange, q))
+             for r in range(2)]
     for pr in procs:
         pr.start()
     try:

@@ -1,10 +1,11 @@
 """Host logic of splitting one call's core grid across GPUs, on CPU ranks (gloo).
 
 The sharded gather -> +1 -> scatter plan counts, per table row, how many of
-this rank's units name the row, all-reduces the counts across ranks, and
-applies f count times to the rows this rank owns.  Here two gloo ranks run
-that decomposition with NumPy in place of the two kernels and must reproduce
-the oracle's sequential, unit-by-unit result exactly.
+this rank's units name the row, reduce-scatters the counts across ranks (each
+rank receives the sums for the row chunk it owns, lower.row_shard), and
+applies f count times to the rows this rank owns.  Here gloo ranks run that
+decomposition with NumPy in place of the two kernels and must reproduce the
+oracle's sequential, unit-by-unit result exactly.
 """
 
 import os
@@ -17,7 +18,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from ktir_cpu_b200 import workloads as W
-from ktir_cpu_b200.lower import core_range
+from ktir_cpu_b200.lower import core_range, row_shard
 
 P = dict(rows=96, cols=8, n_idx=512, grid=4, chunk=32)
 
@@ -39,13 +40,15 @@ def _worker(rank, world, port, q):
         table, idx = kw["table_ptr"], kw["idx_ptr"]
         per_core = P["n_idx"] // P["grid"]
         c0, c1 = core_range(rank, world, P["grid"])
-        counts = torch.zeros(P["rows"], dtype=torch.int32)
+        r0, r1, chunk = row_shard(rank, world, P["rows"])
+        counts = torch.zeros(chunk * world, dtype=torch.int32)
         for core in range(c0, c1):
             for s in range(core * per_core, (core + 1) * per_core, P["chunk"]):
                 for r in np.unique(idx[s:s + P["chunk"]]):
                     counts[int(r)] += 1
-        dist.all_reduce(counts, op=dist.ReduceOp.SUM)
-        r0, r1 = core_range(rank, world, P["rows"])
+        # in place: this rank's chunk of the array receives the sums
+        dist.reduce_scatter_tensor(counts[rank * chunk:(rank + 1) * chunk], counts,
+                                   op=dist.ReduceOp.SUM)
         mine = table[r0:r1].copy()
         for i in range(r1 - r0):
             for _ in range(int(counts[r0 + i])):
@@ -61,7 +64,7 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 3])
 def test_sharded_gather_rmw_matches_sequential_semantics(world):
     from oracle.interp import OracleInterpreter
     ctx = mp.get_context("spawn")
@@ -78,6 +81,17 @@ def test_sharded_gather_rmw_matches_sequential_semantics(world):
     ora.load(W.source("gather_add", **P))
     want = ora.execute_function("gather_add", **W.inputs("gather_add", seed=21, **P))["table_ptr"]
     assert np.array_equal(got, want)
+
+
+def test_row_shards_partition_the_table():
+    for n in (1, 7, 96, 1 << 20):
+        for world in (1, 2, 3, 8):
+            spans = [row_shard(r, world, n) for r in range(world)]
+            chunk = spans[0][2]
+            assert chunk * world >= n and all(c == chunk for _, _, c in spans)
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            assert all(a == min(n, r * chunk) for r, (a, _, _) in enumerate(spans))
 
 
 def test_core_ranges_partition_the_grid():
