@@ -919,6 +919,111 @@ __global__ void __launch_bounds__(256) k_rmw_apply_pairs(const __grid_constant__
   }
 }
 
+// Phase 2 for the common shape: 128-element rows whose every 16-byte vector
+// is aligned (table_off and row_stride multiples of 8 elements), y = x op imm.
+// A warp takes 32 consecutive index positions: each lane reads one index and
+// claims that row's count, so the warp has 32 claims in flight at once; then
+// the claimed rows go through the warp eight at a time, each 8-lane quarter
+// moving two rows (two 16-byte vectors per lane and row), all eight rows'
+// loads issued before any of their stores.
+template <int SOP>
+__device__ __forceinline__ void rmw_row_op(uint4& raw, int m, __half2 imm2) {
+  __half2* h2 = reinterpret_cast<__half2*>(&raw);
+  for (int rep = 0; rep < m; ++rep) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      h2[q] = SOP == OP_FADD ? __hadd2(h2[q], imm2)
+                             : (SOP == OP_FSUB ? __hsub2(h2[q], imm2) : __hmul2(h2[q], imm2));
+  }
+}
+
+template <int SOP>
+__global__ void __launch_bounds__(256) k_rmw_apply_warp(const __grid_constant__ KtirGatherRmwDesc d,
+                                                        const __grid_constant__ KtirBuffers b,
+                                                        int* __restrict__ counts, int64_t n_rows,
+                                                        float simple_imm) {
+  pdl_prologue();
+  const int lane = threadIdx.x & 31;
+  const int quarter = lane >> 3, sub = lane & 7;
+  const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t total = (int64_t)d.n_units * d.unit_len;
+  const bool dense_units = d.idx_unit_stride == d.unit_len;
+  const int64_t row_lo = d.row_hi > 0 ? d.row_lo : 0;
+  const int64_t row_hi = d.row_hi > 0 ? d.row_hi : n_rows;
+  __half* table = (__half*)b.base[d.table_slot];
+  const int64_t tnumel = b.numel[d.table_slot];
+  const __half2 imm2 = __float2half2_rn(simple_imm);
+  for (int64_t base = warp0 * 32; base < total; base += nwarps * 32) {
+    const int64_t g = base + lane;
+    int64_t row = -1;
+    if (g < total) {
+      int64_t pos;
+      if (dense_units) {
+        pos = d.idx_off + g;
+      } else {
+        const int64_t unit = g / d.unit_len;
+        pos = d.idx_off + unit * d.idx_unit_stride + (g - unit * d.unit_len);
+      }
+      row = read_index(b, d.idx_slot, d.idx_dtype, pos);
+    }
+    int m = 0;
+    if (row >= 0 && row < n_rows) m = atomicExch(&counts[row], 0);
+    // rows owned by another shard are consumed (counts stay zero) but not applied
+    unsigned live = __ballot_sync(0xffffffffu, m > 0 && row >= row_lo && row < row_hi);
+    while (live) {
+      // this quarter's two rows of the next eight: lanes src[0], src[1]
+      int src[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        int pick = -1;
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          const int f = live ? __ffs(live) - 1 : -1;
+          if (f >= 0) live &= live - 1;
+          if (qq == quarter) pick = f;
+        }
+        src[t] = pick;
+      }
+      int64_t rr[2];
+      int mm[2];
+      uint4 raw[2][2];
+      bool whole[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        rr[t] = __shfl_sync(0xffffffffu, row, src[t] < 0 ? 0 : src[t]);
+        mm[t] = __shfl_sync(0xffffffffu, m, src[t] < 0 ? 0 : src[t]);
+        const int64_t e = d.table_off + rr[t] * d.row_stride + sub * 16;
+        whole[t] = src[t] >= 0 && e >= 0 && e + 16 <= tnumel;
+        if (whole[t]) {
+          raw[t][0] = *reinterpret_cast<const uint4*>(table + e);
+          raw[t][1] = *reinterpret_cast<const uint4*>(table + e + 8);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (src[t] < 0) continue;
+        const int64_t e = d.table_off + rr[t] * d.row_stride + sub * 16;
+        if (whole[t]) {
+          rmw_row_op<SOP>(raw[t][0], mm[t], imm2);
+          rmw_row_op<SOP>(raw[t][1], mm[t], imm2);
+          *reinterpret_cast<uint4*>(table + e) = raw[t][0];
+          *reinterpret_cast<uint4*>(table + e + 8) = raw[t][1];
+        } else {
+          // the row runs past the table's end: element by element up to it
+          for (int i = 0; i < 16; ++i) {
+            if (e + i < 0 || e + i >= tnumel) continue;
+            float x = __half2float(table[e + i]);
+            for (int rep = 0; rep < mm[t]; ++rep)
+              x = __half2float(__float2half_rn(binf(SOP, x, simple_imm)));
+            table[e + i] = __float2half_rn(x);
+          }
+        }
+      }
+    }
+  }
+}
+
 extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* d, const KtirBuffers* bufs, int32_t* counts,
                                int64_t n_rows, int32_t* status, void* stream) {
   if (!d || !bufs || !counts || !status) return set_err(KTIR_ERR_ARG, "ktir_gather_rmw: null argument");
@@ -960,6 +1065,34 @@ extern "C" int ktir_gather_rmw(const KtirGatherRmwDesc* d, const KtirBuffers* bu
   const int64_t groups = (int64_t)d->n_units * d->unit_len;
   const int blocks = grid_x(groups * 16, 256, 148 * 64);
   const int blocks8 = grid_x(groups * 8, 256, 148 * 64);
+  if (simple_op && d->row_len == 128 && (d->table_off & 7) == 0 && (d->row_stride & 7) == 0) {
+    // one wave of warps, each walking 32 positions at a time
+    static int resident = 0;
+    if (!resident) {
+      int dev = 0, n_sm = 0, per_sm = 0;
+      if (cudaGetDevice(&dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_rmw_apply_warp<OP_FADD>, 256, 0) !=
+              cudaSuccess)
+        return set_err(KTIR_ERR_CUDA, "ktir_gather_rmw: occupancy query failed");
+      resident = n_sm * (per_sm > 0 ? per_sm : 1);
+    }
+    // as many sweeps as one wave needs, spread evenly over the blocks
+    const int64_t sweeps = (groups + (int64_t)resident * 256 - 1) / ((int64_t)resident * 256);
+    const int bb = grid_x((groups + sweeps - 1) / sweeps, 256, resident);
+    switch (simple_op) {
+      case OP_FADD:
+        launch_pdl(k_rmw_apply_warp<OP_FADD>, dim3(bb), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
+        break;
+      case OP_FSUB:
+        launch_pdl(k_rmw_apply_warp<OP_FSUB>, dim3(bb), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
+        break;
+      default:
+        launch_pdl(k_rmw_apply_warp<OP_FMUL>, dim3(bb), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);
+        break;
+    }
+    return check_launch("ktir_gather_rmw(apply)");
+  }
   switch (simple_op) {
     case OP_FADD:
       launch_pdl(k_rmw_apply_pairs<OP_FADD>, dim3(blocks8), dim3(256), 0, s, *d, *bufs, counts, n_rows, simple_imm);

@@ -52,6 +52,28 @@ def test_gather_add_full_size_bitexact():
     assert dup > 0.05
 
 
+@pytest.mark.parametrize("truncate", [0, 64])
+def test_gather_add_duplicates_at_the_table_end(truncate):
+    """Heavy duplicates on the last rows of a table whose allocation ends
+    `truncate` elements before the view does: the last row is read with zero
+    fill and written only up to the allocation's end, as the reference's
+    HBM does (ktir_cpu/memory.py:97-198)."""
+    p = dict(rows=512, cols=128, n_idx=4096, grid=4, chunk=256)
+    src = W.source("gather_add", **p)
+    kw = W.inputs("gather_add", seed=9, **p)
+    kw["idx_ptr"][:] = np.random.default_rng(9).integers(500, 512, p["n_idx"]).astype(np.int32)
+    kw["table_ptr"] = kw["table_ptr"].reshape(-1)[:512 * 128 - truncate].copy()
+    from ktir_cpu_b200 import KTIRInterpreter
+    dev = KTIRInterpreter()
+    dev.load(src)
+    got = dev.execute_function("gather_add", **{k: v.copy() for k, v in kw.items()})
+    assert dev.last_executable.plan.kind == "gather_rmw"
+    ora = OracleInterpreter()
+    ora.load(src)
+    want = ora.execute_function("gather_add", **{k: v.copy() for k, v in kw.items()})
+    assert_matches("table", got["table_ptr"], want["table_ptr"], None)
+
+
 def test_gather_add_negative_index_raises():
     from ktir_cpu_b200 import KTIRInterpreter
     p = dict(rows=512, cols=128, n_idx=1024, grid=4, chunk=256)
