@@ -1400,8 +1400,52 @@ class GenericExecutor:
         self.launches.append(Launch(run, "reduce"))
         self.vals[n.id] = out
 
+    def _dense_aligned(self, n: Node) -> _Val:
+        """Row-major arena copy of n starting on a 16-byte boundary (n's own
+        value when it already is one)."""
+        v = self.view_of(n)
+        if (v.imm is None and v.slot == R.ARENA_SLOT and v.dense
+                and (v.off * n.dtype.itemsize) % 16 == 0):
+            return v
+        out = self.arena_dense(n)     # arena allocations start on 256-byte boundaries
+        self._ew_copy(n, v, out)
+        return out
+
+    def _matmul_tc(self, n: Node, a: Node, bnode: Node) -> bool:
+        """An f16 x f16 -> f16 product on the tensor cores
+        (ktir_gemm_f16_blocked with one block of all of K: an f32 sum rounded
+        to f16 once, as NumPy's half matmul); False when the operands do not
+        fit its TMA tiles (row strides must be multiples of 16 bytes)."""
+        f16 = np.dtype(np.float16)
+        if not (a.dtype == bnode.dtype == n.dtype == f16) or len(a.shape) != 2 \
+                or len(bnode.shape) != 2 or len(n.shape) != 2:
+            return False
+        m, k = a.shape
+        nn = bnode.shape[1]
+        if m < 1 or k < 1 or nn < 1 or k % 8 or nn % 8 or -(-nn // 128) > 65535:
+            return False
+        va, vb = self._dense_aligned(a), self._dense_aligned(bnode)
+        out = self.arena_dense(n)
+        d = R.KtirGemmBlockedDesc()
+        d.lda, d.ldb, d.ldc = k, nn, nn
+        d.m, d.n, d.k = m, nn, k
+        d.block_k, d.acc_f16 = 0, 0
+        lib = self.lib
+        offs = (va.off * 2, vb.off * 2, out.off * 2)
+
+        def run(bufs, stream, status, _d=d, _o=offs):
+            arena = bufs.base[R.ARENA_SLOT]
+            _d.a, _d.b, _d.c = arena + _o[0], arena + _o[1], arena + _o[2]
+            _d.status = status
+            R.check(lib.ktir_gemm_f16_blocked(C.byref(_d), stream), "ktir_gemm_f16_blocked")
+        self.launches.append(Launch(run, "matmul_tc"))
+        self.vals[n.id] = out
+        return True
+
     def matmul(self, n: Node) -> None:
         a, bnode = n.ins
+        if self._matmul_tc(n, a, bnode):
+            return
         va, vb = self.view_of(a), self.view_of(bnode)
         if va.imm is not None:
             va = self.materialize(a)

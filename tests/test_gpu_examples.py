@@ -46,3 +46,23 @@ def test_b200_runs_reference_example(name):
             assert_contraction(f"{name}:{k}", out[k], w, mags[k], g["tol"], u=u)
         else:
             assert_matches(f"{name}:{k}", out[k], w, g["tol"])
+
+
+# the examples whose plans must multiply on the tensor cores: the K-loop
+# matmuls (tcgen05 GEMM plans) and the f16 products inside the 2-D SDPA
+# (generic plan, ktir_gemm_f16_blocked per product)
+TC_PLANS = {"ex_matmul_fwd": "gemm_blocked", "ex_matmul_small": "gemm_blocked",
+            "ex_sdpa_2d": "matmul_tc"}
+
+
+@pytest.mark.parametrize("name,kind", sorted(TC_PLANS.items()))
+def test_example_matmuls_run_on_tensor_cores(name, kind):
+    from ktir_cpu_b200 import KTIRInterpreter
+    g = load_example(name)
+    interp = KTIRInterpreter()
+    interp.load(g["src"])
+    interp.execute_function(g["func"], **{k: (v.copy() if isinstance(v, np.ndarray) else v)
+                                          for k, v in g["inputs"].items()})
+    kinds = [l.kind for l in interp.last_executable.plan.launches]
+    assert kind in kinds, kinds
+    assert "matmul" not in kinds, kinds
