@@ -52,6 +52,7 @@ UNIT = "execs/s"
 HEADLINE = "attention"
 ORDER = ["attention", "gemm", "softmax", "gather_add", "vector_add"]
 L2_BYTES = 126 * 1024 * 1024
+QUEUE_CYCLES = 4_000_000      # device spin ahead of each timed window
 
 # algorithmic work per execution (bytes for HBM-bound, flops for tensor-bound)
 WORK = {
@@ -68,8 +69,8 @@ WORKLOAD = {"softmax": "row softmax f16 [4096,1024], grid 32, 128 rows/core, f32
             "gemm": "GEMM f16 4096^3, f32 accumulate, grid 8x4, 512x1024 per core",
             "gather_add": "indirect gather/+1.0/RMW-scatter, table f16 [1048576,128], "
                           "262144 i32 indices, grid 64",
-            "attention": "causal MHA B4 H32 S2048 D128 f16, grid 32, cores own zigzag "
-                         "query-block pairs"}
+            "attention": "causal MHA B4 H32 S2048 D128 f16, grid 32: 4 head groups, each "
+                         "a ring of 8 cores that own zigzag query-block pairs"}
 
 
 def peaks():
@@ -88,7 +89,7 @@ def peaks():
 
 # variants measured beside the five workloads when the grid is split over GPUs:
 # the attention program with cores that own whole heads (no K/V exchange)
-VARIANTS = {"attention_heads": ("attention", {"layout": "heads"})}
+VARIANTS = {"attention_heads": ("attention", {"layout": "heads", "groups": 1})}
 WORKLOAD["attention_heads"] = ("causal MHA B4 H32 S2048 D128 f16, grid 32, cores own whole "
                                "heads")
 
@@ -425,10 +426,10 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
         _busy(exe, sets, stream, 1.5, dev, torch)
         env.barrier()
         torch.cuda.synchronize(dev)
-        # a short device-side wait ahead of the start event, so the host has
-        # queued the K steps before the clock starts (the host's launch
-        # latency is not device time)
-        torch.cuda._sleep(200000)
+        # a device-side wait (about 2 ms) ahead of the start event, so the
+        # host has queued the K steps (or submitted the whole graph of them)
+        # before the clock starts: the host's launch latency is not device time
+        torch.cuda._sleep(QUEUE_CYCLES)
         if flush:
             k_ms = flushed(steps)
         else:
@@ -440,7 +441,7 @@ def measure(env: Env, name: str, steps: int, with_cpu: bool):
         # a second window of at least 10 ms of device time: the K steps repeated
         reps = max(1, int(math.ceil(10.0 / max(k_ms, 1e-3))))
         env.barrier()
-        torch.cuda._sleep(200000)
+        torch.cuda._sleep(QUEUE_CYCLES)
         if flush:
             long_ms = flushed(steps * reps)
         else:

@@ -116,7 +116,10 @@ typedef struct {
   int64_t row_stride;
   int64_t idx_off;     /* element offset of the first index of unit 0 */
   int64_t idx_unit_stride; /* index offset step between consecutive units */
-  int64_t row_lo, row_hi;  /* apply only to table rows in [row_lo, row_hi); row_hi 0 = all */
+  /* count and apply only table rows in [row_lo, row_hi); row_hi 0 = all.  The
+   * apply pass still consumes (zeroes) every count it finds, so a count-only
+   * call over all rows may be followed by an apply-only call over a range. */
+  int64_t row_lo, row_hi;
   int32_t phases;      /* bit 0: count pass, bit 1: apply pass; 0 = both */
   int32_t pad2;
   KtirEwProgram f;     /* view 0 = the gathered element (load), view 1 = result (store) */
@@ -302,7 +305,10 @@ int ktir_gather_rmw_static(const KtirGatherRmwDesc* desc, const KtirBuffers* buf
 int ktir_wait_selftest(int32_t* status, uint32_t spin_limit, void* stream);
 
 /* tcgen05 GEMM (replaces the linalg.matmul K loop, ktir_cpu/dialects/linalg_ops.py:273-297
- * with ops/arith_ops.py:403-419, for whole-matrix tilings). */
+ * with ops/arith_ops.py:403-419, for whole-matrix tilings).  M, N, K multiples
+ * of 128, 128, 64; persistent over 128 x 256 output tiles, or 128 x 128 ones
+ * when N is not a multiple of 256 or the 256-wide tiles would not fill half
+ * the SMs. */
 int ktir_gemm_f16(const KtirGemmDesc* desc, void* stream);
 
 /* tcgen05 GEMM of any shape with per-block f16 rounding (see
@@ -338,6 +344,29 @@ int ktir_pack_kv(void* dst, const void* k, const void* v, int64_t bh, int64_t se
  * runs on one host.) */
 int ktir_bytes_delta(void* dst, const void* a, const void* b, int64_t n, int32_t subtract,
                      void* stream);
+
+/* Peer memory between the GPUs of one node, one process per GPU (no
+ * counterpart in the reference, whose cores share one host memory).  A split
+ * attention call's staging buffer is allocated, zeroed and exported as a
+ * 64-byte CUDA IPC handle (ktir_ipc_alloc); the other processes of its
+ * exchange group map it (ktir_ipc_open, unmapped with ktir_ipc_close) and
+ * pull K/V shares from it with the copy engines (ktir_copy_async).  32-bit
+ * epoch flags in the owners' buffers order the copies across processes:
+ * ktir_flag_set stores `value` at `flag` (local or a peer's) after the
+ * stream's earlier work, with release semantics at system scope;
+ * ktir_flag_wait holds the stream's later work until each of the n flags at
+ * flags[i * stride] has reached `value` (modulo 2^32), polling with acquire
+ * loads at most spin_limit times (1 .. 2^26, a short sleep between polls),
+ * and on running out sets KTIR_STATUS_TIMEOUT in *status and lets the stream
+ * go on. */
+int ktir_ipc_alloc(int64_t bytes, void** ptr, void* handle);
+int ktir_ipc_open(const void* handle, void** ptr);
+int ktir_ipc_close(void* ptr);
+int ktir_ipc_free(void* ptr);
+int ktir_flag_set(uint32_t* flag, uint32_t value, void* stream);
+int ktir_flag_wait(const uint32_t* flags, int32_t n, int32_t stride, uint32_t value,
+                   uint32_t spin_limit, int32_t* status, void* stream);
+int ktir_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
 
 /* One step of a sequence-split attention call (see KtirFmhaPartDesc): the
  * online-softmax K/V loop of the attention rewrite restricted to the key

@@ -30,13 +30,17 @@ using namespace ktir::tc;
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+// Output tiles are BM x BN with BN = 256, or 128 when a problem has too few
+// 256-wide tiles to give every SM one (a slice of a GEMM split across GPUs).
+constexpr int BM = 128, BK = 64, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;            // 16 KiB
 constexpr int B_BOX_BYTES = 64 * BK * 2;        // 8 KiB per 64-column box
-constexpr int B_BYTES = BK * BN * 2;            // 32 KiB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KiB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
-constexpr uint32_t TMEM_COLS = 512;             // two 256-column accumulators
+template <int BN> struct GemmShape {
+  static constexpr int B_BYTES = BK * BN * 2;            // 32 / 16 KiB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 / 32 KiB
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;          // two accumulators
+};
 
 struct GemmParams {
   __half* c;
@@ -46,9 +50,12 @@ struct GemmParams {
   int* status;
 };
 
+template <int BN>
 __global__ void __launch_bounds__(192, 1)
     k_gemm_tcgen05(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                    const __grid_constant__ GemmParams p) {
+  constexpr int STAGE_BYTES = GemmShape<BN>::STAGE_BYTES;
+  constexpr uint32_t TMEM_COLS = GemmShape<BN>::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
@@ -416,9 +423,9 @@ extern "C" const char* ktir_gemm_error(void) { return g_msg; }
 extern "C" int ktir_gemm_f16(const KtirGemmDesc* d, void* stream) {
   if (!d || !d->a || !d->b || !d->c || !d->status)
     return ktir_set_error(KTIR_ERR_ARG, "ktir_gemm_f16: null argument");
-  if (d->m % BM || d->n % BN || d->k % BK || d->k < BK)
+  if (d->m % BM || d->n % 128 || d->k % BK || d->k < BK)
     return ktir_set_error(KTIR_ERR_UNSUPPORTED,
-                          "ktir_gemm_f16: M, N, K must be multiples of 128, 256, 64");
+                          "ktir_gemm_f16: M, N, K must be multiples of 128, 128, 64");
   if ((reinterpret_cast<uintptr_t>(d->a) | reinterpret_cast<uintptr_t>(d->b) |
        reinterpret_cast<uintptr_t>(d->c)) & 15)
     return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_gemm_f16: operands not 16-byte aligned");
@@ -431,8 +438,10 @@ extern "C" int ktir_gemm_f16(const KtirGemmDesc* d, void* stream) {
     return ktir_set_error(KTIR_ERR_CUDA, "ktir_gemm_f16: tensor map encoding failed");
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(k_gemm_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES) != cudaSuccess)
+    if (cudaFuncSetAttribute(k_gemm_tcgen05<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             GemmShape<256>::SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(k_gemm_tcgen05<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             GemmShape<128>::SMEM_BYTES) != cudaSuccess)
       return ktir_set_error(KTIR_ERR_CUDA, "ktir_gemm_f16: shared-memory attribute refused");
     attr = true;
   }
@@ -451,10 +460,16 @@ extern "C" int ktir_gemm_f16(const KtirGemmDesc* d, void* stream) {
         cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n_sm < 1)
       return ktir_set_error(KTIR_ERR_CUDA, "ktir_gemm_f16: no SM count for the current device");
   }
-  const long long tiles = (d->m / BM) * (d->n / BN);
+  // 256-wide tiles when N allows them and they fill more than half the SMs;
+  // else 128-wide ones (twice the CTAs for the same work)
+  const bool wide = d->n % 256 == 0 && (d->m / BM) * (d->n / 256) > n_sm / 2;
+  const long long tiles = (d->m / BM) * (d->n / (wide ? 256 : 128));
   if (tiles > 0x7fffffffLL) return ktir_set_error(KTIR_ERR_UNSUPPORTED, "ktir_gemm_f16: too many tiles");
   const unsigned grid = (unsigned)(tiles < n_sm ? tiles : n_sm);
-  k_gemm_tcgen05<<<grid, 192, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  if (wide)
+    k_gemm_tcgen05<256><<<grid, 192, GemmShape<256>::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  else
+    k_gemm_tcgen05<128><<<grid, 192, GemmShape<128>::SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   return cudaGetLastError() == cudaSuccess
              ? KTIR_OK : ktir_set_error(KTIR_ERR_CUDA, "ktir_gemm_f16: launch failed");
 }

@@ -666,48 +666,30 @@ class Lowerer:
         return d, n_rows, len(units), R_, C_
 
     def _gather_rmw_plan(self, full, local) -> Plan:
+        """One ktir_gather_rmw launch (count pass, then apply pass).  A split
+        call owns a contiguous range of table rows (equal chunks, row_shard)
+        instead of its cores' units: whether a row is applied, and how often,
+        depends on every unit that names it, so each rank counts over every
+        unit's indices (1 MiB of int32 for the benchmark's 262,144) but only
+        the rows it owns, and applies those.  No counts cross GPUs; the index
+        tensor is read by every rank.  `local` (this rank's own units) does
+        not change the plan."""
+        del local
         d, n_rows, n_units, R_, C_ = full
+        counts = self.dev.zeros_i32(n_rows)
         if self.shard is not None:
-            rank, world, group = self.shard
-            r0, r1, chunk = row_shard(rank, world, n_rows)
-            counts = self.dev.zeros_i32(chunk * world)
-        else:
-            counts = self.dev.zeros_i32(n_rows)
+            rank, world, _ = self.shard
+            r0, r1, _ = row_shard(rank, world, n_rows)
+            d.phases = 0
+            # row_hi 0 would mean every row: an empty range is [n_rows, n_rows)
+            d.row_lo, d.row_hi = (r0, r1) if r1 > r0 else (n_rows, n_rows)
         lib = R.load_library()
         cptr = C.c_void_p(counts.data_ptr())
-        if self.shard is None:
-            def run(bufs, stream, status):
-                R.check(lib.ktir_gather_rmw(C.byref(d), C.byref(bufs), cptr, n_rows,
-                                            C.c_void_p(status), stream), "ktir_gather_rmw")
-            launches = [Launch(run, "gather_rmw", 2)]
-        else:
-            dl = None
-            if local is not None:
-                dl = local[0]
-                dl.phases = 1
-            d.phases = 2
-            d.row_lo, d.row_hi = r0, r1
 
-            def run_count(bufs, stream, status):
-                if dl is not None:
-                    R.check(lib.ktir_gather_rmw(C.byref(dl), C.byref(bufs), cptr, n_rows,
-                                                C.c_void_p(status), stream), "ktir_gather_rmw(count)")
-
-            def run_exchange(bufs, stream, status):
-                # each rank receives the summed counts of the rows it owns, in
-                # place (its own chunk of the count array); the apply pass
-                # consumes every count it finds, owned or not, so the array is
-                # zero again afterwards
-                import torch.distributed as dist
-                dist.reduce_scatter_tensor(counts[rank * chunk:(rank + 1) * chunk], counts,
-                                           op=dist.ReduceOp.SUM, group=group)
-
-            def run_apply(bufs, stream, status):
-                R.check(lib.ktir_gather_rmw(C.byref(d), C.byref(bufs), cptr, n_rows,
-                                            C.c_void_p(status), stream), "ktir_gather_rmw(apply)")
-            launches = [Launch(run_count, "gather_rmw_count", 1 if dl is not None else 0),
-                        Launch(run_exchange, "reduce_scatter_counts", 0),
-                        Launch(run_apply, "gather_rmw_apply", 1)]
+        def run(bufs, stream, status):
+            R.check(lib.ktir_gather_rmw(C.byref(d), C.byref(bufs), cptr, n_rows,
+                                        C.c_void_p(status), stream), "ktir_gather_rmw")
+        launches = [Launch(run, "gather_rmw", 2)]
         plan = Plan("gather_rmw", launches, [], status_check=True)
         plan.scratch["counts"] = counts
         plan.info.update(units=n_units, unit_len=R_, row_len=C_, idx_elems=n_units * R_,

@@ -408,7 +408,8 @@ def match_attention_plan(low, stores):
         if low.shard is not None:
             from .ring import ring_attention_plan
             # KTIR_KV_EXCHANGE picks how the K/V shares travel (ring.EXCHANGES)
-            return ring_attention_plan(low, prob, os.environ.get("KTIR_KV_EXCHANGE", "gather"))
+            return ring_attention_plan(low, prob,
+                                       os.environ.get("KTIR_KV_EXCHANGE", "copy_overlap"))
         return None
     bh = h_hi - h_lo
     off = h_lo * seq * d * 2

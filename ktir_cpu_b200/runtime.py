@@ -143,7 +143,9 @@ EXPORTS = ["ktir_version", "ktir_last_error", "ktir_device_count", "ktir_ew",
            "ktir_softmax_rows", "ktir_gather_rmw", "ktir_reduce", "ktir_matmul",
            "ktir_offsets", "ktir_indirect", "ktir_gemm_f16", "ktir_gemm_f16_blocked", "ktir_fmha_f16",
            "ktir_fmha_f16_part", "ktir_copy_blocks", "ktir_pack_kv", "ktir_bytes_delta",
-           "ktir_wait_selftest", "ktir_host_threads", "ktir_host_upload", "ktir_host_download"]
+           "ktir_wait_selftest", "ktir_host_threads", "ktir_host_upload", "ktir_host_download",
+           "ktir_ipc_alloc", "ktir_ipc_open", "ktir_ipc_close", "ktir_ipc_free", "ktir_flag_set",
+           "ktir_flag_wait", "ktir_copy_async"]
 
 _LIB: Optional[C.CDLL] = None
 
@@ -186,6 +188,13 @@ def load_library(build_if_missing: bool = False) -> C.CDLL:
     lib.ktir_bytes_delta.argtypes = [vp, vp, vp, C.c_int64, C.c_int32, vp]
     lib.ktir_pack_kv.argtypes = [vp, vp, vp, C.c_int64, C.c_int64, C.c_int64, C.c_uint32, vp]
     lib.ktir_wait_selftest.argtypes = [vp, C.c_uint32, vp]
+    lib.ktir_ipc_alloc.argtypes = [C.c_int64, C.POINTER(vp), vp]
+    lib.ktir_ipc_open.argtypes = [vp, C.POINTER(vp)]
+    lib.ktir_ipc_close.argtypes = [vp]
+    lib.ktir_ipc_free.argtypes = [vp]
+    lib.ktir_flag_set.argtypes = [vp, C.c_uint32, vp]
+    lib.ktir_flag_wait.argtypes = [vp, C.c_int32, C.c_int32, C.c_uint32, C.c_uint32, vp, vp]
+    lib.ktir_copy_async.argtypes = [vp, vp, C.c_int64, vp]
     lib.ktir_host_threads.argtypes = []
     lib.ktir_host_upload.argtypes = [C.POINTER(KtirHostXfer), C.c_int, C.c_int, vp]
     lib.ktir_host_download.argtypes = [C.POINTER(KtirHostXfer), C.c_int, C.POINTER(KtirHostCopy),

@@ -13,7 +13,8 @@ forms (ktir_cpu/dialects/linalg_ops.py:273-297, ops/arith_ops.py:403-419):
   f16 tiles into f32 outs).
 
 The whole call becomes one tcgen05 GEMM launch: the aligned persistent
-kernel for widened tilings of 128 x 256 x 64 multiples, else the blocked
+kernel for widened tilings of 128 x 128 x 64 multiples (256-wide output tiles
+where they fill the GPU, 128-wide ones for a slice too small to), else the blocked
 kernel (any shape, per-block rounding).  Numerics: the reference sums each
 tile in OpenBLAS / NumPy order, the tensor cores in their own order — equal
 within the stated tolerance, not bit-exact.
@@ -31,7 +32,7 @@ import numpy as np
 from . import runtime as R
 from .trace import Node, RectTarget, Store
 
-GEMM_TILE_M, GEMM_TILE_N, GEMM_TILE_K = 128, 256, 64
+GEMM_TILE_M, GEMM_TILE_N, GEMM_TILE_K = 128, 128, 64
 
 
 def _is_cast(n, src, dst) -> bool:

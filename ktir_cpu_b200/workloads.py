@@ -215,7 +215,7 @@ def gather_add(rows: int = 1048576, cols: int = 128, n_idx: int = 262144, grid: 
 
 
 def attention(batch: int = 4, heads: int = 32, seq: int = 2048, dim: int = 128, grid: int = 32,
-              bq: int = 64, bk: int = 64, layout: str = "zigzag") -> str:
+              bq: int = 64, bk: int = 64, layout: str = "zigzag", groups: int = 1) -> str:
     """Causal attention; Q/K/V/O are [batch*heads*seq, dim] row-major views.
 
     layout "heads": core c owns heads [c*bh/grid, (c+1)*bh/grid), all query blocks.
@@ -224,7 +224,12 @@ def attention(batch: int = 4, heads: int = 32, seq: int = 2048, dim: int = 128, 
     cores in order (with more cores than pairs, the heads of a pair are split
     between consecutive cores), so any contiguous range of cores owns the same
     amount of work and stretches of the sequence from both ends, and reads the
-    K/V blocks of query blocks other cores own."""
+    K/V blocks of query blocks other cores own.
+    groups > 1 (zigzag only): the heads form `groups` equal groups and the
+    cores grid / groups equal rings; core c serves head group c // (grid /
+    groups) and deals that group's zigzag pairs as above over the cores of
+    its ring (part c % (grid / groups)), so the K/V blocks a core reads
+    belong to cores of its own ring only."""
     bh = batch * heads
     assert seq % bq == 0 and bq == bk
     rows = bh * seq
@@ -245,25 +250,44 @@ def attention(batch: int = 4, heads: int = 32, seq: int = 2048, dim: int = 128, 
                  "      scf.for %qb = %c0 to %nq step %c1 {\n")
         close = "        scf.yield\n      }\n      scf.yield\n    }\n"
     elif layout == "zigzag":
-        assert nq % 2 == 0
+        assert nq % 2 == 0 and groups >= 1 and grid % groups == 0 and bh % groups == 0
         npairs = nq // 2
-        if grid >= npairs:
-            assert grid % npairs == 0 and bh % (grid // npairs) == 0
-            split = grid // npairs
-            bounds = (f"    %split = arith.constant {split} : index\n"
-                      f"    %hper = arith.constant {bh // split} : index\n"
-                      "    %p0 = arith.divsi %core, %split : index\n"
-                      "    %p1 = arith.addi %p0, %c1 : index\n"
-                      "    %hpart = arith.remsi %core, %split : index\n"
-                      "    %h0 = arith.muli %hpart, %hper : index\n"
-                      "    %h1 = arith.addi %h0, %hper : index\n")
+        parts, hg = grid // groups, bh // groups
+        bounds = ""
+        part = "%core"
+        if groups > 1:
+            # head group of the core's ring, and the core's place in that ring
+            bounds = (f"    %parts = arith.constant {parts} : index\n"
+                      f"    %hgroup = arith.constant {hg} : index\n"
+                      "    %grp = arith.divsi %core, %parts : index\n"
+                      "    %part = arith.remsi %core, %parts : index\n"
+                      "    %gh0 = arith.muli %grp, %hgroup : index\n")
+            part = "%part"
+        if parts >= npairs:
+            assert parts % npairs == 0 and hg % (parts // npairs) == 0
+            split = parts // npairs
+            bounds += (f"    %split = arith.constant {split} : index\n"
+                       f"    %hper = arith.constant {hg // split} : index\n"
+                       f"    %p0 = arith.divsi {part}, %split : index\n"
+                       "    %p1 = arith.addi %p0, %c1 : index\n"
+                       f"    %hpart = arith.remsi {part}, %split : index\n")
+            if groups > 1:
+                bounds += ("    %hrel = arith.muli %hpart, %hper : index\n"
+                           "    %h0 = arith.addi %gh0, %hrel : index\n")
+            else:
+                bounds += "    %h0 = arith.muli %hpart, %hper : index\n"
+            bounds += "    %h1 = arith.addi %h0, %hper : index\n"
         else:
-            assert npairs % grid == 0
-            bounds = (f"    %pper = arith.constant {npairs // grid} : index\n"
-                      "    %p0 = arith.muli %core, %pper : index\n"
-                      "    %p1 = arith.addi %p0, %pper : index\n"
-                      "    %h0 = arith.constant 0 : index\n"
-                      f"    %h1 = arith.constant {bh} : index\n")
+            assert npairs % parts == 0
+            bounds += (f"    %pper = arith.constant {npairs // parts} : index\n"
+                       f"    %p0 = arith.muli {part}, %pper : index\n"
+                       "    %p1 = arith.addi %p0, %pper : index\n")
+            if groups > 1:
+                bounds += ("    %h0 = arith.addi %gh0, %c0 : index\n"
+                           "    %h1 = arith.addi %gh0, %hgroup : index\n")
+            else:
+                bounds += ("    %h0 = arith.constant 0 : index\n"
+                           f"    %h1 = arith.constant {bh} : index\n")
         bounds += ("    %c2 = arith.constant 2 : index\n"
                    f"    %nqm1 = arith.constant {nq - 1} : index\n")
         loops = ("    scf.for %h = %h0 to %h1 step %c1 {\n"
@@ -278,6 +302,8 @@ def attention(batch: int = 4, heads: int = 32, seq: int = 2048, dim: int = 128, 
                  "      scf.yield\n    }\n")
     else:
         raise ValueError(f"attention layout {layout!r}")
+    if groups > 1 and layout != "zigzag":
+        raise ValueError("head groups are a zigzag layout parameter")
     head = f"""module {{
   func.func @causal_attention(%q_ptr: index, %k_ptr: index, %v_ptr: index, %o_ptr: index) attributes {{grid = [{grid}]}} {{
     %core = ktdp.get_compute_tile_id : index
@@ -379,7 +405,9 @@ FULL = {
     "softmax": dict(rows=4096, cols=1024, grid=32, chunk=32),
     "gemm": dict(m=4096, n=4096, k=4096, grid=(8, 4)),
     "gather_add": dict(rows=1048576, cols=128, n_idx=262144, grid=64, chunk=1024),
-    "attention": dict(batch=4, heads=32, seq=2048, dim=128, grid=32),
+    # 32 cores: 4 head groups (32 of the 128 heads each), each served by a ring
+    # of 8 cores that own zigzag query-block pairs and read each other's K/V
+    "attention": dict(batch=4, heads=32, seq=2048, dim=128, grid=32, groups=4),
 }
 
 FUNC = {"vector_add": "add_kernel", "softmax": "softmax_rows", "gemm": "gemm_kernel",

@@ -94,14 +94,18 @@ for nm, p in [
                               for k, v in p.items())
     tol = None if nm in ("vector_add", "gather_add") else 1e-2
     # the attention case was recorded with cores owning whole heads
-    src = W.source(nm, **p, layout="heads") if nm == "attention" else W.source(nm, **p)
+    src = W.source(nm, **p, layout="heads", groups=1) if nm == "attention" else W.source(nm, **p)
     case(tag, src, W.FUNC[nm], W.inputs(nm, seed=7, **p), tol=tol)
 
 # attention with the benchmark's core layout: zigzag pairs of query blocks,
 # the heads of a pair split between two cores
 _pz = dict(batch=1, heads=4, seq=512, dim=128, grid=8, bq=64, bk=64)
-case("attention_zigzag_batch1_heads4_seq512_grid8", W.source("attention", **_pz),
+case("attention_zigzag_batch1_heads4_seq512_grid8", W.source("attention", **_pz, groups=1),
      W.FUNC["attention"], W.inputs("attention", seed=9, **_pz), tol=1e-2)
+# the benchmark's layout with head groups: two groups of two heads, each a
+# ring of four cores that own zigzag pairs
+case("attention_groups2_batch1_heads4_seq512_grid8", W.source("attention", **_pz, groups=2),
+     W.FUNC["attention"], W.inputs("attention", seed=10, **_pz), tol=1e-2)
 
 # gather_add with heavy duplication inside and across cores
 p = dict(rows=64, cols=128, n_idx=1024, grid=4, chunk=64)

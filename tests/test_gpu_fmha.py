@@ -140,3 +140,59 @@ def test_fmha_partial_steps_of_the_ring(world):
     assert int(status.item()) == 0
     assert not torch.isnan(o).any().item()
     _check(f"ring emulated over {world} GPUs", o, q, k, v, bh, seq, scale, True)
+
+
+def test_fmha_head_groups_of_the_ring():
+    """The exchange of a program with head groups, emulated on one GPU as the
+    plan issues it for the default ("gather") exchange: two groups of two
+    heads, each served by two GPUs with zigzag query tiles.  Each emulated
+    GPU packs its share from K and V offset to its group's first head
+    (ktir_pack_kv) into its group's staging buffer, and one partial-attention
+    call per GPU over every key tile of the staging layout writes its query
+    tiles of O at the same head offset; all GPUs together must give whole
+    attention."""
+    import torch
+    from ktir_cpu_b200 import runtime as R
+    from ktir_cpu_b200.ring import share_mask, staging_layout
+    lib = R.load_library()
+    bh, seq, d, groups = 4, 1024, 128, 2
+    hg, n_tiles, row_bytes = bh // groups, seq // 128, d * 2
+    tiles_of = [[0, 1, 6, 7], [2, 3, 4, 5]]          # the two GPUs of every group
+    owner, local, kv_tiles = staging_layout(tiles_of, n_tiles)
+    g = torch.Generator(device="cpu").manual_seed(17)
+    q, k, v = (torch.randn(bh * seq, d, generator=g).half().cuda() for _ in range(3))
+    scale = float(1.0 / math.sqrt(128))
+    o = torch.full((bh * seq, d), float("nan"), dtype=torch.float16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    share_rows = hg * kv_tiles * 128
+    for grp in range(groups):
+        hoff = grp * hg * seq * row_bytes
+        kv_all = torch.full((len(tiles_of) * 2 * share_rows * d,), float("nan"),
+                            dtype=torch.float16, device="cuda")
+        for pos, tl in enumerate(tiles_of):
+            dst = kv_all.data_ptr() + pos * 2 * share_rows * row_bytes
+            R.check(lib.ktir_pack_kv(C.c_void_p(dst), C.c_void_p(k.data_ptr() + hoff),
+                                     C.c_void_p(v.data_ptr() + hoff), hg, seq, d,
+                                     share_mask(tl), stream), "ktir_pack_kv")
+        for pos, mine in enumerate(tiles_of):
+            dsc = R.KtirFmhaPartDesc()
+            dsc.q, dsc.o = q.data_ptr() + hoff, o.data_ptr() + hoff
+            dsc.k = kv_all.data_ptr()
+            dsc.v = kv_all.data_ptr() + share_rows * row_bytes
+            dsc.bh, dsc.seq, dsc.d = hg, seq, d
+            dsc.kv_tiles, dsc.kv_rows = kv_tiles, (2 * len(tiles_of) - 1) * share_rows
+            dsc.scale, dsc.causal = scale, 1
+            dsc.n_qtiles = len(mine)
+            dsc.key_mask = share_mask(range(n_tiles))
+            dsc.flags = 3
+            dsc.status = status.data_ptr()
+            for i, qt in enumerate(mine):
+                dsc.qtiles[i] = qt
+            for kt in range(n_tiles):
+                dsc.kv_owner[kt], dsc.kv_local[kt] = 2 * owner[kt], local[kt]
+            R.check(lib.ktir_fmha_f16_part(C.byref(dsc), stream), "ktir_fmha_f16_part")
+        torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert not torch.isnan(o).any().item()
+    _check("head groups emulated over 2 x 2 GPUs", o, q, k, v, bh, seq, scale, True)

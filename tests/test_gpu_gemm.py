@@ -30,10 +30,15 @@ def _gemm(a, b, c):
     assert int(status.item()) == 0
 
 
-# the last two take more than one wave of the persistent grid on a 148-SM B200
-# (512 tiles, 68 in the last wave; 160 tiles, 12)
+# (4096, 4096, 256) and (1280, 4096, 192) take more than one wave of the
+# persistent grid of 128 x 256 tiles on a 148-SM B200 (512 tiles, 68 in the
+# last wave; 160 tiles, 12); the smaller ones, too few 256-wide tiles to fill
+# half the SMs, run 128 x 128 tiles, as do N = 384 and 1408 (not multiples of
+# 256); (2048, 1024, 4096) is one GPU's slice of the 4096^3 GEMM split over
+# eight (128 tiles of 128 x 128, one wave), (4096, 1408, 128) two waves of them
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 128), (512, 256, 1024),
-                                   (384, 768, 320), (4096, 4096, 256), (1280, 4096, 192)])
+                                   (384, 768, 320), (4096, 4096, 256), (1280, 4096, 192),
+                                   (256, 384, 512), (2048, 1024, 4096), (4096, 1408, 128)])
 def test_gemm_matches_fp32(m, n, k):
     import torch
     g = torch.Generator(device="cpu").manual_seed(m * 7 + n + k)

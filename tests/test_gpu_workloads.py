@@ -86,7 +86,8 @@ def test_gather_add_negative_index_raises():
 
 
 def test_attention_uses_tensor_core_plan():
-    p = dict(batch=2, heads=2, seq=512, dim=128, grid=4)
+    # two head groups, each a ring of two cores
+    p = dict(batch=2, heads=2, seq=512, dim=128, grid=4, groups=2)
     kw, got, want, dev = _run_both("attention", **p)
     assert dev.last_executable.plan.kind == "attention"
     mag = contraction_mag("attention_seq512", kw)["o_ptr"]

@@ -7,7 +7,9 @@ gloo ranks then run the ring with NumPy in place of the kernel: each rank
 packs its share of K/V, adds the key tiles of one share per step to its
 queries while the shares travel rank to rank with send/recv, carries the
 online-softmax state (max, sum, O) between steps, and must reproduce whole
-causal attention for its query tiles.
+causal attention for its query tiles.  With head groups (one ring of cores
+per group of heads), each rank's heads give its exchange group
+(ring.exchange_group) and the shares travel within that group only.
 """
 
 import os
@@ -21,9 +23,13 @@ import torch.multiprocessing as mp
 
 from ktir_cpu_b200 import workloads as W
 from ktir_cpu_b200.lower import core_range
-from ktir_cpu_b200.ring import query_tiles, share_mask, staging_layout, step_shares
+from ktir_cpu_b200.ring import (exchange_group, head_tiles, query_tiles, share_mask,
+                                 staging_layout, step_shares)
 
-P = dict(batch=1, heads=2, seq=1024, dim=128, grid=8)
+P = dict(batch=1, heads=2, seq=1024, dim=128, grid=8, groups=1)
+# two head groups of two heads, each a ring of four cores: on four ranks every
+# group's K/V shares pass between two ranks only
+PG = dict(batch=1, heads=4, seq=1024, dim=128, grid=8, groups=2)
 T = 128
 
 
@@ -35,47 +41,55 @@ def _free_port():
     return port
 
 
-def _tiles_per_rank(world):
-    """Query tiles of each rank's core range, from the traced zigzag program."""
+def _spans_per_rank(world, params):
+    """(first head, end head, query tiles) of each rank's core range, from the
+    traced zigzag program."""
     from ktir_cpu_b200 import KTIRInterpreter
     from ktir_cpu_b200.rewrite import attention_problem, attention_rewrites
     from ktir_cpu_b200.trace import Tracer
     it = KTIRInterpreter(device=torch.device("cpu"))
-    it.load(W.source("attention", **P))
-    kw = W.inputs("attention", seed=0, **P)
+    it.load(W.source("attention", **params))
+    kw = W.inputs("attention", seed=0, **params)
     func, kw, ptrs, scalars, _ = it._bind("causal_attention", kw)
     tr = Tracer(func, it._space(ptrs), scalars, ptrs, rewrites=attention_rewrites(func)).run()
     seq = attention_problem(tr.stores)["seq"]
     out = []
     for r in range(world):
-        c0, c1 = core_range(r, world, P["grid"])
+        c0, c1 = core_range(r, world, params["grid"])
         pr = attention_problem([s for s in tr.stores if c0 <= s.core < c1], seq)
-        out.append(query_tiles(pr["rows"], seq, 64))
+        assert query_tiles(pr["rows"], seq, 64) == head_tiles(pr["rows"], seq, 64)[2]
+        out.append(head_tiles(pr["rows"], seq, 64))
     return out
 
 
-def _worker(rank, world, port, tiles_of, q):
+def _worker(rank, world, port, spans, params, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        kw = W.inputs("attention", seed=5, **P)
-        seq, d = P["seq"], P["dim"]
-        bh = P["batch"] * P["heads"]
+        kw = W.inputs("attention", seed=5, **params)
+        seq, d = params["seq"], params["dim"]
+        bh = params["batch"] * params["heads"]
         n_tiles = seq // T
         scale = float(np.float16(1.0 / np.sqrt(d)))
+        members = exchange_group(spans, rank)
+        pos, g = members.index(rank), len(members)
+        h_lo, h_hi, _ = spans[rank]
+        tiles_of = [spans[m][2] for m in members]
         owner, local, kv_tiles = staging_layout(tiles_of, n_tiles)
-        qf, kf, vf = (kw[n].astype(np.float64).reshape(bh, seq, d) for n in ("q_ptr", "k_ptr", "v_ptr"))
-        share = np.zeros((world, 2, bh, kv_tiles, T, d))       # the staging buffers (K, V)
-        for i, t in enumerate(tiles_of[rank]):
-            share[rank, 0, :, i] = kf[:, t * T:(t + 1) * T]
-            share[rank, 1, :, i] = vf[:, t * T:(t + 1) * T]
-        mine = tiles_of[rank]
-        m = np.full((bh, len(mine), T), -np.inf)
-        l_ = np.zeros((bh, len(mine), T))
-        o = np.zeros((bh, len(mine), T, d))
-        shares = step_shares(rank, world)
-        nxt, prv = (rank + 1) % world, (rank - 1) % world
+        qf, kf, vf = (kw[n].astype(np.float64).reshape(bh, seq, d)[h_lo:h_hi]
+                      for n in ("q_ptr", "k_ptr", "v_ptr"))
+        nh = h_hi - h_lo
+        share = np.zeros((g, 2, nh, kv_tiles, T, d))        # the staging buffers (K, V)
+        for i, t in enumerate(tiles_of[pos]):
+            share[pos, 0, :, i] = kf[:, t * T:(t + 1) * T]
+            share[pos, 1, :, i] = vf[:, t * T:(t + 1) * T]
+        mine = tiles_of[pos]
+        m = np.full((nh, len(mine), T), -np.inf)
+        l_ = np.zeros((nh, len(mine), T))
+        o = np.zeros((nh, len(mine), T, d))
+        shares = step_shares(pos, g)
+        nxt, prv = members[(pos + 1) % g], members[(pos - 1) % g]
         for t, s in enumerate(shares):
             mask = share_mask(tiles_of[s])
             for qi, qt in enumerate(mine):
@@ -94,32 +108,40 @@ def _worker(rank, world, port, tiles_of, q):
                     l_[:, qi] = l_[:, qi] * a + p.sum(-1)
                     o[:, qi] = o[:, qi] * a[..., None] + np.einsum("hqk,hkd->hqd", p, vb)
                     m[:, qi] = mn
-            if t < world - 1:
-                # pass share s on, take share shares[t + 1] from the previous rank
+            if t < g - 1:
+                # pass share s on within the group, take share shares[t + 1]
+                # from the previous member
                 send = torch.from_numpy(share[s].copy())
                 recv = torch.empty_like(send)
                 reqs = [dist.isend(send, nxt), dist.irecv(recv, prv)]
                 for rq in reqs:
                     rq.wait()
                 share[shares[t + 1]] = recv.numpy()
-        q.put((rank, mine, o / l_[..., None]))
+        q.put((rank, h_lo, h_hi, mine, o / l_[..., None]))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ring_steps_reproduce_whole_attention(world):
-    tiles_of = _tiles_per_rank(world)
-    n_tiles = P["seq"] // T
-    assert sorted(t for tl in tiles_of for t in tl) == list(range(n_tiles))
-    # zigzag: every rank owns the same amount of causal work
-    work = {sum(t + 1 for t in tl) for tl in tiles_of}
-    assert len(work) == 1, tiles_of
+@pytest.mark.parametrize("world,params,groups", [(2, P, [[0, 1]] * 2),
+                                                 (4, P, [[0, 1, 2, 3]] * 4),
+                                                 (4, PG, [[0, 1], [0, 1], [2, 3], [2, 3]])],
+                         ids=["ring2", "ring4", "head_groups_4ranks"])
+def test_ring_steps_reproduce_whole_attention(world, params, groups):
+    spans = _spans_per_rank(world, params)
+    assert [exchange_group(spans, r) for r in range(world)] == groups
+    n_tiles = params["seq"] // T
+    for members in {tuple(g) for g in groups}:
+        tiles_of = [spans[m][2] for m in members]
+        assert sorted(t for tl in tiles_of for t in tl) == list(range(n_tiles))
+        # zigzag: every rank owns the same amount of causal work
+        work = {sum(t + 1 for t in tl) for tl in tiles_of}
+        assert len(work) == 1, tiles_of
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, tiles_of, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, spans, params, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -130,17 +152,27 @@ def test_ring_steps_reproduce_whole_attention(world):
             if p.is_alive():
                 p.kill()
     assert all(p.exitcode == 0 for p in procs)
-    kw = W.inputs("attention", seed=5, **P)
-    seq, d = P["seq"], P["dim"]
-    bh = P["batch"] * P["heads"]
+    kw = W.inputs("attention", seed=5, **params)
+    seq, d = params["seq"], params["dim"]
+    bh = params["batch"] * params["heads"]
     qf, kf, vf = (kw[n].astype(np.float64).reshape(bh, seq, d) for n in ("q_ptr", "k_ptr", "v_ptr"))
     s = np.einsum("hqd,hkd->hqk", qf, kf) * float(np.float16(1.0 / np.sqrt(d)))
     s = np.where(np.triu(np.ones((seq, seq), bool), 1), -np.inf, s)
     e = np.exp(s - s.max(-1, keepdims=True))
     want = np.einsum("hqk,hkd->hqd", e / e.sum(-1, keepdims=True), vf)
-    for rank, mine, o in got:
+    covered = np.zeros((bh, seq // T), bool)
+    for rank, h_lo, h_hi, mine, o in got:
         for qi, qt in enumerate(mine):
-            np.testing.assert_allclose(o[:, qi], want[:, qt * T:(qt + 1) * T], rtol=1e-9, atol=1e-12)
+            np.testing.assert_allclose(o[:, qi], want[h_lo:h_hi, qt * T:(qt + 1) * T],
+                                       rtol=1e-9, atol=1e-12)
+            covered[h_lo:h_hi, qt] = True
+    assert covered.all()
+
+
+def test_exchange_group_rejects_overlapping_head_ranges():
+    assert exchange_group([(0, 2, [0]), (0, 2, [1]), (2, 4, [0, 1])], 2) == [2]
+    assert exchange_group([(0, 2, [0]), (1, 3, [1])], 0) is None
+    assert head_tiles([0, 64, 1024, 1088, 3072, 3136], 1024, 64) is None   # heads 0, 1, 3
 
 
 def test_staging_layout_rejects_overlaps_and_gaps():

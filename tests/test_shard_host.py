@@ -1,11 +1,12 @@
 """Host logic of splitting one call's core grid across GPUs, on CPU ranks (gloo).
 
-The sharded gather -> +1 -> scatter plan counts, per table row, how many of
-this rank's units name the row, reduce-scatters the counts across ranks (each
-rank receives the sums for the row chunk it owns, lower.row_shard), and
-applies f count times to the rows this rank owns.  Here gloo ranks run that
-decomposition with NumPy in place of the two kernels and must reproduce the
-oracle's sequential, unit-by-unit result exactly.
+The sharded gather -> +1 -> scatter plan gives each rank a contiguous chunk
+of table rows (lower.row_shard); the rank counts, for each of its rows, how
+many units (of every core) name the row, and applies f that many times to
+its rows.  No counts cross ranks: every rank reads the whole index tensor.
+Here gloo ranks run that decomposition with NumPy in place of the two
+kernels, the whole table assembled from the ranks' row chunks, and must
+reproduce the oracle's sequential, unit-by-unit result exactly.
 """
 
 import os
@@ -13,7 +14,6 @@ import socket
 
 import numpy as np
 import pytest
-import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
@@ -38,17 +38,14 @@ def _worker(rank, world, port, q):
     try:
         kw = W.inputs("gather_add", seed=21, **P)
         table, idx = kw["table_ptr"], kw["idx_ptr"]
-        per_core = P["n_idx"] // P["grid"]
-        c0, c1 = core_range(rank, world, P["grid"])
-        r0, r1, chunk = row_shard(rank, world, P["rows"])
-        counts = torch.zeros(chunk * world, dtype=torch.int32)
-        for core in range(c0, c1):
-            for s in range(core * per_core, (core + 1) * per_core, P["chunk"]):
-                for r in np.unique(idx[s:s + P["chunk"]]):
+        r0, r1, _ = row_shard(rank, world, P["rows"])
+        counts = np.zeros(P["rows"], np.int64)
+        # every unit of every core, only the rows this rank owns
+        for s in range(0, P["n_idx"], P["chunk"]):
+            for r in np.unique(idx[s:s + P["chunk"]]):
+                if r0 <= r < r1:
                     counts[int(r)] += 1
-        # in place: this rank's chunk of the array receives the sums
-        dist.reduce_scatter_tensor(counts[rank * chunk:(rank + 1) * chunk], counts,
-                                   op=dist.ReduceOp.SUM)
+        assert not counts[:r0].any() and not counts[r1:].any()
         mine = table[r0:r1].copy()
         for i in range(r1 - r0):
             for _ in range(int(counts[r0 + i])):
