@@ -429,4 +429,8 @@ def match_attention_plan(low, stores):
     plan = Plan("attention", [Launch(run, "fmha")], [], status_check=True)
     flops = 4 * bh * seq * seq * d // (2 if causal else 1)
     plan.info.update(bh=bh, seq=seq, d=d, causal=causal, scale=scale, flops=flops)
+    if low.shard is not None:
+        # a split reads only its heads' rows of Q, K and V: (buffer index, byte ranges)
+        plan.info["upload_ranges"] = {b.index: [(off, bh * seq * d * 2)]
+                                      for b in (qbuf, kbuf, vbuf)}
     return plan
