@@ -114,6 +114,30 @@ def share_mask(tiles: Sequence[int]) -> int:
     return m
 
 
+def copy_schedule(pos: int, gsize: int, epoch: int) -> List[Tuple]:
+    """The stream operations of one execution's copy exchange on the GPU at
+    place `pos` of a group of `gsize`, in issue order (epochs count from 1,
+    modulo 2^32):
+
+      ("wait_taken", i, e - 1)  until member i has copied this GPU's share of
+                                the previous execution (a flag in this GPU's
+                                staging buffer, word 1 + i)
+      ("pack",)                 this GPU's share into its staging buffer
+      ("set_ready", e)          this GPU's "packed" flag (word 0)
+      ("wait_ready", i, e)      until member i has packed its share
+      ("copy", i)               member i's share into this GPU's buffer
+      ("set_taken", i, e)       "copied" in member i's buffer (word 1 + pos)
+
+    Other members are visited in ring order from this GPU."""
+    e = epoch & 0xFFFFFFFF
+    order = [(pos + t) % gsize for t in range(1, gsize)]
+    ops: List[Tuple] = [("wait_taken", i, (e - 1) & 0xFFFFFFFF) for i in order]
+    ops += [("pack",), ("set_ready", e)]
+    for i in order:
+        ops += [("wait_ready", i, e), ("copy", i), ("set_taken", i, e)]
+    return ops
+
+
 EXCHANGES = ("copy_overlap", "copy", "gather", "allgather", "ring")
 
 # staging buffer of the copy exchanges: a 256-byte block of epoch flags (word 0:
@@ -324,20 +348,27 @@ def ring_attention_plan(low, prob, exchange: str = "gather"):
         def wait(addr, value):
             R.check(lib.ktir_flag_wait(C.c_void_p(addr), 1, 1, value, FLAG_SPIN_LIMIT, stp, st),
                     "ktir_flag_wait")
-        order = [(pos + t) % gsize for t in range(1, gsize)]
-        for i in order:
-            wait(flags + 4 * (1 + i), (e - 1) & 0xFFFFFFFF)
-        R.check(lib.ktir_pack_kv(C.c_void_p(kv_base + pos * share_bytes),
-                                 C.c_void_p(bufs.base[sk] + hoff), C.c_void_p(bufs.base[sv] + hoff),
-                                 bh, seq, d, own_mask, st), "ktir_pack_kv")
-        R.check(lib.ktir_flag_set(C.c_void_p(flags), e, st), "ktir_flag_set")
-        for i in order:
-            peer = staging.peer[i]
-            wait(peer, e)
-            R.check(lib.ktir_copy_async(C.c_void_p(kv_base + i * share_bytes),
-                                        C.c_void_p(peer + FLAG_BYTES + i * share_bytes),
-                                        share_bytes, st), "ktir_copy_async")
-            R.check(lib.ktir_flag_set(C.c_void_p(peer + 4 * (1 + pos)), e, st), "ktir_flag_set")
+        for op in copy_schedule(pos, gsize, e):
+            kind = op[0]
+            if kind == "wait_taken":
+                wait(flags + 4 * (1 + op[1]), op[2])
+            elif kind == "pack":
+                R.check(lib.ktir_pack_kv(C.c_void_p(kv_base + pos * share_bytes),
+                                         C.c_void_p(bufs.base[sk] + hoff),
+                                         C.c_void_p(bufs.base[sv] + hoff),
+                                         bh, seq, d, own_mask, st), "ktir_pack_kv")
+            elif kind == "set_ready":
+                R.check(lib.ktir_flag_set(C.c_void_p(flags), op[1], st), "ktir_flag_set")
+            elif kind == "wait_ready":
+                wait(staging.peer[op[1]], op[2])
+            elif kind == "copy":
+                i = op[1]
+                R.check(lib.ktir_copy_async(C.c_void_p(kv_base + i * share_bytes),
+                                            C.c_void_p(staging.peer[i] + FLAG_BYTES + i * share_bytes),
+                                            share_bytes, st), "ktir_copy_async")
+            else:                                   # set_taken
+                R.check(lib.ktir_flag_set(C.c_void_p(staging.peer[op[1]] + 4 * (1 + pos)), op[2],
+                                          st), "ktir_flag_set")
 
     def gather_shares():
         """Every member's share into its place of kv_all: one all-gather when

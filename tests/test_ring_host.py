@@ -9,7 +9,9 @@ queries while the shares travel rank to rank with send/recv, carries the
 online-softmax state (max, sum, O) between steps, and must reproduce whole
 causal attention for its query tiles.  With head groups (one ring of cores
 per group of heads), each rank's heads give its exchange group
-(ring.exchange_group) and the shares travel within that group only.
+(ring.exchange_group) and the shares travel within that group only.  The
+copy exchange's epoch-flag protocol (ring.copy_schedule) is run by 2-4
+simulated members under random interleavings of their streams.
 """
 
 import os
@@ -185,3 +187,72 @@ def test_staging_layout_rejects_overlaps_and_gaps():
     assert step_shares(1, 4) == [1, 0, 3, 2]
     assert query_tiles([0, 64, 448, 192], 512, 64) is None          # a half tile
     assert query_tiles([0, 64, 512, 576], 512, 64) == [0]           # two heads, tile 0
+
+
+def _reached(flag: int, value: int) -> bool:
+    """The device wait's test: flag has reached value, modulo 2^32."""
+    d = (flag - value) & 0xFFFFFFFF
+    return d < 0x80000000
+
+
+@pytest.mark.parametrize("gsize,first", [(2, 1), (3, 1), (4, 1), (2, 0xFFFFFFFE), (3, 0xFFFFFFFD)])
+def test_copy_exchange_schedule_never_blocks_and_never_reads_a_share_being_packed(gsize, first):
+    """The copy exchange's flag protocol (ring.copy_schedule), run by every
+    member of a group over several executions under random interleavings of
+    their streams: every wait ends, and every pull of a share reads the
+    owner's pack of the same execution, with no later pack of that owner
+    between the start and the end of the pull.  Epochs may wrap past 2^32."""
+    import random
+    from ktir_cpu_b200.ring import copy_schedule
+    n_exec = 6
+    epochs = [(first + k) & 0xFFFFFFFF for k in range(n_exec)]
+    for seed in range(200):
+        rng = random.Random(seed)
+        prev = (first - 1) & 0xFFFFFFFF
+        ready = [prev] * gsize                      # word 0 of each member's buffer
+        taken = [[prev] * gsize for _ in range(gsize)]   # taken[owner][reader]
+        packed = [None] * gsize                     # the epoch each owner's share holds
+        ops = []
+        for r in range(gsize):
+            seq_r = []
+            for e in epochs:
+                for op in copy_schedule(r, gsize, e):
+                    if op[0] == "copy":
+                        # a pull takes time: other streams may move in between
+                        seq_r += [("copy_start", op[1], e), ("copy_end", op[1], e)]
+                    elif op[0] == "pack":
+                        seq_r.append(("pack", e))
+                    else:
+                        seq_r.append(op)
+            ops.append(seq_r)
+        pc = [0] * gsize
+        pulling = {}                                 # (reader, owner) -> epoch read at start
+
+        def runnable(r):
+            if pc[r] >= len(ops[r]):
+                return False
+            op = ops[r][pc[r]]
+            if op[0] == "wait_taken":
+                return _reached(taken[r][op[1]], op[2])
+            if op[0] == "wait_ready":
+                return _reached(ready[op[1]], op[2])
+            return True
+
+        while any(pc[r] < len(ops[r]) for r in range(gsize)):
+            cand = [r for r in range(gsize) if runnable(r)]
+            assert cand, f"seed {seed}: every remaining stream waits ({pc})"
+            r = rng.choice(cand)
+            op = ops[r][pc[r]]
+            pc[r] += 1
+            if op[0] == "pack":
+                assert all(o != r for (_, o) in pulling), "a share packed while it is pulled"
+                packed[r] = op[1]
+            elif op[0] == "set_ready":
+                ready[r] = op[1]
+            elif op[0] == "copy_start":
+                pulling[(r, op[1])] = packed[op[1]]
+            elif op[0] == "copy_end":
+                start = pulling.pop((r, op[1]))
+                assert start == op[2] == packed[op[1]], "pulled a share of another execution"
+            elif op[0] == "set_taken":
+                taken[op[1]][r] = op[2]
