@@ -14,7 +14,6 @@ import os
 import socket
 from datetime import timedelta
 
-import numpy as np
 import pytest
 
 from golden_util import assert_contraction, assert_matches, contraction_mag
