@@ -264,10 +264,11 @@ def ring_attention_plan(low, prob, exchange: str = "gather"):
     if exchange not in EXCHANGES:
         raise ValueError(f"K/V exchange {exchange!r}: expected one of {EXCHANGES}")
     copies = exchange in ("copy", "copy_overlap")
-    if copies and (dev.type != "cuda" or
+    if copies and (dev.type != "cuda" or gsize > FLAG_BYTES // 4 - 1 or
                    any(len(exchange_group(spans, r) or ()) < 2 for r in range(world))):
-        # peer mappings need GPUs, and every rank of the process group must
-        # take part in the handle exchange: plain NCCL otherwise
+        # peer mappings need GPUs, every rank of the process group must take
+        # part in the handle exchange, and the flag block holds one "copied"
+        # word per member: plain NCCL otherwise
         exchange, copies = ("gather", False)
     lib = R.load_library()
     staging = kv_all = None
