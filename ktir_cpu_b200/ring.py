@@ -264,8 +264,8 @@ def ring_attention_plan(low, prob, exchange: str = "gather"):
     if exchange not in EXCHANGES:
         raise ValueError(f"K/V exchange {exchange!r}: expected one of {EXCHANGES}")
     copies = exchange in ("copy", "copy_overlap")
-    if copies and (dev.type != "cuda" or gsize > FLAG_BYTES // 4 - 1 or
-                   any(len(exchange_group(spans, r) or ()) < 2 for r in range(world))):
+    sizes = [len(exchange_group(spans, r) or ()) for r in range(world)]
+    if copies and (dev.type != "cuda" or min(sizes) < 2 or max(sizes) > FLAG_BYTES // 4 - 1):
         # peer mappings need GPUs, every rank of the process group must take
         # part in the handle exchange, and the flag block holds one "copied"
         # word per member: plain NCCL otherwise
